@@ -1,0 +1,217 @@
+/*
+ * xspmm_b200.h -- C ABI of the B200-native xSpMM hot path (libxspmm_b200.so).
+ *
+ * Plain pointers and sizes only. Every pointer to matrix data is a DEVICE pointer on the handle's
+ * device (the reference's API takes device pointers too: include/xspmm/xspmm.hpp:14-40). Work is
+ * enqueued on the handle's stream; functions that must return a size to the host (the CSR->BCSR
+ * count) synchronize that stream. Every function returns an xspmm_status_t; on failure
+ * xspmm_last_error() gives a message for the calling thread.
+ *
+ * Index types: the reference templates every function on IndexType in {int32_t, int64_t}
+ * (include/xspmm/matrix/csr.hpp:12, bcsr.hpp:12); each entry point here exists with suffix _i32
+ * and _i64. Value types: __half (f16) and float (f32), the instantiations the reference's CUDA
+ * backend names (src/cuda/unstructured_mtx_mul.cu:137-148).
+ *
+ * The C++ API mirroring the reference (xspmm::spmm, CudaExecutor, CSRMatrix, BCSRMatrix,
+ * SpMMTimings) is header-only on top of this ABI: include/xspmm/xspmm.hpp.
+ */
+#ifndef XSPMM_B200_H
+#define XSPMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum xspmm_status {
+    XSPMM_STATUS_OK = 0,
+    XSPMM_STATUS_INVALID_ARGUMENT = 1, /* bad sizes/pointers, or a malformed CSR/permutation */
+    XSPMM_STATUS_UNSUPPORTED = 2,      /* e.g. a SpMM block size other than 16x16 */
+    XSPMM_STATUS_CUDA_ERROR = 3,
+    XSPMM_STATUS_OUT_OF_MEMORY = 4,
+    XSPMM_STATUS_NCCL_ERROR = 5,
+    XSPMM_STATUS_TIMEOUT = 6,
+    XSPMM_STATUS_INTERNAL = 7
+} xspmm_status_t;
+
+typedef struct xspmm_handle_s* xspmm_handle_t;
+
+/* Mirrors xspmm::SpMMTimings (include/xspmm/core/timings.hpp:7-14). Milliseconds, device time
+ * measured with CUDA events on the handle's stream. */
+typedef struct xspmm_timings {
+    double clustering_ms;
+    double permutation_ms;
+    double conversion_ms;
+    double spmm_ms;
+    double unpermutation_ms;
+    double total_pipeline_ms;
+} xspmm_timings_t;
+
+/* ---------------------------------------------------------------------------------------------
+ * Handle. Replaces the role of xspmm::CudaExecutor (include/xspmm/core/executor.hpp:37-51,
+ * src/core/executor.cpp:80-108): it binds a device (made current inside every call, so handles on
+ * different devices can be used from one thread) and a stream. stream == NULL means the legacy
+ * default stream, which is what the reference launches on (src/cuda/unstructured_mtx_mul.cu:47).
+ * ------------------------------------------------------------------------------------------- */
+xspmm_status_t xspmm_create(int device, void* stream, xspmm_handle_t* out);
+xspmm_status_t xspmm_destroy(xspmm_handle_t h);
+xspmm_status_t xspmm_set_stream(xspmm_handle_t h, void* stream);
+xspmm_status_t xspmm_get_device(xspmm_handle_t h, int* device);
+/* Number of kernels this library has launched on the handle since creation (or the last reset). */
+xspmm_status_t xspmm_get_launch_count(xspmm_handle_t h, uint64_t* count);
+xspmm_status_t xspmm_reset_launch_count(xspmm_handle_t h);
+const char* xspmm_status_string(xspmm_status_t s);
+const char* xspmm_last_error(void);
+/* Device memory through the handle: replaces Executor::allocate/free/copy_*
+ * (include/xspmm/core/executor.hpp:14-21). Copies are stream-ordered and synchronous w.r.t. the
+ * host on return, like the reference's cudaMemcpy (src/core/executor.cpp:94-104). */
+xspmm_status_t xspmm_malloc(xspmm_handle_t h, void** ptr, size_t bytes);
+xspmm_status_t xspmm_free(xspmm_handle_t h, void* ptr);
+xspmm_status_t xspmm_memcpy_h2d(xspmm_handle_t h, void* dst, const void* src, size_t bytes);
+xspmm_status_t xspmm_memcpy_d2h(xspmm_handle_t h, void* dst, const void* src, size_t bytes);
+xspmm_status_t xspmm_memcpy_d2d(xspmm_handle_t h, void* dst, const void* src, size_t bytes);
+xspmm_status_t xspmm_synchronize(xspmm_handle_t h);
+
+/* ---------------------------------------------------------------------------------------------
+ * Tier-1 BCSR SpMM: C = A * B with A in BCSR (16x16 blocks, row-major inside a block).
+ * Replaces xspmm::spmm(const BCSRMatrix&, const In* B, Out* C, N) (include/xspmm/xspmm.hpp:14-18,
+ * dispatch src/xspmm.cpp:29-52, launcher src/cuda/unstructured_mtx_mul.cu:31-51, kernel
+ * src/common/spmm_math.hpp:20-146).
+ *   A: num_block_rows, num_block_cols, num_blocks, row_ptr[num_block_rows+1], col_ind[num_blocks],
+ *      values[num_blocks*r_block*c_block]; r_block = c_block = 16 (else UNSUPPORTED -- the
+ *      reference kernel hard-codes 16, src/cuda/unstructured_mtx_mul.cu:39).
+ *   B: K x N row-major (ld = N); C: M x N row-major fp32 (ld = N), every row overwritten.
+ *   M, K: true row counts of C and B. Pass num_block_rows*16 / num_block_cols*16 for the
+ *      reference's behaviour; smaller values guard the ragged last block row / column, which the
+ *      reference kernel reads and writes out of bounds (src/common/spmm_math.hpp:80, :118-122).
+ *   out_row_map: NULL, or int array of M entries giving the row of C that row i of A*B goes to
+ *      (fuses the Tier-2 unpermute into the store). Same index type as row_ptr.
+ * ------------------------------------------------------------------------------------------- */
+xspmm_status_t xspmm_bcsr_spmm_f16f32_i32(xspmm_handle_t h, int32_t num_block_rows,
+    int32_t num_block_cols, int32_t num_blocks, int32_t r_block, int32_t c_block,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const void* B, float* C,
+    int32_t M, int32_t K, int32_t N, const int32_t* out_row_map);
+xspmm_status_t xspmm_bcsr_spmm_f16f32_i64(xspmm_handle_t h, int64_t num_block_rows,
+    int64_t num_block_cols, int64_t num_blocks, int64_t r_block, int64_t c_block,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
+    int64_t M, int64_t K, int64_t N, const int64_t* out_row_map);
+xspmm_status_t xspmm_bcsr_spmm_f32f32_i32(xspmm_handle_t h, int32_t num_block_rows,
+    int32_t num_block_cols, int32_t num_blocks, int32_t r_block, int32_t c_block,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const void* B, float* C,
+    int32_t M, int32_t K, int32_t N, const int32_t* out_row_map);
+xspmm_status_t xspmm_bcsr_spmm_f32f32_i64(xspmm_handle_t h, int64_t num_block_rows,
+    int64_t num_block_cols, int64_t num_blocks, int64_t r_block, int64_t c_block,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
+    int64_t M, int64_t K, int64_t N, const int64_t* out_row_map);
+
+/* ---------------------------------------------------------------------------------------------
+ * Greedy 1-D Jaccard (Sylos-Labini) row clustering. Replaces
+ * xspmm::compute_1d_jaccard_clustering(exec, A, dist_thresh, block_width, perm_out)
+ * (include/xspmm/clustering.hpp:19-25, src/xspmm.cpp:57-67, src/cpu/clustering_sylos_labini.cpp:
+ * 51-120). Writes perm_out[M] (perm[new] = old), bit-identical to the reference. Only row_ptr and
+ * col_ind are read (the reference ignores values too).
+ * ------------------------------------------------------------------------------------------- */
+xspmm_status_t xspmm_cluster_jaccard_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, float dist_thresh, int32_t block_width,
+    int32_t* perm_out);
+xspmm_status_t xspmm_cluster_jaccard_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, float dist_thresh, int64_t block_width,
+    int64_t* perm_out);
+
+/* ---------------------------------------------------------------------------------------------
+ * CSR row permutation: out row i = row perm[i] of A, entries in their original order. Replaces
+ * xspmm::apply_permutation (include/xspmm/clustering.hpp:34-38, src/cuda/mtx_permutation.cu:12-65,
+ * kernels src/common/permutation.hpp:15-66). Output arrays are caller-allocated: out_row_ptr[M+1],
+ * out_col_ind[nnz], out_values[nnz]. perm must be a permutation of [0, M) (checked: entries out
+ * of range give INVALID_ARGUMENT).
+ * ------------------------------------------------------------------------------------------- */
+xspmm_status_t xspmm_permute_rows_f16_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const int32_t* perm,
+    int32_t* out_row_ptr, int32_t* out_col_ind, void* out_values);
+xspmm_status_t xspmm_permute_rows_f16_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const int64_t* perm,
+    int64_t* out_row_ptr, int64_t* out_col_ind, void* out_values);
+xspmm_status_t xspmm_permute_rows_f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const int32_t* perm,
+    int32_t* out_row_ptr, int32_t* out_col_ind, void* out_values);
+xspmm_status_t xspmm_permute_rows_f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const int64_t* perm,
+    int64_t* out_row_ptr, int64_t* out_col_ind, void* out_values);
+
+/* ---------------------------------------------------------------------------------------------
+ * CSR -> BCSR on the device, in two calls so the caller can allocate the outputs (the reference
+ * builds on the host, src/core/conversion.cpp:8-100, and returns a BCSRMatrix:
+ * include/xspmm/matrix/conversion.hpp:19-22).
+ *   _count: writes bcsr_row_ptr[ceil(M/r_block)+1] and returns the number of blocks in
+ *           *num_blocks (synchronizes). Validates the CSR (row_ptr monotone, 0 <= col < K).
+ *   _fill:  given that row_ptr, writes col_ind[num_blocks] (ascending per block row) and
+ *           values[num_blocks*r_block*c_block] (zero-filled blocks, a duplicate (row,col) keeps
+ *           its last value in CSR order -- conversion.cpp:75-91). values may be NULL when only
+ *           the structure is wanted.
+ * Any r_block, c_block >= 1.
+ * ------------------------------------------------------------------------------------------- */
+xspmm_status_t xspmm_csr_to_bcsr_count_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, int32_t r_block, int32_t c_block,
+    int32_t* bcsr_row_ptr, int64_t* num_blocks);
+xspmm_status_t xspmm_csr_to_bcsr_count_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, int64_t r_block, int64_t c_block,
+    int64_t* bcsr_row_ptr, int64_t* num_blocks);
+xspmm_status_t xspmm_csr_to_bcsr_fill_f16_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t r_block,
+    int32_t c_block, const int32_t* bcsr_row_ptr, int32_t* bcsr_col_ind, void* bcsr_values);
+xspmm_status_t xspmm_csr_to_bcsr_fill_f16_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, int64_t r_block,
+    int64_t c_block, const int64_t* bcsr_row_ptr, int64_t* bcsr_col_ind, void* bcsr_values);
+xspmm_status_t xspmm_csr_to_bcsr_fill_f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t r_block,
+    int32_t c_block, const int32_t* bcsr_row_ptr, int32_t* bcsr_col_ind, void* bcsr_values);
+xspmm_status_t xspmm_csr_to_bcsr_fill_f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, int64_t r_block,
+    int64_t c_block, const int64_t* bcsr_row_ptr, int64_t* bcsr_col_ind, void* bcsr_values);
+
+/* ---------------------------------------------------------------------------------------------
+ * Dense unpermute: out[perm[r]*N + c] = in[r*N + c]. Replaces xspmm::unpermute_dense_matrix
+ * (include/xspmm/xspmm.hpp:35-40, src/xspmm.cpp:116-134, src/cuda/mtx_permutation.cu:71-85,
+ * kernel src/common/permutation.hpp:89-108). in and out must not overlap.
+ * ------------------------------------------------------------------------------------------- */
+xspmm_status_t xspmm_unpermute_dense_f32_i32(xspmm_handle_t h, const void* in, void* out,
+    const int32_t* perm, int32_t M, int32_t N);
+xspmm_status_t xspmm_unpermute_dense_f32_i64(xspmm_handle_t h, const void* in, void* out,
+    const int64_t* perm, int64_t M, int64_t N);
+xspmm_status_t xspmm_unpermute_dense_f16_i32(xspmm_handle_t h, const void* in, void* out,
+    const int32_t* perm, int32_t M, int32_t N);
+xspmm_status_t xspmm_unpermute_dense_f16_i64(xspmm_handle_t h, const void* in, void* out,
+    const int64_t* perm, int64_t M, int64_t N);
+
+/* ---------------------------------------------------------------------------------------------
+ * Tier-2 pipeline: C = A * B for A in CSR, with optional clustering. Replaces
+ * xspmm::spmm(exec, CSR A, B, C, N, hw_block_size, optimize_pattern, timings)
+ * (include/xspmm/xspmm.hpp:24-32, src/xspmm.cpp:137-162, src/cuda/unstructured_mtx_mul.cu:56-130):
+ *   enable_clustering != 0: perm = cluster(A, 0.5, hw_block_size); A' = permute(A, perm);
+ *   A'' = csr_to_bcsr(A', 16, 16); C[perm[i]] = (A'' * B)[i]  (the unpermute is fused into the
+ *   SpMM store, so unpermutation_ms reports 0 and no M x N temporary is allocated).
+ *   enable_clustering == 0: C = csr_to_bcsr(A) * B.
+ * hw_block_size must be 16 (UNSUPPORTED otherwise). timings may be NULL; when given, the call
+ * synchronizes at the end of every stage to read its events, like the reference
+ * (src/cuda/unstructured_mtx_mul.cu:14-26).
+ * ------------------------------------------------------------------------------------------- */
+xspmm_status_t xspmm_spmm_csr_f16f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const void* B, float* C,
+    int32_t N, int32_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
+xspmm_status_t xspmm_spmm_csr_f16f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
+    int64_t N, int64_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
+xspmm_status_t xspmm_spmm_csr_f32f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const void* B, float* C,
+    int32_t N, int32_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
+xspmm_status_t xspmm_spmm_csr_f32f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
+    int64_t N, int64_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* XSPMM_B200_H */

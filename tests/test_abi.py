@@ -1,0 +1,62 @@
+"""CPU tests of the boundary: the C-ABI library loads, exports every symbol include/*.h declares,
+and its host-side argument handling answers without a GPU. No kernel is launched."""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from xspmm_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.lib()
+    declared = _lib.declared_symbols()
+    assert len(declared) >= 38
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [s for s in declared if s not in exported]
+    assert not missing, missing
+    for s in declared:
+        assert getattr(L, s) is not None
+
+
+def test_status_strings():
+    L = _lib.lib()
+    assert L.xspmm_status_string(0) == b"ok"
+    assert L.xspmm_status_string(2) == b"unsupported"
+
+
+def test_null_handle_is_rejected_without_a_gpu():
+    L = _lib.lib()
+    rc = L.xspmm_bcsr_spmm_f16f32_i32(None, 1, 1, 1, 16, 16, None, None, None, None, None, 16,
+                                      16, 8, None)
+    assert rc == 1  # INVALID_ARGUMENT
+    assert b"null handle" in L.xspmm_last_error()
+    c = ctypes.c_uint64()
+    assert L.xspmm_get_launch_count(None, ctypes.byref(c)) == 1
+
+
+def test_create_reports_a_status_instead_of_crashing():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present: creation is covered by the GPU tests")
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    rc = L.xspmm_create(0, None, ctypes.byref(h))
+    assert rc in (1, 3)  # no device: invalid ordinal or CUDA error
+
+
+def test_cpp_api_header_compiles_against_the_abi():
+    """include/xspmm/xspmm.hpp (the reference-shaped C++ API) compiles with the host compiler."""
+    src = os.path.join(ROOT, "tests", "cpp", "api_compile_check.cpp")
+    if not os.path.exists(src):
+        pytest.skip("no C++ compile check source")
+    cuda_inc = "/usr/local/cuda/include"
+    r = subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-I" + os.path.join(ROOT, "include"),
+                        "-I" + cuda_inc, src], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr

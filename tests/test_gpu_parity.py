@@ -1,0 +1,262 @@
+"""GPU parity tests: every stage of the hot path through the C ABI, checked against the golden
+fixtures (made by the reference's own host code) and the CPU oracle on the same seeded inputs.
+
+Bar: bit-exact permutation, permuted CSR, BCSR structure/values and unpermute; C within the
+north star's tolerance (max relative error 1e-3 for fp16 inputs, 1e-5 for fp32) under the guarded
+metric of tests.util.errors, with the reference's strict metric reported alongside."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import xspmm_b200 as xs
+from tests.util import TOL, errors, fp32_block_emulation, golden_cases, load_golden
+from xspmm_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+CASES = golden_cases()
+IDX = [torch.int32, torch.int64]
+NP_IDX = {torch.int32: np.int32, torch.int64: np.int64}
+
+
+def _csr(ex, M, K, rp, ci, v, idx, vdt=np.float16):
+    return xs.CSRMatrix.from_host(ex, M, K, rp, ci, np.asarray(v).astype(vdt), index_dtype=idx)
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+# ------------------------------------------------------------------------------------------------
+# structure: clustering, permutation, conversion, unpermute -- bit-exact
+# ------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("idx", IDX, ids=["i32", "i64"])
+@pytest.mark.parametrize("path", CASES, ids=[os.path.basename(p)[:-4] for p in CASES])
+def test_golden_structure(executor, path, idx):
+    g = load_golden(path)
+    M, K, tau, w = int(g["M"]), int(g["K"]), float(g["tau"]), int(g["w"])
+    A = _csr(executor, M, K, g["row_ptr"], g["col_ind"], g["vals"], idx, np.float32)
+    perm = torch.zeros(max(M, 1), dtype=idx, device=executor.device)
+    xs.compute_1d_jaccard_clustering(executor, A, tau, w, perm)
+    assert np.array_equal(_np(perm)[:M], g["perm"]), "clustering permutation"
+    permt = torch.as_tensor(g["perm"].astype(NP_IDX[idx])).to(executor.device)
+    P = xs.apply_permutation(executor, A, permt)
+    assert np.array_equal(_np(P.row_ptr), g["p_row_ptr"])
+    assert np.array_equal(_np(P.col_ind), g["p_col_ind"])
+    assert np.array_equal(_np(P.values).view(np.uint32), g["p_vals"].view(np.uint32))
+    for src, pre in ((A, "b_"), (P, "pb_")):
+        Bm = xs.csr_to_bcsr(executor, src, 16, 16)
+        assert np.array_equal(_np(Bm.row_ptr), g[pre + "row_ptr"])
+        assert np.array_equal(_np(Bm.col_ind), g[pre + "col_ind"])
+        assert np.array_equal(_np(Bm.values).reshape(-1).view(np.uint32),
+                              g[pre + "vals"].reshape(-1).view(np.uint32))
+
+
+def _random(seed, M=None, K=None):
+    rng = np.random.default_rng(seed)
+    M = int(rng.integers(1, 400)) if M is None else M
+    K = int(rng.integers(1, 400)) if K is None else K
+    dens = float(rng.choice([0.005, 0.02, 0.1, 0.3]))
+    rp, ci, v = synth.random_csr(M, K, dens, seed=seed,
+                                 empty_row_frac=float(rng.choice([0, 0.2])),
+                                 dup_frac=float(rng.choice([0, 0.05])),
+                                 shuffle_cols=bool(rng.integers(0, 2)))
+    return M, K, rp, ci, v
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_structure_vs_oracle(executor, seed):
+    M, K, rp, ci, v = _random(seed)
+    idx = IDX[seed % 2]
+    tau = [0.5, 0.3, 0.8, 0.5][seed % 4]
+    w = [16, 16, 4, 7][(seed // 2) % 4]
+    A = _csr(executor, M, K, rp, ci, v, idx)
+    perm = torch.zeros(M, dtype=idx, device=executor.device)
+    xs.compute_1d_jaccard_clustering(executor, A, tau, w, perm)
+    ref_perm = oracle.cluster_fast(rp, ci, M, K, tau, w)
+    assert np.array_equal(_np(perm), ref_perm)
+    P = xs.apply_permutation(executor, A, perm)
+    orp, oci, ov = oracle.permute_rows(rp, ci, np.asarray(v, np.float16), ref_perm)
+    assert np.array_equal(_np(P.row_ptr), orp) and np.array_equal(_np(P.col_ind), oci)
+    assert np.array_equal(_np(P.values).view(np.uint16), ov.view(np.uint16))
+    for rb, cb in ((16, 16), (3, 5), (1, 16), (32, 8)):
+        Bm = xs.csr_to_bcsr(executor, P, rb, cb)
+        brp, bci, bv = oracle.csr_to_bcsr(orp, oci, ov, M, K, rb, cb)
+        assert np.array_equal(_np(Bm.row_ptr), brp) and np.array_equal(_np(Bm.col_ind), bci)
+        assert np.array_equal(_np(Bm.values).reshape(-1).view(np.uint16),
+                              bv.reshape(-1).view(np.uint16))
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("cfg2", {}),                                   # full size: 16384^2 hidden blocks
+    ("cfg3", dict(N=16)),                           # full size: 4096 x 11008, 10 %
+    ("cfg1", {}),                                   # full size (clustering structure only)
+    ("cfg4", dict(n=1 << 16, N=8)),
+    ("cfg5", dict(scale=14, N=8)),
+])
+def test_config_clustering_vs_oracle(executor, name, kw):
+    P = synth.CONFIGS[name](**kw)
+    A = _csr(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values, torch.int32,
+             P.values.dtype)
+    perm = torch.zeros(P.M, dtype=torch.int32, device=executor.device)
+    xs.compute_1d_jaccard_clustering(executor, A, 0.5, 16, perm)
+    assert np.array_equal(_np(perm), oracle.cluster_fast(P.row_ptr, P.col_ind, P.M, P.K))
+
+
+@pytest.mark.parametrize("idx", IDX, ids=["i32", "i64"])
+def test_unpermute_bit_exact(executor, idx):
+    rng = np.random.default_rng(5)
+    for M, N, dt in ((1000, 37, torch.float32), (513, 64, torch.float32), (77, 16, torch.float16)):
+        X = torch.randn(M, N, device=executor.device).to(dt)
+        perm_np = rng.permutation(M)
+        perm = torch.as_tensor(perm_np.astype(NP_IDX[idx])).to(executor.device)
+        out = torch.zeros_like(X)
+        xs.unpermute_dense_matrix(executor, X, out, perm, M, N)
+        exp = oracle.unpermute_dense(_np(X), perm_np)
+        assert np.array_equal(_np(out).view(np.uint8), exp.view(np.uint8))
+
+
+# ------------------------------------------------------------------------------------------------
+# Tier-1 SpMM -- within tolerance of the fp64 restatement
+# ------------------------------------------------------------------------------------------------
+def _tier1_check(executor, M, K, N, rp, ci, v, vdt, idx, seed=0, long_rows=False):
+    """long_rows: also accept up to twice the error of an IEEE fp32 emulation of the reference's
+    block loop. The guarded floor of 1e-3*rms asks for absolute errors below ~1e-6*rms, which
+    fp32 accumulation over thousands of terms cannot give (the reference's WMMA path included)."""
+    rng = np.random.default_rng(seed)
+    B = rng.standard_normal((K, N)).astype(vdt)
+    A = _csr(executor, M, K, rp, ci, v, idx, vdt)
+    Ab = xs.csr_to_bcsr(executor, A, 16, 16)
+    Bt = torch.as_tensor(B).to(executor.device)
+    C = torch.full((M, N), float("nan"), dtype=torch.float32, device=executor.device)
+    xs.spmm(Ab, Bt, C, N)
+    brp, bci, bv = oracle.csr_to_bcsr(rp, ci, np.asarray(v).astype(vdt), M, K)
+    ref = oracle.bcsr_spmm_f64(M, K, N, brp, bci, bv, B)
+    e = errors(ref, _np(C), floor_rel=TOL[np.dtype(vdt)])
+    assert np.isfinite(_np(C)).all(), "C not fully written"
+    bound = TOL[np.dtype(vdt)]
+    if long_rows and e["max_rel_guarded"] > bound:
+        e32 = errors(ref, fp32_block_emulation(M, N, brp, bci, bv, B), TOL[np.dtype(vdt)])
+        e["fp32_emulation_guarded"] = e32["max_rel_guarded"]
+        bound = max(bound, 2.0 * e32["max_rel_guarded"])
+    assert e["max_rel_guarded"] <= bound, e
+    return e
+
+
+@pytest.mark.parametrize("vdt", [np.float16, np.float32], ids=["f16", "f32"])
+@pytest.mark.parametrize("N", [1, 2, 4, 8, 17, 18, 24, 30, 31, 64, 128, 200, 256, 300])
+def test_tier1_ragged_n(executor, vdt, N):
+    """The reference's examples/06 N sweep, on a 16x16-unaligned matrix."""
+    M, K, rp, ci, v = _random(100 + N, M=203, K=181)
+    _tier1_check(executor, M, K, N, rp, ci, v, vdt, torch.int32 if N % 2 else torch.int64)
+
+
+@pytest.mark.parametrize("vdt", [np.float16, np.float32], ids=["f16", "f32"])
+def test_tier1_empty_rows_and_blocks(executor, vdt):
+    rp, ci, v = synth.random_csr(160, 96, 0.05, seed=7, empty_row_frac=0.6)
+    _tier1_check(executor, 160, 96, 40, rp, ci, v, vdt, torch.int64)
+    rp, ci, v = synth.random_csr(48, 48, 0.0, seed=8)
+    _tier1_check(executor, 48, 48, 16, rp, ci, v, vdt, torch.int32)
+
+
+def test_tier1_dense_blocks_long_rows(executor):
+    """Every block present (the pruned-LLM structure) with long block rows and N up to 1024."""
+    P = synth.cfg3_pruned_llm(seed=11, M=256, K=2048, N=8)
+    for N in (16, 256, 1024):
+        _tier1_check(executor, P.M, P.K, N, P.row_ptr, P.col_ind, P.values, np.float16,
+                     torch.int32, seed=N, long_rows=True)
+
+
+def test_tier1_row_map_scatter(executor):
+    M, K, N = 300, 200, 48
+    rp, ci, v = synth.random_csr(M, K, 0.05, seed=9)
+    rng = np.random.default_rng(9)
+    B = rng.standard_normal((K, N)).astype(np.float16)
+    perm = rng.permutation(M).astype(np.int64)
+    A = _csr(executor, M, K, rp, ci, v, torch.int64)
+    Ab = xs.csr_to_bcsr(executor, A, 16, 16)
+    C = torch.zeros((M, N), dtype=torch.float32, device=executor.device)
+    xs.api._tier1(Ab, torch.as_tensor(B).to(executor.device), C, N,
+                  out_row_map=torch.as_tensor(perm).to(executor.device))
+    brp, bci, bv = oracle.csr_to_bcsr(rp, ci, np.asarray(v, np.float16), M, K)
+    ref = oracle.unpermute_dense(oracle.bcsr_spmm_f64(M, K, N, brp, bci, bv, B), perm)
+    assert errors(ref, _np(C), 1e-3)["max_rel_guarded"] <= 1e-3
+
+
+# ------------------------------------------------------------------------------------------------
+# Tier-2 pipeline
+# ------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("clustering", [True, False])
+@pytest.mark.parametrize("name,kw,vdt", [
+    ("cfg2", dict(n=4096, N=64), np.float16),
+    ("cfg1", dict(M=1024, K=1024, N=128), np.float32),
+    ("cfg4", dict(n=1 << 14, N=64), np.float16),
+    ("cfg5", dict(scale=12, N=32), np.float16),
+])
+def test_pipeline_vs_oracle(executor, name, kw, vdt, clustering):
+    P = synth.CONFIGS[name](**kw)
+    A = _csr(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values, torch.int64, vdt)
+    B = torch.as_tensor(P.B.astype(vdt)).to(executor.device)
+    C = torch.full((P.M, P.N), float("nan"), dtype=torch.float32, device=executor.device)
+    t = xs.SpMMTimings()
+    xs.spmm(executor, A, B, C, P.N, 16, clustering, t)
+    if clustering:
+        perm = oracle.cluster_fast(P.row_ptr, P.col_ind, P.M, P.K)
+        prp, pci, pv = oracle.permute_rows(P.row_ptr, P.col_ind, P.values.astype(vdt), perm)
+        brp, bci, bv = oracle.csr_to_bcsr(prp, pci, pv, P.M, P.K)
+        ref = oracle.unpermute_dense(
+            oracle.bcsr_spmm_f64(P.M, P.K, P.N, brp, bci, bv, P.B.astype(vdt)), perm)
+        assert t.clustering_ms > 0
+    else:
+        brp, bci, bv = oracle.csr_to_bcsr(P.row_ptr, P.col_ind, P.values.astype(vdt), P.M, P.K)
+        ref = oracle.bcsr_spmm_f64(P.M, P.K, P.N, brp, bci, bv, P.B.astype(vdt))
+    e = errors(ref, _np(C), TOL[np.dtype(vdt)])
+    assert e["max_rel_guarded"] <= TOL[np.dtype(vdt)], e
+    assert t.total_pipeline_ms >= t.spmm_ms > 0 and t.conversion_ms > 0
+
+
+def test_pipeline_int32_and_launch_count(executor):
+    P = synth.cfg2_hidden_block(seed=3, n=2048, N=32)
+    A = _csr(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values, torch.int32)
+    B = torch.as_tensor(P.B).to(executor.device)
+    C = torch.zeros((P.M, P.N), dtype=torch.float32, device=executor.device)
+    executor.reset_launch_count()
+    xs.spmm(executor, A, B, C, P.N)
+    assert executor.launch_count() >= 8
+    perm = oracle.cluster_fast(P.row_ptr, P.col_ind, P.M, P.K)
+    prp, pci, pv = oracle.permute_rows(P.row_ptr, P.col_ind, P.values, perm)
+    brp, bci, bv = oracle.csr_to_bcsr(prp, pci, pv, P.M, P.K)
+    ref = oracle.unpermute_dense(oracle.bcsr_spmm_f64(P.M, P.K, P.N, brp, bci, bv, P.B), perm)
+    assert errors(ref, _np(C), 1e-3)["max_rel_guarded"] <= 1e-3
+
+
+# ------------------------------------------------------------------------------------------------
+# error behaviour (host-side checks and device flags; nothing faults)
+# ------------------------------------------------------------------------------------------------
+def test_errors(executor):
+    rp, ci, v = synth.random_csr(32, 32, 0.2, seed=1)
+    A = _csr(executor, 32, 32, rp, ci, v, torch.int64)
+    B = torch.zeros((32, 8), dtype=torch.float16, device=executor.device)
+    C = torch.zeros((32, 8), dtype=torch.float32, device=executor.device)
+    with pytest.raises(xs.XSpMMError, match="UNSUPPORTED"):
+        xs.spmm(executor, A, B, C, 8, 8, True)
+    bad = torch.as_tensor(np.arange(32)[::-1].copy()).to(executor.device)
+    bad[3] = 40
+    with pytest.raises(xs.XSpMMError, match="INVALID_ARGUMENT"):
+        xs.apply_permutation(executor, A, bad)
+    bad[3] = 5  # duplicate entry
+    with pytest.raises(xs.XSpMMError, match="INVALID_ARGUMENT"):
+        xs.apply_permutation(executor, A, bad)
+    ci2 = ci.copy()
+    ci2[0] = 99  # column outside [0, K)
+    A2 = _csr(executor, 32, 32, rp, ci2, v, torch.int64)
+    with pytest.raises(xs.XSpMMError, match="INVALID_ARGUMENT"):
+        xs.csr_to_bcsr(executor, A2, 16, 16)
+    with pytest.raises(ValueError):
+        xs.CSRMatrix(executor, -1, 3, 0)
+    # the handle stays usable after reported errors
+    xs.spmm(executor, A, B, C, 8)
+    executor.synchronize()

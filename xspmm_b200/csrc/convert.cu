@@ -1,0 +1,296 @@
+// convert.cu -- CSR -> BCSR on the device.
+//
+// Reproduces src/core/conversion.cpp:8-100 bit for bit:
+//   * block row br covers rows [br*rb, min(M, br*rb+rb)); its blocks are the distinct column
+//     blocks floor(col/cb) of those rows, sorted ascending (conversion.cpp:42-64);
+//   * row_ptr is the running count (:66-68);
+//   * values are zero-filled, then every CSR entry is stored at
+//     (row_ptr[br] + rank(bc))*rb*cb + (r % rb)*cb + col % cb, in CSR order, so a duplicated
+//     (row, col) keeps its last value (:75-91). Explicit zeros still create blocks.
+//
+// Design: one warp per block row. The warp marks the block columns of its rows in a bitmap window
+// of 8192 bits held in shared memory (atomicOr), so the sorted distinct list falls out of the bit
+// order: count = sum of popc over the window, and an entry's rank = the prefix popcount up to its
+// bit. Ranges wider than a window take several passes. The count kernel writes per-block-row
+// counts (scanned on the device into row_ptr); the fill kernel rebuilds the bitmap, writes the
+// column indices and scatters values. Rows whose columns are strictly increasing (no duplicates)
+// scatter in parallel across lanes -- distinct rows never share a destination; any other row is
+// written by one lane in CSR order so the last duplicate wins, as in the reference.
+#include "ops.cuh"
+
+#include <algorithm>
+
+namespace xspmm_b200 {
+namespace {
+
+constexpr int CV_WARPS = 8;
+constexpr int WIN_WORDS = 256;
+constexpr int64_t WIN_BITS = (int64_t)WIN_WORDS * 32;
+constexpr int WORDS_PER_LANE = WIN_WORDS / 32;
+
+struct BlockDiv {
+    int shift;    // >= 0 when the block width is a power of two
+    int64_t div;  // block width
+    __device__ __forceinline__ int64_t operator()(int64_t c) const {
+        return shift >= 0 ? (c >> shift) : (c / div);
+    }
+};
+
+BlockDiv make_div(int64_t w) {
+    BlockDiv d{-1, w};
+    if (w > 0 && (w & (w - 1)) == 0) {
+        int s = 0;
+        while ((int64_t(1) << s) < w) ++s;
+        d.shift = s;
+    }
+    return d;
+}
+
+__device__ __forceinline__ int64_t warp_min64(int64_t v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = min(v, (int64_t)__shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ int64_t warp_max64(int64_t v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = max(v, (int64_t)__shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ int64_t warp_sum64(int64_t v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Block-column range [lo, hi] of entries [e0, e1); flags out-of-range columns. hi < 0 if none.
+template <typename IT>
+__device__ void block_col_range(const IT* ci, int64_t e0, int64_t e1, int64_t K, BlockDiv bd,
+                                int64_t& lo, int64_t& hi, unsigned* err) {
+    const int lane = threadIdx.x & 31;
+    lo = INT64_MAX;
+    hi = -1;
+    bool bad = false;
+    for (int64_t e = e0 + lane; e < e1; e += 32) {
+        const int64_t c = (int64_t)ci[e];
+        if (c < 0 || c >= K) {
+            bad = true;
+            continue;
+        }
+        const int64_t b = bd(c);
+        lo = min(lo, b);
+        hi = max(hi, b);
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0 && err) flag_error(err, DERR_COL_OUT_OF_RANGE);
+    lo = warp_min64(lo);
+    hi = warp_max64(hi);
+}
+
+// Marks the block columns of entries [e0, e1) that fall in [wb, wb + nwords*32) in win.
+template <typename IT>
+__device__ void mark_window(uint32_t* win, int nwords, const IT* ci, int64_t e0, int64_t e1,
+                            int64_t K, BlockDiv bd, int64_t wb) {
+    const int lane = threadIdx.x & 31;
+    for (int w = lane; w < nwords; w += 32) win[w] = 0u;
+    __syncwarp();
+    const int64_t span = (int64_t)nwords * 32;
+    for (int64_t e = e0 + lane; e < e1; e += 32) {
+        const int64_t c = (int64_t)ci[e];
+        if (c < 0 || c >= K) continue;
+        const int64_t d = bd(c) - wb;
+        if (d >= 0 && d < span) atomicOr(&win[d >> 5], 1u << (d & 31));
+    }
+    __syncwarp();
+}
+
+// Validates row_ptr over [r0, r1]; returns false (and flags) when it is malformed.
+template <typename IT>
+__device__ bool rows_ok(const IT* rp, int64_t r0, int64_t r1, int64_t nnz, unsigned* err) {
+    const int lane = threadIdx.x & 31;
+    bool bad = false;
+    for (int64_t r = r0 + lane; r < r1; r += 32) {
+        const int64_t a = (int64_t)rp[r], b = (int64_t)rp[r + 1];
+        if (a < 0 || a > b || b > nnz) bad = true;
+    }
+    if (__any_sync(0xffffffffu, bad)) {
+        if (lane == 0 && err) flag_error(err, DERR_ROW_PTR);
+        return false;
+    }
+    return true;
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(CV_WARPS * 32)
+bcsr_count_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, int64_t M, int64_t K,
+                  int64_t nnz, int64_t nbr, int64_t rb, BlockDiv bd, IT* __restrict__ counts,
+                  unsigned* err) {
+    __shared__ uint32_t win_all[CV_WARPS][WIN_WORDS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t* win = win_all[warp];
+    for (int64_t br = (int64_t)blockIdx.x * CV_WARPS + warp; br < nbr;
+         br += (int64_t)gridDim.x * CV_WARPS) {
+        const int64_t r0 = br * rb, r1 = min(M, r0 + rb);
+        if (!rows_ok(rp, r0, r1, nnz, err)) {
+            if (lane == 0) counts[br] = 0;
+            continue;
+        }
+        const int64_t e0 = rp[r0], e1 = rp[r1];
+        int64_t lo, hi;
+        block_col_range(ci, e0, e1, K, bd, lo, hi, err);
+        int64_t count = 0;
+        for (int64_t wb = lo; wb <= hi; wb += WIN_BITS) {
+            const int nwords = (int)min((int64_t)WIN_WORDS, (hi - wb) / 32 + 1);
+            mark_window(win, nwords, ci, e0, e1, K, bd, wb);
+            int64_t c = 0;
+            for (int w = lane; w < nwords; w += 32) c += __popc(win[w]);
+            count += warp_sum64(c);
+            __syncwarp();
+        }
+        if (lane == 0) counts[br] = (IT)count;
+    }
+}
+
+template <typename VT, typename IT>
+__global__ void __launch_bounds__(CV_WARPS * 32)
+bcsr_fill_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const VT* __restrict__ v,
+                 int64_t M, int64_t K, int64_t nbr, int64_t rb, int64_t cb, BlockDiv bd,
+                 const IT* __restrict__ brp, IT* __restrict__ bci, VT* __restrict__ bvals) {
+    __shared__ uint32_t win_all[CV_WARPS][WIN_WORDS];
+    __shared__ uint32_t pre_all[CV_WARPS][WIN_WORDS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t* win = win_all[warp];
+    uint32_t* pre = pre_all[warp];
+    const int64_t bsz = rb * cb;
+    for (int64_t br = (int64_t)blockIdx.x * CV_WARPS + warp; br < nbr;
+         br += (int64_t)gridDim.x * CV_WARPS) {
+        const int64_t base = brp[br], nb = (int64_t)brp[br + 1] - base;
+        if (nb <= 0) continue;
+        const int64_t r0 = br * rb, r1 = min(M, r0 + rb);
+        const int64_t e0 = rp[r0], e1 = rp[r1];
+        if (bvals) {  // zero the block row's blocks
+            VT* z = bvals + base * bsz;
+            const int64_t n = nb * bsz;
+            const int64_t bytes = n * (int64_t)sizeof(VT);
+            if (reinterpret_cast<uintptr_t>(z) % 16 == 0 && bytes % 16 == 0) {
+                uint4* z4 = reinterpret_cast<uint4*>(z);
+                for (int64_t t = lane; t < bytes / 16; t += 32) z4[t] = make_uint4(0, 0, 0, 0);
+            } else {
+                for (int64_t t = lane; t < n; t += 32) z[t] = VT(0.0f);
+            }
+            __syncwarp();
+        }
+        int64_t lo, hi;
+        block_col_range(ci, e0, e1, K, bd, lo, hi, nullptr);
+        int64_t rank_base = 0;
+        for (int64_t wb = lo; wb <= hi; wb += WIN_BITS) {
+            const int nwords = (int)min((int64_t)WIN_WORDS, (hi - wb) / 32 + 1);
+            mark_window(win, nwords, ci, e0, e1, K, bd, wb);
+            // exclusive prefix popcount per word; lane owns words [lane*8, lane*8+8)
+            uint32_t local[WORDS_PER_LANE];
+            uint32_t lsum = 0;
+#pragma unroll
+            for (int k = 0; k < WORDS_PER_LANE; ++k) {
+                const int w = lane * WORDS_PER_LANE + k;
+                local[k] = w < nwords ? __popc(win[w]) : 0u;
+                lsum += local[k];
+            }
+            const uint32_t incl = warp_inclusive_sum(lsum);
+            uint32_t run = incl - lsum;
+#pragma unroll
+            for (int k = 0; k < WORDS_PER_LANE; ++k) {
+                const int w = lane * WORDS_PER_LANE + k;
+                if (w < nwords) {
+                    pre[w] = run;
+                    // column indices of this word's blocks, ascending
+                    uint32_t x = win[w];
+                    int64_t o = base + rank_base + run;
+                    while (x) {
+                        const int b = __ffs(x) - 1;
+                        bci[o++] = (IT)(wb + (int64_t)w * 32 + b);
+                        x &= x - 1;
+                    }
+                }
+                run += local[k];
+            }
+            const uint32_t wtotal = __shfl_sync(0xffffffffu, incl, 31);
+            __syncwarp();
+            if (bvals) {
+                for (int64_t r = r0; r < r1; ++r) {
+                    const int64_t s = rp[r], t = rp[r + 1];
+                    bool unsorted = false;
+                    for (int64_t e = s + lane; e + 1 < t; e += 32)
+                        if (ci[e] >= ci[e + 1]) unsorted = true;
+                    unsorted = __any_sync(0xffffffffu, unsorted);
+                    const int64_t roff = (r - r0) * cb;
+                    auto put = [&](int64_t e) {
+                        const int64_t c = (int64_t)ci[e];
+                        if (c < 0 || c >= K) return;
+                        const int64_t b = bd(c);
+                        const int64_t d = b - wb;
+                        if (d < 0 || d >= (int64_t)nwords * 32) return;
+                        const uint32_t word = win[d >> 5];
+                        const int64_t rank =
+                            rank_base + pre[d >> 5] + __popc(word & ((1u << (d & 31)) - 1u));
+                        bvals[(base + rank) * bsz + roff + (c - b * cb)] = v[e];
+                    };
+                    if (!unsorted) {
+                        for (int64_t e = s + lane; e < t; e += 32) put(e);
+                    } else if (lane == 0) {
+                        for (int64_t e = s; e < t; ++e) put(e);
+                    }
+                }
+            }
+            rank_base += wtotal;
+            __syncwarp();
+        }
+    }
+}
+
+unsigned cv_grid(Handle& h, int64_t nbr) {
+    const int64_t want = ceil_div(nbr, CV_WARPS);
+    const int64_t cap = (int64_t)sm_count(h.device) * 32;
+    return (unsigned)std::max<int64_t>(1, std::min(want, cap));
+}
+
+}  // namespace
+
+template <typename IT>
+int64_t csr_to_bcsr_count(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
+                          const IT* col_ind, int64_t rb, int64_t cb, IT* brp) {
+    const int64_t nbr = ceil_div(M, rb);
+    if (nbr == 0) {
+        XS_CHECK_CUDA(cudaMemsetAsync(brp, 0, sizeof(IT), h.stream));
+        return 0;
+    }
+    bcsr_count_kernel<IT><<<cv_grid(h, nbr), CV_WARPS * 32, 0, h.stream>>>(
+        row_ptr, col_ind, M, K, nnz, nbr, rb, make_div(cb), brp, h.d_err);
+    after_launch(h, "bcsr_count");
+    exclusive_scan<IT>(h, brp, brp, nbr);
+    throw_on_device_errors(h, "csr_to_bcsr");
+    return (int64_t)read_scalar<IT>(h, brp + nbr);
+}
+
+template <typename VT, typename IT>
+void csr_to_bcsr_fill(Handle& h, int64_t M, int64_t K, int64_t, const IT* row_ptr,
+                      const IT* col_ind, const VT* values, int64_t rb, int64_t cb, const IT* brp,
+                      IT* bci, VT* bvals) {
+    const int64_t nbr = ceil_div(M, rb);
+    if (nbr == 0) return;
+    bcsr_fill_kernel<VT, IT><<<cv_grid(h, nbr), CV_WARPS * 32, 0, h.stream>>>(
+        row_ptr, col_ind, values, M, K, nbr, rb, cb, make_div(cb), brp, bci, bvals);
+    after_launch(h, "bcsr_fill");
+}
+
+template int64_t csr_to_bcsr_count<int32_t>(Handle&, int64_t, int64_t, int64_t, const int32_t*,
+                                            const int32_t*, int64_t, int64_t, int32_t*);
+template int64_t csr_to_bcsr_count<int64_t>(Handle&, int64_t, int64_t, int64_t, const int64_t*,
+                                            const int64_t*, int64_t, int64_t, int64_t*);
+#define XS_INST_FILL(VT, IT)                                                                      \
+    template void csr_to_bcsr_fill<VT, IT>(Handle&, int64_t, int64_t, int64_t, const IT*,         \
+                                           const IT*, const VT*, int64_t, int64_t, const IT*, IT*, \
+                                           VT*);
+XS_INST_FILL(__half, int32_t)
+XS_INST_FILL(__half, int64_t)
+XS_INST_FILL(float, int32_t)
+XS_INST_FILL(float, int64_t)
+
+}  // namespace xspmm_b200

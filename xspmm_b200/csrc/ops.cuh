@@ -1,0 +1,47 @@
+// ops.cuh -- internal host entry points of the library, one per hot-path operation. The C ABI in
+// capi.cu validates arguments, picks the instantiation and calls these; the Tier-2 pipeline
+// composes them.
+#pragma once
+
+#include "common.cuh"
+
+namespace xspmm_b200 {
+
+// Tier-1 BCSR SpMM (16x16 blocks). VT = __half or float; C is fp32. row_map may be null.
+template <typename VT, typename IT>
+void bcsr_spmm(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* row_ptr,
+               const IT* col_ind, const VT* values, const VT* B, float* C, int64_t M, int64_t K,
+               int64_t N, const IT* row_map);
+
+// Exact greedy Jaccard clustering (writes perm[M]).
+template <typename IT>
+void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
+                     const IT* col_ind, float tau, int64_t w, IT* perm);
+
+// CSR row permutation into caller-provided arrays. check = validate perm and synchronize.
+template <typename VT, typename IT>
+void permute_rows(Handle& h, int64_t M, int64_t nnz, const IT* row_ptr, const IT* col_ind,
+                  const VT* values, const IT* perm, IT* out_row_ptr, IT* out_col_ind,
+                  VT* out_values, bool check);
+
+// CSR -> BCSR: count (writes brp[nbr+1], returns nnzb, synchronizes) and fill.
+template <typename IT>
+int64_t csr_to_bcsr_count(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
+                          const IT* col_ind, int64_t rb, int64_t cb, IT* brp);
+template <typename VT, typename IT>
+void csr_to_bcsr_fill(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
+                      const IT* col_ind, const VT* values, int64_t rb, int64_t cb, const IT* brp,
+                      IT* bci, VT* bvals);
+
+// Dense unpermute out[perm[r]] = in[r] (rows of N elements).
+template <typename VT, typename IT>
+void unpermute_dense(Handle& h, const VT* in, VT* out, const IT* perm, int64_t M, int64_t N,
+                     bool check);
+
+// Tier-2 pipeline.
+template <typename VT, typename IT>
+void spmm_csr_pipeline(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
+                       const IT* col_ind, const VT* values, const VT* B, float* C, int64_t N,
+                       int64_t hw, bool clustering, xspmm_timings_t* timings);
+
+}  // namespace xspmm_b200

@@ -1,0 +1,242 @@
+// spmm_f16.cu -- Tier-1 BCSR SpMM, fp16 blocks x fp16 B -> fp32 C, on the warp-level tensor-core
+// path (mma.sync m16n8k16 with fp32 accumulation).
+//
+// Semantics follow the reference kernel (src/common/spmm_math.hpp:59-122): for block row br,
+// C[16br+i, n] = sum over its blocks j (in col_ind order) of A_j[i, :] . B[16 col_j + :, n], every
+// row of C written (zeros for block rows without blocks). Unlike the reference it guards the
+// ragged last block row (rows >= M are not written) and block column (B rows >= K read as zero),
+// takes a 1-D grid over block rows (the reference's gridDim.y = num_block_rows stops at 65,535)
+// and uses 64-bit value offsets (the reference's int32 i*256 overflows past 2^31 values).
+//
+// Work split: a CTA owns one block row and a TN = 64*WARPS column tile; each warp owns 64 columns
+// (8 n8 tiles, 32 fp32 accumulators per thread). Each block's product is formed by the tensor core
+// in a zeroed fragment and added to the accumulators with IEEE round-to-nearest adds, so a long
+// block row does not collect one accumulator truncation per block. Per block the CTA stages the 16x16 A block
+// (512 B) and the 16 x TN slab of B rows 16*col .. 16*col+15 into shared memory with 16-byte
+// cp.async, STAGES deep. A is read with ldmatrix.x4 (rows XOR-swizzled by (row>>2)&1), B with
+// ldmatrix.x4.trans (16-byte chunks XOR-swizzled by k&7), both conflict-free. When N is not a
+// multiple of 8 the B rows are not 16-byte aligned and the slab is loaded with guarded scalar
+// loads instead.
+#include "ops.cuh"
+
+namespace xspmm_b200 {
+namespace {
+
+constexpr int STAGES = 4;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <typename IT, int WARPS, bool ALIGNED>
+__global__ void __launch_bounds__(WARPS * 32)
+bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_ind,
+                         const __half* __restrict__ vals, const __half* __restrict__ B,
+                         float* __restrict__ C, const IT* __restrict__ row_map, int64_t M,
+                         int64_t K, int64_t N, unsigned* __restrict__ err) {
+    constexpr int TN = 64 * WARPS;
+    constexpr int A_BYTES = 512;
+    constexpr int ROW_BYTES = TN * 2;
+    constexpr int B_BYTES = 16 * ROW_BYTES;
+    constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    constexpr int CPR = TN / 8;  // 16-byte chunks per B row
+    constexpr int THREADS = WARPS * 32;
+    extern __shared__ __align__(128) uint8_t smem[];
+
+    const int64_t br = blockIdx.x;
+    const int64_t n0 = (int64_t)blockIdx.y * TN;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t jb = row_ptr[br];
+    const int nblk = (int)(row_ptr[br + 1] - jb);
+    const bool warp_active = n0 + warp * 64 < N;
+
+    auto load_stage = [&](int stage, int64_t j) {
+        uint8_t* sA = smem + stage * STAGE_BYTES;
+        uint8_t* sB = sA + A_BYTES;
+        const int64_t bc = (int64_t)col_ind[j];
+        if (threadIdx.x < 32) {
+            const int c = threadIdx.x, row = c >> 1, ch = c & 1;
+            uint8_t* dst = sA + row * 32 + ((ch ^ ((row >> 2) & 1)) * 16);
+            const __half* src = vals + j * 256 + row * 16 + ch * 8;
+            if constexpr (ALIGNED) {
+                cp_async16(dst, src, 16);
+            } else {
+                __align__(16) __half t[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) t[e] = src[e];
+                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(t);
+            }
+        }
+        for (int c = threadIdx.x; c < 16 * CPR; c += THREADS) {
+            const int k = c / CPR, ch = c % CPR;
+            const int64_t grow = bc * 16 + k;
+            const int64_t gcol = n0 + ch * 8;
+            uint8_t* dst = sB + k * ROW_BYTES + ((ch ^ (k & 7)) * 16);
+            if constexpr (ALIGNED) {
+                const bool ok = grow < K && gcol < N;
+                cp_async16(dst, ok ? (const void*)(B + grow * N + gcol) : (const void*)B,
+                           ok ? 16 : 0);
+            } else {
+                __align__(16) __half t[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    t[e] = (grow < K && gcol + e < N) ? B[grow * N + gcol + e] : __half(0.0f);
+                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(t);
+            }
+        }
+    };
+
+    float acc[8][4];
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
+
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < nblk) load_stage(s, jb + s);
+        cp_async_commit();
+    }
+
+    // per-lane ldmatrix offsets (bytes within a stage)
+    const int mi = lane >> 3, rin = lane & 7;
+    const int a_row = rin + 8 * (mi & 1);
+    const int a_off = a_row * 32 + (((mi >> 1) ^ ((a_row >> 2) & 1)) * 16);
+    const int b_k = rin + 8 * (mi & 1);
+
+    for (int i = 0; i < nblk; ++i) {
+        cp_async_wait<STAGES - 2>();
+        __syncthreads();
+        const uint8_t* sA = smem + (i % STAGES) * STAGE_BYTES;
+        const uint8_t* sB = sA + A_BYTES;
+        if (warp_active) {
+            uint32_t a[4];
+            ldmatrix_x4(a, sA + a_off);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int chunk = (warp * 64 + j * 16) / 8 + (mi >> 1);
+                uint32_t b[4];
+                ldmatrix_x4_trans(b, sB + b_k * ROW_BYTES + ((chunk ^ (b_k & 7)) * 16));
+                // One block's 16-term products go through the tensor core into a zeroed
+                // fragment; the running sum is kept with round-to-nearest FADD. Accumulating in
+                // the MMA itself would add one truncation per block to every output.
+                float p0[4] = {0.f, 0.f, 0.f, 0.f}, p1[4] = {0.f, 0.f, 0.f, 0.f};
+                mma_16816(p0, a, b[0], b[1]);
+                mma_16816(p1, a, b[2], b[3]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    acc[2 * j][e] = __fadd_rn(acc[2 * j][e], p0[e]);
+                    acc[2 * j + 1][e] = __fadd_rn(acc[2 * j + 1][e], p1[e]);
+                }
+            }
+        }
+        const int nx = i + STAGES - 1;
+        if (nx < nblk) load_stage(nx % STAGES, jb + nx);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+
+    if (!warp_active) return;
+    const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int64_t r = br * 16 + g + 8 * half;
+        if (r >= M) continue;
+        const int64_t orow = row_map ? (int64_t)row_map[r] : r;
+        if (orow < 0 || orow >= M) {
+            flag_error(err, DERR_PERM_OUT_OF_RANGE);
+            continue;
+        }
+        float* crow = C + orow * N;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int64_t col = n0 + warp * 64 + t * 8 + 2 * q;
+            const float v0 = acc[t][2 * half], v1 = acc[t][2 * half + 1];
+            if constexpr (ALIGNED) {
+                if (col < N) *reinterpret_cast<float2*>(crow + col) = make_float2(v0, v1);
+            } else {
+                if (col < N) crow[col] = v0;
+                if (col + 1 < N) crow[col + 1] = v1;
+            }
+        }
+    }
+}
+
+template <typename IT, int WARPS, bool ALIGNED>
+void launch(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v, const __half* B,
+            float* C, int64_t M, int64_t K, int64_t N, const IT* map) {
+    constexpr int TN = 64 * WARPS;
+    constexpr int smem = STAGES * (512 + 16 * TN * 2);
+    static_assert(smem <= 48 * 1024, "stage ring must fit the default dynamic smem limit");
+    auto kern = bcsr_spmm_f16_mma_kernel<IT, WARPS, ALIGNED>;
+    dim3 grid((unsigned)nbr, (unsigned)ceil_div(N, TN));
+    kern<<<grid, WARPS * 32, smem, h.stream>>>(rp, ci, v, B, C, map, M, K, N, h.d_err);
+    after_launch(h, "bcsr_spmm_f16_mma");
+}
+
+}  // namespace
+
+template <typename IT>
+static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, const IT* rp, const IT* ci,
+                               const __half* v, const __half* B, float* C, int64_t M, int64_t K,
+                               int64_t N, const IT* map) {
+    if (nbr == 0 || N == 0 || M == 0) return;
+    XS_REQUIRE(ceil_div(N, 64) <= 65535, XSPMM_STATUS_UNSUPPORTED, "N above 4,194,240 columns");
+    const bool aligned = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(v) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(C) % 8 == 0);
+    const int warps = N <= 64 ? 1 : (N <= 128 ? 2 : 4);
+    if (aligned) {
+        if (warps == 1) launch<IT, 1, true>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+        else if (warps == 2) launch<IT, 2, true>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+        else launch<IT, 4, true>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+    } else {
+        if (warps == 1) launch<IT, 1, false>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+        else if (warps == 2) launch<IT, 2, false>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+        else launch<IT, 4, false>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+    }
+}
+
+template <>
+void bcsr_spmm<__half, int32_t>(Handle& h, int64_t nbr, int64_t, int64_t, const int32_t* rp,
+                                const int32_t* ci, const __half* v, const __half* B, float* C,
+                                int64_t M, int64_t K, int64_t N, const int32_t* map) {
+    bcsr_spmm_f16_impl<int32_t>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+}
+template <>
+void bcsr_spmm<__half, int64_t>(Handle& h, int64_t nbr, int64_t, int64_t, const int64_t* rp,
+                                const int64_t* ci, const __half* v, const __half* B, float* C,
+                                int64_t M, int64_t K, int64_t N, const int64_t* map) {
+    bcsr_spmm_f16_impl<int64_t>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+}
+
+}  // namespace xspmm_b200
