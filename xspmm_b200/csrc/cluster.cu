@@ -27,18 +27,32 @@
 // Data: row patterns come from the CSR->BCSR kernels run with r_block = 1, c_block = w (sorted
 // distinct block columns per row). The inverted index maps a block column to its rows grouped by
 // pattern size in 32 classes (sizes 1..31 exact, 32 = "32 or more"), so a size window is a
-// contiguous slice. The greedy loop itself is inherently sequential across clusters and runs in
-// one persistent CTA of 1024 threads; all per-pass work (gather, evaluate, compaction, sorting,
+// contiguous slice.
+//
+// Gathering: a column of p whose inverted list is short ("light") is walked whole once, and
+// every eligible row on it gets one hit on a per-row counter, so |q n p| over light columns is a
+// counter read -- no dependent load of the candidate's pattern. Long lists ("heavy", the hub
+// columns of power-law matrices) are walked only when the light columns of p are fewer than
+// |p| - m + 1, and then only over the size window of (2); a candidate's hits in heavy columns are
+// looked up in its pattern. The greedy loop is inherently sequential across clusters and runs in
+// one persistent CTA of 256 threads; all per-pass work (gather, evaluate, compaction, sorting,
 // replay) is parallel inside it. Every loop is bounded by the data sizes; an internal consistency
 // failure sets an error flag and stops instead of spinning.
+
 #include "ops.cuh"
 
 namespace xspmm_b200 {
 namespace {
 
-constexpr int CL_THREADS = 1024;
-constexpr int NCLS = 32;          // size classes per block column
-constexpr int SORT_CAP = 2048;    // in-shared-memory sort capacity (uint64 keys)
+constexpr int CL_THREADS = 256;
+constexpr int NCLS = 32;            // size classes per block column in the inverted index
+constexpr int SORT_CAP = 1024;      // settled acceptances kept in shared memory (uint64 keys)
+constexpr int CAND_CAP = 1024;      // candidates kept in shared memory (the rest in global)
+constexpr int HOLE_CAP = 1024;      // holes of a pass kept in shared memory (the rest in global)
+constexpr int SMEM_ROWS = 20480;    // U and pos live in shared memory up to this many rows
+constexpr int64_t HEAVY = 2048;     // inverted lists longer than this are walked by size window
+constexpr int LIGHT_MASK = (1 << 30) - 1;
+constexpr int HEAVY_MARK = 1 << 30;
 
 struct ClusterArgs {
     int32_t M;
@@ -49,20 +63,20 @@ struct ClusterArgs {
     const int2* ient;       // inverted index entries (row, pattern size)
     int32_t* U;             // [M] unclustered rows by position
     int32_t* pos;           // [M] position of a row in U, -1 once clustered
-    int32_t* stamp;         // [M] pass in which a row was gathered
-    int32_t* cstamp;        // [nbc] pass in which a column joined the gathered set
+    int32_t* cnt;           // [M] light-column hits this pass (| HEAVY_MARK); 0 between passes
+    int32_t* cstamp;        // [nbc] pass in which a heavy column joined the window-gathered set
     int32_t* cslot;         // [nbc] next size class to gather for that column
     uint32_t* pbits;        // [ceil(nbc/32)] pattern of the current cluster
-    int32_t* plist;         // [nbc] columns of p
-    int32_t* glist;         // [nbc] gathered columns of this pass
-    int32_t* cand;          // [M] pending candidate rows
-    int32_t* cand2;         // [M] compaction buffer
-    uint8_t* cflag;         // [M] evaluation result per candidate slot
-    uint64_t* racc;         // [M] (pos << 32 | row) accepted in the current round
-    uint64_t* gsort;        // [M] global sort scratch (pow2-padded sizes up to 2M)
-    int32_t* holes;         // [M] accepted positions of this pass, decreasing
-    int32_t* hpass;         // [M] by position: pass in which it became a hole
-    int32_t* hrank;         // [M] by position: rank among the pass's holes
+    int32_t* plist;         // [nbc] columns of p, in insertion order
+    int32_t* hlist;         // [nbc] heavy columns of p
+    int32_t* glist;         // [nbc] window-gathered heavy columns of this pass
+    int32_t* crow;          // [2*M] candidates beyond the shared-memory part (two buffers)
+    int32_t* clen;          // [2*M]
+    int32_t* cpos;          // [2*M]
+    uint8_t* cflag;         // [M]
+    uint64_t* racc;         // [max(M,nbc)] scratch: settled keys / (cost << 32 | col)
+    uint64_t* gsort;        // [pow2 >= M] global sort scratch
+    int32_t* holes;         // [M] holes of a pass beyond the shared-memory part
     int32_t* perm;          // [M] output (int32 view)
     float tau;
     double t_lo;
@@ -89,17 +103,17 @@ __device__ __forceinline__ float jaccard_distance(int64_t inter, int64_t uni) {
     return __fsub_rn(1.0f, q);
 }
 
-// CTA-wide exclusive scan of one int per thread; returns the prefix, *total gets the sum.
+// CTA-wide exclusive scans of one value per thread (3 barriers).
 __device__ int cta_excl_scan(int v, int* s_warp, int* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int inc = warp_inclusive_sum(v);
     if (lane == 31) s_warp[warp] = inc;
     __syncthreads();
     if (warp == 0) {
-        const int w = s_warp[lane];
+        const int w = lane < CL_THREADS / 32 ? s_warp[lane] : 0;
         const int wi = warp_inclusive_sum(w);
-        s_warp[lane] = wi - w;
-        if (lane == 31) *total = wi;
+        if (lane < CL_THREADS / 32) s_warp[lane] = wi - w;
+        if (lane == CL_THREADS / 32 - 1) *total = wi;
     }
     __syncthreads();
     const int r = s_warp[warp] + inc - v;
@@ -107,17 +121,16 @@ __device__ int cta_excl_scan(int v, int* s_warp, int* total) {
     return r;
 }
 
-// CTA-wide exclusive scan of one int64 per thread.
 __device__ int64_t cta_excl_scan64(int64_t v, int64_t* s_warp, int64_t* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t inc = warp_inclusive_sum(v);
     if (lane == 31) s_warp[warp] = inc;
     __syncthreads();
     if (warp == 0) {
-        const int64_t w = s_warp[lane];
+        const int64_t w = lane < CL_THREADS / 32 ? s_warp[lane] : 0;
         const int64_t wi = warp_inclusive_sum(w);
-        s_warp[lane] = wi - w;
-        if (lane == 31) *total = wi;
+        if (lane < CL_THREADS / 32) s_warp[lane] = wi - w;
+        if (lane == CL_THREADS / 32 - 1) *total = wi;
     }
     __syncthreads();
     const int64_t r = s_warp[warp] + inc - v;
@@ -125,9 +138,8 @@ __device__ int64_t cta_excl_scan64(int64_t v, int64_t* s_warp, int64_t* total) {
     return r;
 }
 
-// Bitonic sort of n uint64 keys (ascending, or descending if desc) held in `a`, which may live in
-// shared or global memory; padded to a power of two with +inf/-inf sentinels by the caller's
-// capacity. cap must be a power of two >= n.
+// Bitonic sort of n uint64 keys in `a` (shared or global memory), ascending or descending,
+// padded up to cap (a power of two >= n) with sentinels.
 __device__ void cta_bitonic_sort(uint64_t* a, int n, int cap, bool desc) {
     const uint64_t pad = desc ? 0ull : ~0ull;
     for (int i = n + threadIdx.x; i < cap; i += CL_THREADS) a[i] = pad;
@@ -160,22 +172,128 @@ struct Shared {
     int total;
     int64_t s_warp64[32];
     int64_t total64;
-    int64_t col_beg[CL_THREADS];      // gather: first entry of each column's slice
-    int64_t col_off[CL_THREADS + 1];  // gather: exclusive offsets of the slices
-    int n, out, k, pass, seed;
-    int pcount, gcount, ncand, nracc, need;
+    int64_t col_beg[CL_THREADS];      // flattened walks of heavy windows
+    int64_t col_off[CL_THREADS + 1];
+    int n, out, k, pass, seed, stop;
+    int pcount, nproc, nheavy, hg, ncand, nkeep, nr, smax, limit, grown, need, cur;
     int64_t m, ub;
-    int limit;
-    int smax;
-    int grown;
-    int stop;
-    int new_cols;
+    int crow[2][CAND_CAP];            // pending candidates (double-buffered): row,
+    int clen[2][CAND_CAP];            //   pattern size,
+    int cpos[2][CAND_CAP];            //   position in U (fixed during the pass)
+    uint8_t cflag[CAND_CAP];
     uint64_t sortbuf[SORT_CAP];
+    int holes[HOLE_CAP];              // first HOLE_CAP holes of the pass
 };
 
+// Rows' positions and U live in shared memory when they fit (SU), else in global memory.
+template <bool SU>
+struct RowState {
+    int32_t* U;
+    int32_t* pos;
+    __device__ __forceinline__ int u(int i) const { return U[i]; }
+    __device__ __forceinline__ void set_u(int i, int v) const { U[i] = v; }
+    __device__ __forceinline__ int p(int r) const { return pos[r]; }
+    __device__ __forceinline__ void set_p(int r, int v) const { pos[r] = v; }
+};
+
+__device__ __forceinline__ void cand_get(const Shared& sh, const ClusterArgs& a, int buf, int c,
+                                         int& r, int& len, int& pr) {
+    if (c < CAND_CAP) {
+        r = sh.crow[buf][c];
+        len = sh.clen[buf][c];
+        pr = sh.cpos[buf][c];
+    } else {
+        const int64_t g = (int64_t)buf * a.M + c;
+        r = a.crow[g];
+        len = a.clen[g];
+        pr = a.cpos[g];
+    }
+}
+__device__ __forceinline__ void cand_set(Shared& sh, ClusterArgs& a, int buf, int c, int r,
+                                         int len, int pr) {
+    if (c < CAND_CAP) {
+        sh.crow[buf][c] = r;
+        sh.clen[buf][c] = len;
+        sh.cpos[buf][c] = pr;
+    } else {
+        const int64_t g = (int64_t)buf * a.M + c;
+        a.crow[g] = r;
+        a.clen[g] = len;
+        a.cpos[g] = pr;
+    }
+}
+__device__ __forceinline__ uint8_t flag_get(const Shared& sh, const ClusterArgs& a, int c) {
+    return c < CAND_CAP ? sh.cflag[c] : a.cflag[c];
+}
+__device__ __forceinline__ void flag_set(Shared& sh, ClusterArgs& a, int c, uint8_t f) {
+    if (c < CAND_CAP) sh.cflag[c] = f; else a.cflag[c] = f;
+}
+__device__ __forceinline__ int hole_get(const Shared& sh, const ClusterArgs& a, int t) {
+    return t < HOLE_CAP ? sh.holes[t] : a.holes[t];
+}
+__device__ __forceinline__ void hole_set(Shared& sh, ClusterArgs& a, int t, int v) {
+    if (t < HOLE_CAP) sh.holes[t] = v; else a.holes[t] = v;
+}
+
+__device__ __forceinline__ void append_candidate(Shared& sh, ClusterArgs& a, int r, int len,
+                                                 int pr) {
+    const int slot = atomicAdd(&sh.ncand, 1);
+    if (slot < a.M) cand_set(sh, a, sh.cur, slot, r, len, pr);
+    else flag_error(a.err, DERR_INTERNAL);
+}
+
+// Walks the entries of up to CL_THREADS inverted-list slices (one per thread) spread over the
+// whole CTA (used for the long lists of heavy columns).
+template <typename F>
+__device__ void flat_walk(Shared& sh, const int2* ient, int64_t e_beg, int64_t e_cnt, F&& f) {
+    const int tid = threadIdx.x;
+    const int64_t off = cta_excl_scan64(e_cnt, sh.s_warp64, &sh.total64);
+    sh.col_beg[tid] = e_beg;
+    sh.col_off[tid] = off;
+    if (tid == CL_THREADS - 1) sh.col_off[CL_THREADS] = off + e_cnt;
+    __syncthreads();
+    const int64_t total = sh.total64;
+    for (int64_t fi = tid; fi < total; fi += CL_THREADS) {
+        int lo = 0, hi = CL_THREADS - 1;  // last slice with col_off <= fi (a non-empty one)
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (sh.col_off[mid] <= fi) lo = mid; else hi = mid - 1;
+        }
+        f(ient[sh.col_beg[lo] + (fi - sh.col_off[lo])]);
+    }
+    __syncthreads();
+}
+
+// Does the sorted pattern [b, e) contain column x?
+__device__ __forceinline__ bool pattern_has(const int32_t* qcol, int64_t b, int64_t e, int x) {
+    while (b < e) {
+        const int64_t mid = b + ((e - b) >> 1);
+        const int v = qcol[mid];
+        if (v == x) return true;
+        if (v < x) b = mid + 1; else e = mid;
+    }
+    return false;
+}
+
+template <bool SU>
 __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
     __shared__ Shared sh;
-    const int tid = threadIdx.x;
+    extern __shared__ int32_t dyn[];
+    RowState<SU> st;
+    if constexpr (SU) {
+        st.U = dyn;
+        st.pos = dyn + a.M;
+    } else {
+        st.U = a.U;
+        st.pos = a.pos;
+    }
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if constexpr (SU) {
+        for (int i = tid; i < a.M; i += CL_THREADS) {
+            st.U[i] = i;
+            st.pos[i] = i;
+        }
+    }
     if (tid == 0) {
         sh.n = a.M;
         sh.out = 0;
@@ -186,14 +304,14 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
 
     while (sh.n > 0 && !sh.stop) {
         if (tid == 0) {
-            const int seed = a.U[sh.n - 1];
+            const int seed = st.u(sh.n - 1);
             if (seed < 0 || seed >= a.M || sh.out >= a.M) {
                 flag_error(a.err, DERR_INTERNAL);
                 sh.stop = 1;
             } else {
                 sh.seed = seed;
                 sh.n -= 1;
-                a.pos[seed] = -1;
+                st.set_p(seed, -1);
                 a.perm[sh.out++] = seed;
                 sh.k = 0;
             }
@@ -203,7 +321,8 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
         const int pass = sh.pass;
         const int seed = sh.seed;
         const int n = sh.n;
-        const int64_t slen = a.qptr[seed + 1] - a.qptr[seed];
+        const int64_t s0 = a.qptr[seed];
+        const int64_t slen = a.qptr[seed + 1] - s0;
 
         if (slen == 0) {
             // Empty pattern: accepts exactly the empty rows, in decreasing position order.
@@ -211,15 +330,15 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                 const int i = hi - 1 - tid;
                 int f = 0, r = -1;
                 if (i >= 0) {
-                    r = a.U[i];
+                    r = st.u(i);
                     f = (a.qptr[r + 1] == a.qptr[r]) ? 1 : 0;
                 }
                 const int idx = cta_excl_scan(f, sh.s_warp, &sh.total);
                 if (f) {
                     if (sh.out + idx < a.M && sh.k + idx < a.M) {
                         a.perm[sh.out + idx] = r;
-                        a.holes[sh.k + idx] = i;
-                        a.pos[r] = -1;
+                        hole_set(sh, a, sh.k + idx, i);
+                        st.set_p(r, -1);
                     } else {
                         flag_error(a.err, DERR_INTERNAL);
                     }
@@ -232,56 +351,76 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                 __syncthreads();
             }
         } else {
-            // p = q_seed
-            const int64_t s0 = a.qptr[seed];
-            for (int t = tid; t < slen; t += CL_THREADS) {
+            for (int t = tid; t < slen; t += CL_THREADS) {  // p = q_seed
                 const int b = a.qcol[s0 + t];
                 atomicOr(&a.pbits[b >> 5], 1u << (b & 31));
                 a.plist[t] = b;
             }
             if (tid == 0) {
                 sh.pcount = (int)slen;
-                sh.gcount = 0;
+                sh.nproc = 0;
+                sh.nheavy = 0;
+                sh.hg = 0;
                 sh.ncand = 0;
                 sh.limit = n;
                 sh.grown = 1;
+                sh.cur = 0;
+                sh.m = min_inter(a.t_lo, slen);
+                sh.ub = max_len(a.t_lo, slen);
+                sh.need = (int)(slen - sh.m + 1);
             }
             __syncthreads();
 
             for (int round = 0;; ++round) {
-                if (round > a.M + 1) {  // each round settles >= 1 candidate; cannot exceed M
+                if (round > a.M + 1) {  // each round settles >= 1 candidate
                     if (tid == 0) { flag_error(a.err, DERR_INTERNAL); sh.stop = 1; }
                     __syncthreads();
                     break;
                 }
                 if (sh.grown) {
-                    if (tid == 0) {
-                        sh.m = min_inter(a.t_lo, sh.pcount);
-                        sh.ub = max_len(a.t_lo, sh.pcount);
-                        sh.need = (int)(sh.pcount - sh.m + 1);
-                        sh.new_cols = 0;
+                    const int64_t m = sh.m, ub = sh.ub;
+                    const int limit = sh.limit;
+                    const int pc = sh.pcount;
+                    // (1) New columns of p. A light list is walked whole by one warp and every
+                    // eligible row on it gets one hit, so |q n p| over light columns is a
+                    // counter; heavy lists are set aside.
+                    for (int t = sh.nproc + warp; t < pc; t += CL_THREADS / 32) {
+                        const int b = a.plist[t];
+                        const int64_t lo = a.iptr[(int64_t)b * NCLS];
+                        const int64_t hi = a.iptr[(int64_t)(b + 1) * NCLS];
+                        if (hi - lo > HEAVY) {
+                            if (lane == 0) a.hlist[atomicAdd(&sh.nheavy, 1)] = b;
+                            continue;
+                        }
+                        for (int64_t e = lo + lane; e < hi; e += 32) {
+                            const int2 en = a.ient[e];
+                            const int pr = st.p(en.x);
+                            if (pr < 0 || pr >= limit) continue;
+                            if (atomicAdd(&a.cnt[en.x], 1) == 0)
+                                append_candidate(sh, a, en.x, en.y, pr);
+                        }
                     }
                     __syncthreads();
-                    const int64_t m = sh.m, ub = sh.ub;
+                    if (tid == 0) sh.nproc = pc;
+                    // (2) Heavy columns are needed only when the light ones are fewer than
+                    // |p| - m + 1; then take the cheapest ones over the size window [m, ub].
+                    const int nheavy = sh.nheavy;
+                    const int want = sh.need - (pc - nheavy) - sh.hg;
                     const int slo = slot_of(m), shi = slot_of(ub < NCLS ? ub : NCLS);
-                    // Columns to add: the cheapest ungathered columns of p.
-                    const int want = sh.need - sh.gcount;
                     if (want > 0) {
-                        // collect ungathered columns with their window cost
-                        if (tid == 0) sh.nracc = 0;
+                        if (tid == 0) sh.nr = 0;
                         __syncthreads();
-                        for (int t = tid; t < sh.pcount; t += CL_THREADS) {
-                            const int b = a.plist[t];
+                        for (int t = tid; t < nheavy; t += CL_THREADS) {
+                            const int b = a.hlist[t];
                             if (a.cstamp[b] != pass) {
                                 const int64_t c = a.iptr[(int64_t)b * NCLS + shi + 1] -
                                                   a.iptr[(int64_t)b * NCLS + slo];
                                 const uint64_t cost = c > 0xffffffffll ? 0xffffffffull : (uint64_t)c;
-                                const int slot = atomicAdd(&sh.nracc, 1);
-                                a.racc[slot] = (cost << 32) | (uint32_t)b;
+                                a.racc[atomicAdd(&sh.nr, 1)] = (cost << 32) | (uint32_t)b;
                             }
                         }
                         __syncthreads();
-                        const int nu = sh.nracc;
+                        const int nu = sh.nr;
                         int take = nu;
                         if (want < nu && nu <= SORT_CAP) {
                             for (int t = tid; t < nu; t += CL_THREADS) sh.sortbuf[t] = a.racc[t];
@@ -295,21 +434,17 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             const int b = (int)(uint32_t)a.racc[t];
                             a.cstamp[b] = pass;
                             a.cslot[b] = slo;
-                            a.glist[sh.gcount + t] = b;
+                            a.glist[sh.hg + t] = b;
                         }
                         __syncthreads();
-                        if (tid == 0) sh.gcount += take;
+                        if (tid == 0) sh.hg += take;
                         __syncthreads();
                     }
-                    // Gather every gathered column over its not-yet-gathered classes up to shi.
-                    // Work is flattened over (column, entry): a scan of the slice lengths of up
-                    // to CL_THREADS columns, then threads stride over the entries and find their
-                    // column by binary search, so one long column is spread over the CTA.
-                    const int limit = sh.limit;
-                    for (int c0 = 0; c0 < sh.gcount; c0 += CL_THREADS) {
+                    const int hg = sh.hg;
+                    for (int c0 = 0; c0 < hg; c0 += CL_THREADS) {
                         const int ci = c0 + tid;
                         int64_t e_beg = 0, e_cnt = 0;
-                        if (ci < sh.gcount) {
+                        if (ci < hg) {
                             const int b = a.glist[ci];
                             const int from = max(a.cslot[b], slo);
                             if (from <= shi) {
@@ -318,170 +453,181 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             }
                             if (a.cslot[b] < shi + 1) a.cslot[b] = shi + 1;
                         }
-                        const int64_t off = cta_excl_scan64(e_cnt, sh.s_warp64, &sh.total64);
-                        sh.col_beg[tid] = e_beg;
-                        sh.col_off[tid] = off;
-                        if (tid == CL_THREADS - 1) sh.col_off[CL_THREADS] = off + e_cnt;
-                        __syncthreads();
-                        const int64_t total = sh.total64;
-                        for (int64_t f = tid; f < total; f += CL_THREADS) {
-                            int lo = 0, hi = CL_THREADS - 1;  // last j with col_off[j] <= f
-                            while (lo < hi) {
-                                const int mid = (lo + hi + 1) >> 1;
-                                if (sh.col_off[mid] <= f) lo = mid; else hi = mid - 1;
-                            }
-                            const int2 en = a.ient[sh.col_beg[lo] + (f - sh.col_off[lo])];
-                            if ((int64_t)en.y < m) continue;
-                            const int r = en.x;
-                            const int pr = a.pos[r];
-                            if (pr < 0 || pr >= limit) continue;
-                            if (atomicExch(&a.stamp[r], pass) == pass) continue;
-                            const int slot = atomicAdd(&sh.ncand, 1);
-                            a.cand[slot] = r;
-                        }
-                        __syncthreads();
+                        flat_walk(sh, a.ient, e_beg, e_cnt, [&](int2 en) {
+                            if ((int64_t)en.y < m) return;
+                            const int pr = st.p(en.x);
+                            if (pr < 0 || pr >= limit) return;
+                            if (atomicOr(&a.cnt[en.x], HEAVY_MARK) == 0)
+                                append_candidate(sh, a, en.x, en.y, pr);
+                        });
                     }
-                    __syncthreads();
-                    if (tid == 0) sh.grown = 0;
+                    if (tid == 0) {
+                        sh.grown = 0;
+                        sh.smax = -1;
+                        sh.nr = 0;
+                        sh.nkeep = 0;
+                    }
                     __syncthreads();
                 }
                 const int ncand = sh.ncand;
                 if (ncand == 0) break;
+                const int buf = sh.cur;
 
                 // Evaluate every pending candidate against the current p.
-                if (tid == 0) sh.smax = -1;
-                __syncthreads();
                 const int pcount = sh.pcount;
+                const int nheavy = sh.nheavy;
                 for (int c = tid; c < ncand; c += CL_THREADS) {
-                    const int r = a.cand[c];
-                    const int64_t q0 = a.qptr[r], q1 = a.qptr[r + 1];
-                    int64_t inter = 0;
-                    for (int64_t j = q0; j < q1; ++j) {
-                        const int b = a.qcol[j];
-                        inter += (a.pbits[b >> 5] >> (b & 31)) & 1u;
+                    int r, len, pr;
+                    cand_get(sh, a, buf, c, r, len, pr);
+                    int64_t inter = a.cnt[r] & LIGHT_MASK;
+                    if (nheavy > 0) {
+                        const int64_t q0 = a.qptr[r], q1 = a.qptr[r + 1];
+                        if ((int64_t)nheavy * 4 >= len) {  // scan q against all of p
+                            inter = 0;
+                            for (int64_t j = q0; j < q1; ++j) {
+                                const int b = a.qcol[j];
+                                inter += (a.pbits[b >> 5] >> (b & 31)) & 1u;
+                            }
+                        } else {  // light hits are counted; look the heavy columns up in q
+                            for (int h = 0; h < nheavy; ++h)
+                                inter += pattern_has(a.qcol, q0, q1, a.hlist[h]) ? 1 : 0;
+                        }
                     }
-                    const int64_t len = q1 - q0;
-                    const int64_t uni = pcount + len - inter;
+                    const int64_t uni = pcount + (int64_t)len - inter;
                     const bool acc = jaccard_distance(inter, uni) <= a.tau;
                     const bool grow = acc && len > inter;
-                    a.cflag[c] = acc ? (grow ? 2 : 1) : 0;
-                    if (grow) atomicMax(&sh.smax, a.pos[r]);
+                    flag_set(sh, a, c, acc ? (grow ? 2 : 1) : 0);
+                    if (grow) atomicMax(&sh.smax, pr);
                 }
                 __syncthreads();
                 const int smax = sh.smax;
 
-                // Settle every candidate at or above smax; keep the rest pending.
-                if (tid == 0) sh.nracc = 0;
-                __syncthreads();
-                int keep_total = 0;
-                for (int c0 = 0; c0 < ncand; c0 += CL_THREADS) {
-                    const int c = c0 + tid;
-                    int keep = 0;
-                    int r = -1, pr = -1;
-                    uint8_t f = 0;
-                    if (c < ncand) {
-                        r = a.cand[c];
-                        pr = a.pos[r];
-                        f = a.cflag[c];
-                        if (pr < smax) keep = 1;
-                        else if (f) {
-                            const int slot = atomicAdd(&sh.nracc, 1);
-                            a.racc[slot] = ((uint64_t)(uint32_t)pr << 32) | (uint32_t)r;
+                // Settle every candidate at or above smax (its counter is cleared: it can never
+                // be gathered again in this pass); keep the rest, in any order, in the other
+                // buffer. Settled acceptances are collected with their positions.
+                for (int c = tid; c < ncand; c += CL_THREADS) {
+                    int r, len, pr;
+                    cand_get(sh, a, buf, c, r, len, pr);
+                    if (pr < smax) {
+                        cand_set(sh, a, buf ^ 1, atomicAdd(&sh.nkeep, 1), r, len, pr);
+                    } else {
+                        a.cnt[r] = 0;
+                        if (flag_get(sh, a, c)) {
+                            const int slot = atomicAdd(&sh.nr, 1);
+                            const uint64_t kv = ((uint64_t)(uint32_t)pr << 32) | (uint32_t)r;
+                            if (slot < SORT_CAP) sh.sortbuf[slot] = kv; else a.racc[slot] = kv;
                         }
                     }
-                    const int idx = cta_excl_scan(keep, sh.s_warp, &sh.total);
-                    if (keep) a.cand2[keep_total + idx] = r;
-                    keep_total += sh.total;
-                    __syncthreads();
                 }
-                for (int c = tid; c < keep_total; c += CL_THREADS) a.cand[c] = a.cand2[c];
                 __syncthreads();
-                const int nr = sh.nracc;
-                // order the settled accepted rows by decreasing position
-                if (nr > 1) {
-                    if (nr <= SORT_CAP) {
-                        for (int t = tid; t < nr; t += CL_THREADS) sh.sortbuf[t] = a.racc[t];
-                        __syncthreads();
-                        cta_bitonic_sort(sh.sortbuf, nr, pow2_at_least(nr), true);
-                        for (int t = tid; t < nr; t += CL_THREADS) a.racc[t] = sh.sortbuf[t];
-                    } else {
-                        for (int t = tid; t < nr; t += CL_THREADS) a.gsort[t] = a.racc[t];
-                        __syncthreads();
-                        cta_bitonic_sort(a.gsort, nr, pow2_at_least(nr), true);
-                        for (int t = tid; t < nr; t += CL_THREADS) a.racc[t] = a.gsort[t];
+                const int nr = sh.nr;
+                // Append the settled acceptances in decreasing position order.
+                if (nr <= CL_THREADS) {  // rank by counting
+                    if (tid < nr) {
+                        const uint64_t kv = sh.sortbuf[tid];
+                        int rank = 0;
+                        for (int j = 0; j < nr; ++j) rank += sh.sortbuf[j] > kv;
+                        const int r = (int)(uint32_t)kv, pr = (int)(kv >> 32);
+                        if (sh.out + rank < a.M && sh.k + rank < a.M) {
+                            a.perm[sh.out + rank] = r;
+                            hole_set(sh, a, sh.k + rank, pr);
+                            st.set_p(r, -1);
+                        } else {
+                            flag_error(a.err, DERR_INTERNAL);
+                        }
                     }
+                } else {
+                    uint64_t* keys = a.gsort;
+                    for (int t = tid; t < nr; t += CL_THREADS)
+                        keys[t] = t < SORT_CAP ? sh.sortbuf[t] : a.racc[t];
                     __syncthreads();
-                }
-                for (int t = tid; t < nr; t += CL_THREADS) {
-                    const uint64_t kv = a.racc[t];
-                    const int r = (int)(uint32_t)kv, pr = (int)(kv >> 32);
-                    if (sh.out + t < a.M && sh.k + t < a.M) {
-                        a.perm[sh.out + t] = r;
-                        a.holes[sh.k + t] = pr;
-                        a.pos[r] = -1;
-                    } else {
-                        flag_error(a.err, DERR_INTERNAL);
+                    cta_bitonic_sort(keys, nr, pow2_at_least(nr), true);
+                    for (int t = tid; t < nr; t += CL_THREADS) {
+                        const uint64_t kv = keys[t];
+                        const int r = (int)(uint32_t)kv, pr = (int)(kv >> 32);
+                        if (sh.out + t < a.M && sh.k + t < a.M) {
+                            a.perm[sh.out + t] = r;
+                            hole_set(sh, a, sh.k + t, pr);
+                            st.set_p(r, -1);
+                        } else {
+                            flag_error(a.err, DERR_INTERNAL);
+                        }
                     }
                 }
                 __syncthreads();
                 if (tid == 0) {
                     sh.out += nr;
                     sh.k += nr;
-                    sh.ncand = keep_total;
+                    sh.ncand = sh.nkeep;
+                    sh.cur = buf ^ 1;
+                    sh.smax = -1;
+                    sh.nr = 0;
+                    sh.nkeep = 0;
                 }
-                __syncthreads();
-                if (smax < 0) break;  // nothing grew p: every candidate is settled
-
+                if (smax < 0) {  // nothing grew p: every candidate is settled
+                    __syncthreads();
+                    break;
+                }
                 // The candidate at smax was accepted and adds columns: grow p.
-                const int grow_row = a.U[smax];
+                const int grow_row = st.u(smax);
                 const int64_t g0 = a.qptr[grow_row], g1 = a.qptr[grow_row + 1];
                 for (int64_t j = g0 + tid; j < g1; j += CL_THREADS) {
                     const int b = a.qcol[j];
                     const uint32_t bit = 1u << (b & 31);
-                    if (!(atomicOr(&a.pbits[b >> 5], bit) & bit)) {
-                        const int slot = atomicAdd(&sh.pcount, 1);
-                        a.plist[slot] = b;
-                    }
+                    if (!(atomicOr(&a.pbits[b >> 5], bit) & bit)) a.plist[atomicAdd(&sh.pcount, 1)] = b;
                 }
                 __syncthreads();
                 if (tid == 0) {
                     sh.limit = smax;
                     sh.grown = 1;
+                    sh.m = min_inter(a.t_lo, sh.pcount);
+                    sh.ub = max_len(a.t_lo, sh.pcount);
+                    sh.need = (int)(sh.pcount - sh.m + 1);
                 }
                 __syncthreads();
             }
-            // clear p
-            for (int t = tid; t < sh.pcount; t += CL_THREADS) {
-                const int b = a.plist[t];
-                a.pbits[b >> 5] = 0u;
-            }
-            __syncthreads();
+            for (int t = tid; t < sh.pcount; t += CL_THREADS) a.pbits[a.plist[t] >> 5] = 0u;
         }
 
-        // Replay the pass's removals (fact 4).
-        const int k = sh.k;
-        for (int t = tid; t < k; t += CL_THREADS) {
-            const int h = a.holes[t];
-            a.hpass[h] = pass;
-            a.hrank[h] = t;
-        }
+        // Replay the pass's removals (U[h] = U.back(); pop, h decreasing): for a hole h_t below
+        // n-k the element that lands there is U[chase(n-1-t)], chase(x) = x unless x is itself a
+        // hole h_j, then chase(n-1-j). Only holes >= n-k can be chased into; they are a prefix of
+        // the decreasing holes list, searched by bisection.
         __syncthreads();
-        for (int t = tid; t < k; t += CL_THREADS) {
-            const int h = a.holes[t];
-            if (h >= n - k) continue;
+        const int k = sh.k;
+        int ktop;
+        {
+            int lo = 0, hi = k;  // first index with holes[idx] < n-k
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (hole_get(sh, a, mid) >= n - k) lo = mid + 1; else hi = mid;
+            }
+            ktop = lo;
+        }
+        for (int t = ktop + tid; t < k; t += CL_THREADS) {
+            const int h = hole_get(sh, a, t);
             int x = n - 1 - t;
             int steps = 0;
-            while (x < n && a.hpass[x] == pass && steps <= k) {
-                x = n - 1 - a.hrank[x];
-                ++steps;
+            for (;;) {
+                int lo = 0, hi = ktop;  // find x in holes[0, ktop) (decreasing)
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if (hole_get(sh, a, mid) > x) lo = mid + 1; else hi = mid;
+                }
+                if (lo < ktop && hole_get(sh, a, lo) == x && steps <= k) {
+                    x = n - 1 - lo;
+                    ++steps;
+                } else {
+                    break;
+                }
             }
             if (steps > k || x >= n) {
                 flag_error(a.err, DERR_INTERNAL);
                 continue;
             }
-            const int r = a.U[x];
-            a.U[h] = r;
-            a.pos[r] = h;
+            const int r = st.u(x);
+            st.set_u(h, r);
+            st.set_p(r, h);
         }
         __syncthreads();
         if (tid == 0) {
@@ -491,18 +637,22 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
         }
         __syncthreads();
     }
+    if constexpr (SU) {  // leave U/pos in global memory consistent for debugging
+        for (int i = tid; i < a.M; i += CL_THREADS) {
+            a.U[i] = st.U[i];
+            a.pos[i] = st.pos[i];
+        }
+    }
 }
 
 // --- preprocessing kernels -----------------------------------------------------------------------
 
-__global__ void init_rows_kernel(int32_t* U, int32_t* pos, int32_t* stamp, int32_t* hpass,
-                                 int32_t M) {
+__global__ void init_rows_kernel(int32_t* U, int32_t* pos, int32_t* cnt, int32_t M) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M;
          i += (int64_t)gridDim.x * blockDim.x) {
         U[i] = (int32_t)i;
         pos[i] = (int32_t)i;
-        stamp[i] = -1;
-        hpass[i] = -1;
+        cnt[i] = 0;
     }
 }
 
@@ -615,7 +765,8 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     qcol_it.release();
 
     // Inverted index by (block column, size class).
-    const int64_t nslots = std::max<int64_t>(nbc, 1) * NCLS;
+    const int64_t nb = std::max<int64_t>(nbc, 1);
+    const int64_t nslots = nb * NCLS;
     DevBuf<int64_t> iptr(nslots + 1, s);
     DevBuf<int64_t> cursor(nslots + 1, s);
     DevBuf<int2> ient(std::max<int64_t>(npat, 1), s);
@@ -632,16 +783,15 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     cursor.release();
 
     // State of the greedy loop.
-    const int64_t nb = std::max<int64_t>(nbc, 1);
     int sort_cap = 1;
     while (sort_cap < M) sort_cap <<= 1;
-    DevBuf<int32_t> U(M, s), pos(M, s), stamp(M, s), cstamp(nb, s), cslot(nb, s), plist(nb, s),
-        glist(nb, s), cand(M, s), cand2(M, s), holes(M, s), hpass(M, s), hrank(M, s), perm32(M, s);
+    DevBuf<int32_t> U(M, s), pos(M, s), cnt(M, s), cstamp(nb, s), cslot(nb, s), plist(nb, s),
+        hlist(nb, s), glist(nb, s), crow(2 * M, s), clen(2 * M, s), cpos(2 * M, s), holes(M, s),
+        perm32(M, s);
     DevBuf<uint32_t> pbits(ceil_div(nb, 32), s);
     DevBuf<uint8_t> cflag(M, s);
     DevBuf<uint64_t> racc(std::max<int64_t>(M, nb), s), gsort(sort_cap, s);
-    init_rows_kernel<<<grid_1d(h, M, 256), 256, 0, s>>>(U.get(), pos.get(), stamp.get(),
-                                                         hpass.get(), (int32_t)M);
+    init_rows_kernel<<<grid_1d(h, M, 256), 256, 0, s>>>(U.get(), pos.get(), cnt.get(), (int32_t)M);
     after_launch(h, "cluster_init_rows");
     init_cols_kernel<<<grid_1d(h, nb, 256), 256, 0, s>>>(cstamp.get(), pbits.get(), (int32_t)nb);
     after_launch(h, "cluster_init_cols");
@@ -655,25 +805,32 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     a.ient = ient.get();
     a.U = U.get();
     a.pos = pos.get();
-    a.stamp = stamp.get();
+    a.cnt = cnt.get();
     a.cstamp = cstamp.get();
     a.cslot = cslot.get();
     a.pbits = pbits.get();
     a.plist = plist.get();
+    a.hlist = hlist.get();
     a.glist = glist.get();
-    a.cand = cand.get();
-    a.cand2 = cand2.get();
+    a.crow = crow.get();
+    a.clen = clen.get();
+    a.cpos = cpos.get();
     a.cflag = cflag.get();
     a.racc = racc.get();
     a.gsort = gsort.get();
     a.holes = holes.get();
-    a.hpass = hpass.get();
-    a.hrank = hrank.get();
     a.perm = perm32.get();
     a.tau = tau;
     a.t_lo = (1.0 - (double)tau) - 1.0 / (double)(1 << 22);
     a.err = h.d_err;
-    cluster_kernel<<<1, CL_THREADS, 0, s>>>(a);
+    if (M <= SMEM_ROWS) {
+        const size_t dyn = (size_t)M * 2 * sizeof(int32_t);
+        XS_CHECK_CUDA(cudaFuncSetAttribute(cluster_kernel<true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
+        cluster_kernel<true><<<1, CL_THREADS, dyn, s>>>(a);
+    } else {
+        cluster_kernel<false><<<1, CL_THREADS, 0, s>>>(a);
+    }
     after_launch(h, "cluster_greedy");
     store_perm_kernel<IT><<<grid_1d(h, M, 256), 256, 0, s>>>(perm32.get(), perm, M);
     after_launch(h, "cluster_store_perm");
