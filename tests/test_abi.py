@@ -53,7 +53,7 @@ def test_create_reports_a_status_instead_of_crashing():
 
 def test_cpp_api_header_compiles_against_the_abi():
     """include/xspmm/xspmm.hpp (the reference-shaped C++ API) compiles with the host compiler."""
-    src = os.path.join(ROOT, "tests", "cpp", "api_compile_check.cpp")
+    src = os.path.join(ROOT, "tests", "cpp", "pipeline_example.cpp")
     if not os.path.exists(src):
         pytest.skip("no C++ compile check source")
     cuda_inc = "/usr/local/cuda/include"
