@@ -141,6 +141,23 @@ xspmm_status_t xspmm_permute_rows_f32_i64(xspmm_handle_t h, int64_t M, int64_t K
     int64_t* out_row_ptr, int64_t* out_col_ind, void* out_values);
 
 /* ---------------------------------------------------------------------------------------------
+ * CSR row permutation that allocates no device memory. This entry point has no counterpart in the
+ * reference. It is for callers that cannot allocate device memory while they run -- for example a
+ * serving process whose device memory is fully reserved by its own pool, or code that must not
+ * take the device-wide synchronization cudaMalloc/cudaFree can cause. Result, validation and
+ * synchronization are those of xspmm_permute_rows_{f16,f32}_i32; value_bytes is 2 (fp16) or 4
+ * (fp32), indices are int32.
+ * Its scratch is a fixed 270,336-byte array compiled into the library (every GPU that loads the
+ * library holds it until exit), so M is limited to 2,097,152 rows; larger M returns
+ * INVALID_ARGUMENT. The first call on a device looks up the array's device address, so make that
+ * first call before any stream capture. All calls on a device share the array: calls that overlap
+ * on the GPU race and must be serialized by the caller.
+ * ------------------------------------------------------------------------------------------- */
+xspmm_status_t xspmm_permute_rows_noalloc_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t value_bytes,
+    const int32_t* perm, int32_t* out_row_ptr, int32_t* out_col_ind, void* out_values);
+
+/* ---------------------------------------------------------------------------------------------
  * CSR -> BCSR on the device, in two calls so the caller can allocate the outputs (the reference
  * builds on the host, src/core/conversion.cpp:8-100, and returns a BCSRMatrix:
  * include/xspmm/matrix/conversion.hpp:19-22).

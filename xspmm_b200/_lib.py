@@ -86,6 +86,8 @@ def lib():
             getattr(L, f"xspmm_permute_rows_{v}_{suf}").argtypes = s["permute"]
             getattr(L, f"xspmm_csr_to_bcsr_fill_{v}_{suf}").argtypes = s["fill"]
             getattr(L, f"xspmm_unpermute_dense_{v}_{suf}").argtypes = s["unpermute"]
+    L.xspmm_permute_rows_noalloc_i32.argtypes = [_P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P,
+                                                  _P, _P]
     _lib = L
     return L
 

@@ -5,49 +5,11 @@
 
 #include <new>
 
-#define XS_API extern "C" __attribute__((visibility("default")))
-
-struct xspmm_handle_s {
-    xspmm_b200::Handle h;
-    bool destroyed = false;
-};
-
 namespace xspmm_b200 {
 const char* last_error_cstr();
 }
 
 using namespace xspmm_b200;
-
-namespace {
-
-template <typename F>
-xspmm_status_t guarded(F&& f) {
-    try {
-        f();
-        return XSPMM_STATUS_OK;
-    } catch (const Error& e) {
-        set_last_error(e.what());
-        return e.status;
-    } catch (const std::bad_alloc&) {
-        set_last_error("host allocation failed");
-        return XSPMM_STATUS_OUT_OF_MEMORY;
-    } catch (const std::exception& e) {
-        set_last_error(e.what());
-        return XSPMM_STATUS_INTERNAL;
-    } catch (...) {
-        set_last_error("unknown exception");
-        return XSPMM_STATUS_INTERNAL;
-    }
-}
-
-Handle& H(xspmm_handle_t h) {
-    XS_REQUIRE(h != nullptr && !h->destroyed, XSPMM_STATUS_INVALID_ARGUMENT, "null handle");
-    return h->h;
-}
-
-void need(bool ok, const char* what) { XS_REQUIRE(ok, XSPMM_STATUS_INVALID_ARGUMENT, what); }
-
-}  // namespace
 
 XS_API const char* xspmm_status_string(xspmm_status_t s) {
     switch (s) {

@@ -130,6 +130,40 @@ void exclusive_scan(Handle& h, const T* in, T* out, int64_t n) {
     after_launch(h, "scan_down");
 }
 
+int64_t scan_scratch_elems(int64_t n) {
+    int64_t total = 0;
+    while (n > SCAN_TILE) {
+        const int64_t tiles = ceil_div(n, SCAN_TILE);
+        total += tiles + 1;
+        n = tiles;
+    }
+    return total;
+}
+
+template <typename T>
+void exclusive_scan_scratch(Handle& h, const T* in, T* out, int64_t n, T* scratch,
+                            int64_t scratch_elems) {
+    if (n <= 0) {
+        XS_CHECK_CUDA(cudaMemsetAsync(out, 0, sizeof(T), h.stream));
+        return;
+    }
+    const int64_t tiles = ceil_div(n, SCAN_TILE);
+    if (tiles == 1) {
+        scan_down_kernel<T><<<1, SCAN_THREADS, 0, h.stream>>>(in, out, n, nullptr);
+        after_launch(h, "scan_down");
+        return;
+    }
+    XS_REQUIRE(scratch_elems >= tiles + 1, XSPMM_STATUS_INVALID_ARGUMENT,
+               "scan scratch too small");
+    T* part = scratch;
+    scan_reduce_kernel<T><<<(unsigned)tiles, SCAN_THREADS, 0, h.stream>>>(in, n, part);
+    after_launch(h, "scan_reduce");
+    exclusive_scan_scratch<T>(h, part, part, tiles, scratch + tiles + 1,
+                              scratch_elems - (tiles + 1));
+    scan_down_kernel<T><<<(unsigned)tiles, SCAN_THREADS, 0, h.stream>>>(in, out, n, part);
+    after_launch(h, "scan_down");
+}
+
 template <typename T>
 T read_scalar(Handle& h, const T* dptr) {
     T v{};
@@ -140,6 +174,10 @@ T read_scalar(Handle& h, const T* dptr) {
 
 template void exclusive_scan<int32_t>(Handle&, const int32_t*, int32_t*, int64_t);
 template void exclusive_scan<int64_t>(Handle&, const int64_t*, int64_t*, int64_t);
+template void exclusive_scan_scratch<int32_t>(Handle&, const int32_t*, int32_t*, int64_t,
+                                              int32_t*, int64_t);
+template void exclusive_scan_scratch<int64_t>(Handle&, const int64_t*, int64_t*, int64_t,
+                                              int64_t*, int64_t);
 template int32_t read_scalar<int32_t>(Handle&, const int32_t*);
 template int64_t read_scalar<int64_t>(Handle&, const int64_t*);
 

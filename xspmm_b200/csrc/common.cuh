@@ -128,6 +128,13 @@ struct DevBuf {
 template <typename T>
 void exclusive_scan(Handle& h, const T* in, T* out, int64_t n);
 
+// Same scan with caller-provided scratch for the tile partials (no allocation). Needs
+// scan_scratch_elems(n) elements; throws INVALID_ARGUMENT if scratch_elems is smaller.
+int64_t scan_scratch_elems(int64_t n);
+template <typename T>
+void exclusive_scan_scratch(Handle& h, const T* in, T* out, int64_t n, T* scratch,
+                            int64_t scratch_elems);
+
 // Copies the last element of an exclusive scan (the total) to the host.
 template <typename T>
 T read_scalar(Handle& h, const T* dptr);

@@ -5,6 +5,8 @@
 
 #include "common.cuh"
 
+#include <new>
+
 namespace xspmm_b200 {
 
 // Tier-1 BCSR SpMM (16x16 blocks). VT = __half or float; C is fp32. row_map may be null.
@@ -23,6 +25,14 @@ template <typename VT, typename IT>
 void permute_rows(Handle& h, int64_t M, int64_t nnz, const IT* row_ptr, const IT* col_ind,
                   const VT* values, const IT* perm, IT* out_row_ptr, IT* out_col_ind,
                   VT* out_values, bool check);
+
+// permute_rows with caller-provided scratch instead of allocations: seen = ceil(M/32) words
+// (cleared here), scan scratch of scan_scratch_elems(M) elements. Validates and synchronizes.
+template <typename VT, typename IT>
+void permute_rows_scratch(Handle& h, int64_t M, int64_t nnz, const IT* row_ptr, const IT* col_ind,
+                          const VT* values, const IT* perm, IT* out_row_ptr, IT* out_col_ind,
+                          VT* out_values, unsigned* seen, IT* scan_scratch,
+                          int64_t scan_scratch_elems);
 
 // CSR -> BCSR: count (writes brp[nbr+1], returns nnzb, synchronizes) and fill.
 template <typename IT>
@@ -43,5 +53,49 @@ template <typename VT, typename IT>
 void spmm_csr_pipeline(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
                        const IT* col_ind, const VT* values, const VT* B, float* C, int64_t N,
                        int64_t hw, bool clustering, xspmm_timings_t* timings);
+
+}  // namespace xspmm_b200
+
+// ------------------------------------------------------------------------------------------------
+// Pieces shared by the files that define extern "C" entry points.
+// ------------------------------------------------------------------------------------------------
+#define XS_API extern "C" __attribute__((visibility("default")))
+
+struct xspmm_handle_s {
+    xspmm_b200::Handle h;
+    bool destroyed = false;
+};
+
+namespace xspmm_b200 {
+
+// Runs f, turning exceptions into a status code and the calling thread's last-error message.
+template <typename F>
+xspmm_status_t guarded(F&& f) {
+    try {
+        f();
+        return XSPMM_STATUS_OK;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return e.status;
+    } catch (const std::bad_alloc&) {
+        set_last_error("host allocation failed");
+        return XSPMM_STATUS_OUT_OF_MEMORY;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return XSPMM_STATUS_INTERNAL;
+    } catch (...) {
+        set_last_error("unknown exception");
+        return XSPMM_STATUS_INTERNAL;
+    }
+}
+
+inline Handle& H(xspmm_handle_t h) {
+    XS_REQUIRE(h != nullptr && !h->destroyed, XSPMM_STATUS_INVALID_ARGUMENT, "null handle");
+    return h->h;
+}
+
+inline void need(bool ok, const char* what) {
+    XS_REQUIRE(ok, XSPMM_STATUS_INVALID_ARGUMENT, what);
+}
 
 }  // namespace xspmm_b200

@@ -108,6 +108,26 @@ void permute_rows(Handle& h, int64_t M, int64_t nnz, const IT* row_ptr, const IT
 }
 
 template <typename VT, typename IT>
+void permute_rows_scratch(Handle& h, int64_t M, int64_t nnz, const IT* row_ptr, const IT* col_ind,
+                          const VT* values, const IT* perm, IT* out_row_ptr, IT* out_col_ind,
+                          VT* out_values, unsigned* seen, IT* scan_scratch,
+                          int64_t scan_scratch_elems) {
+    if (M == 0) {
+        XS_CHECK_CUDA(cudaMemsetAsync(out_row_ptr, 0, sizeof(IT), h.stream));
+        return;
+    }
+    XS_CHECK_CUDA(cudaMemsetAsync(seen, 0, (size_t)ceil_div(M, 32) * sizeof(unsigned), h.stream));
+    permute_lengths_kernel<IT><<<grid_for(h, M, 256), 256, 0, h.stream>>>(
+        row_ptr, perm, out_row_ptr, M, seen, h.d_err);
+    after_launch(h, "permute_lengths");
+    exclusive_scan_scratch<IT>(h, out_row_ptr, out_row_ptr, M, scan_scratch, scan_scratch_elems);
+    permute_copy_kernel<VT, IT><<<grid_for(h, M * 32, 256), 256, 0, h.stream>>>(
+        row_ptr, col_ind, values, perm, out_row_ptr, out_col_ind, out_values, M, nnz, h.d_err);
+    after_launch(h, "permute_copy");
+    throw_on_device_errors(h, "apply_permutation");
+}
+
+template <typename VT, typename IT>
 void unpermute_dense(Handle& h, const VT* in, VT* out, const IT* perm, int64_t M, int64_t N,
                      bool check) {
     if (M == 0 || N == 0) return;
@@ -128,6 +148,14 @@ void unpermute_dense(Handle& h, const VT* in, VT* out, const IT* perm, int64_t M
                                        const IT*, IT*, IT*, VT*, bool);                           \
     template void unpermute_dense<VT, IT>(Handle&, const VT*, VT*, const IT*, int64_t, int64_t,   \
                                           bool);
+template void permute_rows_scratch<__half, int32_t>(Handle&, int64_t, int64_t, const int32_t*,
+                                                    const int32_t*, const __half*, const int32_t*,
+                                                    int32_t*, int32_t*, __half*, unsigned*,
+                                                    int32_t*, int64_t);
+template void permute_rows_scratch<float, int32_t>(Handle&, int64_t, int64_t, const int32_t*,
+                                                   const int32_t*, const float*, const int32_t*,
+                                                   int32_t*, int32_t*, float*, unsigned*, int32_t*,
+                                                   int64_t);
 XS_INST_PERM(__half, int32_t)
 XS_INST_PERM(__half, int64_t)
 XS_INST_PERM(float, int32_t)
