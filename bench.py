@@ -463,6 +463,50 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_tier1_compare(args):
+    """mma.sync vs tcgen05 Tier-1 kernels on the pruned-LLM config (
+    4096 x 11008, every 16x16 block present) over the N sweep; one JSON line per (N, kernel)."""
+    import torch
+
+    import xspmm_b200 as xs
+    from xspmm_b200 import synth
+
+    P = synth.cfg3_pruned_llm(N=16)
+    ex = xs.CudaExecutor(0)
+    A = xs.CSRMatrix.from_host(ex, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int32)
+    Ab = xs.csr_to_bcsr(ex, A, 16, 16)
+    pk = peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    for N in [int(x) for x in args.compare_n.split(",")]:
+        B = torch.randn((P.K, N), device="cuda").half()
+        C = torch.empty((P.M, N), dtype=torch.float32, device="cuda")
+        for kind in args.compare_kernels.split(","):
+            ex.set_tier1_kernel(kind)
+            for _ in range(args.warmup):
+                xs.api._tier1(Ab, B, C, N)
+            torch.cuda.synchronize()
+            ts = []
+            for i in range(args.steps):
+                flush.fill_(float(i))
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                xs.api._tier1(Ab, B, C, N)
+                s1.record()
+                torch.cuda.synchronize()
+                ts.append(s0.elapsed_time(s1))
+            ms = sorted(ts)[len(ts) // 2]
+            padded = 2.0 * Ab.num_blocks * 256 * N / (ms * 1e-3) / 1e12
+            print(json.dumps({
+                "workload": "cfg3_pruned_llm", "N": N, "kernel": kind, "ms": round(ms, 4),
+                "effective_tflops": round(2.0 * P.nnz * N / (ms * 1e-3) / 1e12, 2),
+                "padded_tflops": round(padded, 2),
+                "padded_frac_of_bf16_peak": round(padded / pk["bf16_tflops"], 4),
+                "peak_source": pk["source"], "nnzb": Ab.num_blocks, "steps": args.steps,
+                "l2": "flushed before every launch"}), flush=True)
+        ex.set_tier1_kernel("auto")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -472,7 +516,14 @@ def main():
     ap.add_argument("--n-cols", type=int, default=256)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tier1-compare", action="store_true",
+                    help="mma.sync vs tcgen05 Tier-1 on the pruned-LLM config, N sweep")
+    ap.add_argument("--compare-n", default="16,64,256,1024,4096")
+    ap.add_argument("--compare-kernels", default="mma,tc")
     args = ap.parse_args()
+    if args.tier1_compare:
+        run_tier1_compare(args)
+        return
     if args.warmup < 3 and args.impl == "xspmm":
         args.warmup = 3
     if args.impl == "reference":

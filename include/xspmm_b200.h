@@ -62,6 +62,12 @@ xspmm_status_t xspmm_get_device(xspmm_handle_t h, int* device);
 /* Number of kernels this library has launched on the handle since creation (or the last reset). */
 xspmm_status_t xspmm_get_launch_count(xspmm_handle_t h, uint64_t* count);
 xspmm_status_t xspmm_reset_launch_count(xspmm_handle_t h);
+/* Selects the fp16 Tier-1 kernel for this handle: 0 = automatic (tcgen05 for dense block
+ * structure, mma.sync otherwise), 1 = warp-level mma.sync m16n8k16, 2 = tcgen05/TMEM with 8 block
+ * rows stacked per MMA (falls back to mma.sync when N % 8 != 0 or pointers are not 16-byte
+ * aligned). The reference has a single WMMA kernel; this choice exists for the comparison of the
+ * two tensor-core paths. Results agree within the SpMM tolerance either way. */
+xspmm_status_t xspmm_set_tier1_kernel(xspmm_handle_t h, int kind);
 const char* xspmm_status_string(xspmm_status_t s);
 const char* xspmm_last_error(void);
 /* Device memory through the handle: replaces Executor::allocate/free/copy_*

@@ -66,6 +66,7 @@ def lib():
     L.xspmm_get_device.argtypes = [_P, ctypes.POINTER(ctypes.c_int)]
     L.xspmm_get_launch_count.argtypes = [_P, ctypes.POINTER(ctypes.c_uint64)]
     L.xspmm_reset_launch_count.argtypes = [_P]
+    L.xspmm_set_tier1_kernel.argtypes = [_P, ctypes.c_int]
     L.xspmm_status_string.argtypes = [ctypes.c_int]
     L.xspmm_status_string.restype = ctypes.c_char_p
     L.xspmm_last_error.argtypes = []

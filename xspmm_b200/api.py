@@ -86,6 +86,10 @@ class CudaExecutor:
     def reset_launch_count(self) -> None:
         check(lib().xspmm_reset_launch_count(self._h))
 
+    def set_tier1_kernel(self, kind: str) -> None:
+        """'auto', 'mma' (mma.sync m16n8k16) or 'tc' (tcgen05/TMEM) for the fp16 Tier-1 SpMM."""
+        check(lib().xspmm_set_tier1_kernel(self._h, {"auto": 0, "mma": 1, "tc": 2}[kind]))
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h and _lib._lib is not None:

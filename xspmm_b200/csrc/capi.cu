@@ -96,6 +96,13 @@ XS_API xspmm_status_t xspmm_reset_launch_count(xspmm_handle_t hh) {
     return guarded([&] { H(hh).launches = 0; });
 }
 
+XS_API xspmm_status_t xspmm_set_tier1_kernel(xspmm_handle_t hh, int kind) {
+    return guarded([&] {
+        need(kind >= 0 && kind <= 2, "kind must be 0 (auto), 1 (mma.sync) or 2 (tcgen05)");
+        H(hh).tier1_kernel = kind;
+    });
+}
+
 XS_API xspmm_status_t xspmm_malloc(xspmm_handle_t hh, void** ptr, size_t bytes) {
     return guarded([&] {
         Handle& h = H(hh);

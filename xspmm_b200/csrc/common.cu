@@ -29,8 +29,10 @@ void throw_on_device_errors(Handle& h, const char* stage) {
     if (e & DERR_PERM_OUT_OF_RANGE) m += " permutation entry outside [0, M) or not a permutation;";
     if (e & DERR_CAPACITY) m += " internal capacity exceeded;";
     if (e & DERR_INTERNAL) m += " internal consistency check failed;";
-    xspmm_status_t s = (e & (DERR_INTERNAL | DERR_CAPACITY)) ? XSPMM_STATUS_INTERNAL
-                                                             : XSPMM_STATUS_INVALID_ARGUMENT;
+    if (e & DERR_TIMEOUT) m += " a bounded wait inside a kernel timed out;";
+    xspmm_status_t s = (e & DERR_TIMEOUT) ? XSPMM_STATUS_TIMEOUT
+                       : (e & (DERR_INTERNAL | DERR_CAPACITY)) ? XSPMM_STATUS_INTERNAL
+                                                               : XSPMM_STATUS_INVALID_ARGUMENT;
     throw Error(s, m);
 }
 

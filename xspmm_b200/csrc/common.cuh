@@ -49,6 +49,7 @@ enum DeviceError : unsigned {
     DERR_PERM_OUT_OF_RANGE = 1u << 2,
     DERR_INTERNAL = 1u << 3,
     DERR_CAPACITY = 1u << 4,
+    DERR_TIMEOUT = 1u << 5,
 };
 
 // ------------------------------------------------------------------------------------------------
@@ -61,6 +62,7 @@ struct Handle {
     unsigned* h_err = nullptr;       // pinned mirror
     unsigned long long launches = 0;  // kernels this library launched on the handle
     cudaEvent_t ev[8] = {};           // stage timing events
+    int tier1_kernel = 0;             // 0 auto, 1 mma.sync, 2 tcgen05 (xspmm_set_tier1_kernel)
 };
 
 // RAII: make the handle's device current for the duration of a call.

@@ -17,6 +17,7 @@
 // scatter in parallel across lanes -- distinct rows never share a destination; any other row is
 // written by one lane in CSR order so the last duplicate wins, as in the reference.
 #include "ops.cuh"
+#include "blockcols.cuh"
 
 #include <algorithm>
 
@@ -24,83 +25,6 @@ namespace xspmm_b200 {
 namespace {
 
 constexpr int CV_WARPS = 8;
-constexpr int WIN_WORDS = 256;
-constexpr int64_t WIN_BITS = (int64_t)WIN_WORDS * 32;
-constexpr int WORDS_PER_LANE = WIN_WORDS / 32;
-
-struct BlockDiv {
-    int shift;    // >= 0 when the block width is a power of two
-    int64_t div;  // block width
-    __device__ __forceinline__ int64_t operator()(int64_t c) const {
-        return shift >= 0 ? (c >> shift) : (c / div);
-    }
-};
-
-BlockDiv make_div(int64_t w) {
-    BlockDiv d{-1, w};
-    if (w > 0 && (w & (w - 1)) == 0) {
-        int s = 0;
-        while ((int64_t(1) << s) < w) ++s;
-        d.shift = s;
-    }
-    return d;
-}
-
-__device__ __forceinline__ int64_t warp_min64(int64_t v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = min(v, (int64_t)__shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-__device__ __forceinline__ int64_t warp_max64(int64_t v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = max(v, (int64_t)__shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-__device__ __forceinline__ int64_t warp_sum64(int64_t v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// Block-column range [lo, hi] of entries [e0, e1); flags out-of-range columns. hi < 0 if none.
-template <typename IT>
-__device__ void block_col_range(const IT* ci, int64_t e0, int64_t e1, int64_t K, BlockDiv bd,
-                                int64_t& lo, int64_t& hi, unsigned* err) {
-    const int lane = threadIdx.x & 31;
-    lo = INT64_MAX;
-    hi = -1;
-    bool bad = false;
-    for (int64_t e = e0 + lane; e < e1; e += 32) {
-        const int64_t c = (int64_t)ci[e];
-        if (c < 0 || c >= K) {
-            bad = true;
-            continue;
-        }
-        const int64_t b = bd(c);
-        lo = min(lo, b);
-        hi = max(hi, b);
-    }
-    if (__any_sync(0xffffffffu, bad) && lane == 0 && err) flag_error(err, DERR_COL_OUT_OF_RANGE);
-    lo = warp_min64(lo);
-    hi = warp_max64(hi);
-}
-
-// Marks the block columns of entries [e0, e1) that fall in [wb, wb + nwords*32) in win.
-template <typename IT>
-__device__ void mark_window(uint32_t* win, int nwords, const IT* ci, int64_t e0, int64_t e1,
-                            int64_t K, BlockDiv bd, int64_t wb) {
-    const int lane = threadIdx.x & 31;
-    for (int w = lane; w < nwords; w += 32) win[w] = 0u;
-    __syncwarp();
-    const int64_t span = (int64_t)nwords * 32;
-    for (int64_t e = e0 + lane; e < e1; e += 32) {
-        const int64_t c = (int64_t)ci[e];
-        if (c < 0 || c >= K) continue;
-        const int64_t d = bd(c) - wb;
-        if (d >= 0 && d < span) atomicOr(&win[d >> 5], 1u << (d & 31));
-    }
-    __syncwarp();
-}
 
 // Validates row_ptr over [r0, r1]; returns false (and flags) when it is malformed.
 template <typename IT>

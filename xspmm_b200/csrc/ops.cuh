@@ -15,6 +15,20 @@ void bcsr_spmm(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* row_
                const IT* col_ind, const VT* values, const VT* B, float* C, int64_t M, int64_t K,
                int64_t N, const IT* row_map);
 
+// Tier-1 on tcgen05 (block rows stacked to M=128, TMA-fed); tc_supported says whether the
+// shapes and alignments allow it.
+bool tc_supported(int64_t nbr, int64_t nbc, int64_t nnzb, const void* vals, const void* B,
+                  const void* C, int64_t N);
+template <typename IT>
+void bcsr_spmm_tc(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
+                  const __half* vals, const __half* B, float* C, int64_t M, int64_t K, int64_t N,
+                  const IT* map);
+
+// Which Tier-1 fp16 kernel runs: the handle's setting (xspmm_set_tier1_kernel) if not auto, else
+// the environment XSPMM_TIER1_KERNEL = mma | tc | auto (default auto).
+enum class Tier1Kernel { Auto, Mma, Tc };
+Tier1Kernel tier1_kernel_choice(const Handle& h);
+
 // Exact greedy Jaccard clustering (writes perm[M]).
 template <typename IT>
 void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,

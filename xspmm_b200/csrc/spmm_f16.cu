@@ -19,6 +19,9 @@
 // loads instead.
 #include "ops.cuh"
 
+#include <cstdlib>
+#include <cstring>
+
 namespace xspmm_b200 {
 namespace {
 
@@ -205,11 +208,36 @@ void launch(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
 
 }  // namespace
 
+Tier1Kernel tier1_kernel_choice(const Handle& h) {
+    if (h.tier1_kernel == 1) return Tier1Kernel::Mma;
+    if (h.tier1_kernel == 2) return Tier1Kernel::Tc;
+    static const Tier1Kernel k = [] {
+        const char* e = std::getenv("XSPMM_TIER1_KERNEL");
+        if (e && std::strcmp(e, "mma") == 0) return Tier1Kernel::Mma;
+        if (e && std::strcmp(e, "tc") == 0) return Tier1Kernel::Tc;
+        return Tier1Kernel::Auto;
+    }();
+    return k;
+}
+
+// tcgen05 stacks 8 block rows per MMA over the union of their block columns, so it pays when the
+// block grid is dense (little zero padding) and block rows are long (B tiles reused 8 times).
+static bool tc_preferred(int64_t nbr, int64_t nbc, int64_t nnzb) {
+    const double density = (double)nnzb / ((double)nbr * (double)nbc);
+    return density >= 0.25 && nnzb >= 32 * nbr;
+}
+
 template <typename IT>
-static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, const IT* rp, const IT* ci,
-                               const __half* v, const __half* B, float* C, int64_t M, int64_t K,
-                               int64_t N, const IT* map) {
+static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,
+                               const IT* ci, const __half* v, const __half* B, float* C,
+                               int64_t M, int64_t K, int64_t N, const IT* map) {
     if (nbr == 0 || N == 0 || M == 0) return;
+    const Tier1Kernel choice = tier1_kernel_choice(h);
+    if (choice != Tier1Kernel::Mma && tc_supported(nbr, nbc, nnzb, v, B, C, N) &&
+        (choice == Tier1Kernel::Tc || tc_preferred(nbr, nbc, nnzb))) {
+        bcsr_spmm_tc<IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
+        return;
+    }
     XS_REQUIRE(ceil_div(N, 64) <= 65535, XSPMM_STATUS_UNSUPPORTED, "N above 4,194,240 columns");
     const bool aligned = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(v) % 16 == 0) &&
@@ -227,16 +255,18 @@ static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, const IT* rp, const IT* c
 }
 
 template <>
-void bcsr_spmm<__half, int32_t>(Handle& h, int64_t nbr, int64_t, int64_t, const int32_t* rp,
-                                const int32_t* ci, const __half* v, const __half* B, float* C,
-                                int64_t M, int64_t K, int64_t N, const int32_t* map) {
-    bcsr_spmm_f16_impl<int32_t>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+void bcsr_spmm<__half, int32_t>(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb,
+                                const int32_t* rp, const int32_t* ci, const __half* v,
+                                const __half* B, float* C, int64_t M, int64_t K, int64_t N,
+                                const int32_t* map) {
+    bcsr_spmm_f16_impl<int32_t>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
 }
 template <>
-void bcsr_spmm<__half, int64_t>(Handle& h, int64_t nbr, int64_t, int64_t, const int64_t* rp,
-                                const int64_t* ci, const __half* v, const __half* B, float* C,
-                                int64_t M, int64_t K, int64_t N, const int64_t* map) {
-    bcsr_spmm_f16_impl<int64_t>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+void bcsr_spmm<__half, int64_t>(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb,
+                                const int64_t* rp, const int64_t* ci, const __half* v,
+                                const __half* B, float* C, int64_t M, int64_t K, int64_t N,
+                                const int64_t* map) {
+    bcsr_spmm_f16_impl<int64_t>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
 }
 
 }  // namespace xspmm_b200

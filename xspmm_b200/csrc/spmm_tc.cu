@@ -1,0 +1,631 @@
+// spmm_tc.cu -- Tier-1 BCSR SpMM on the 5th-generation tensor cores: tcgen05.mma with the
+// accumulator in TMEM, operands staged by TMA through an mbarrier ring.
+//
+// Same result as the reference kernel (src/common/spmm_math.hpp:59-122): C[16br+i, n] =
+// sum over the blocks j of block row br of A_j[i, :] . B[16 col_j + :, n], every row written.
+//
+// Mapping (block rows stacked to M = 128): a CTA owns a group of 8 consecutive block rows and a
+// 256-column tile of C. The group's block columns are merged into one sorted union list (the
+// "group plan", built on the device per call). For every union column u one MMA
+//   D[128 x 256] += A_u[128 x 16] . B[16u .. 16u+15, n0 .. n0+255]
+// is issued, where A_u stacks the 8 block rows' blocks at column u (zeros where a block row has
+// no block there). One B tile therefore feeds 8 block
+// rows -- the mma.sync kernel re-reads it for every block row -- and each MMA is a full-width
+// 128x256x16 tcgen05 instruction. Dense-block matrices (every union column present in every
+// block row) waste nothing; on scattered patterns the zero rows are wasted work, so the
+// dispatcher only picks this kernel for dense block structure.
+//
+// Before the MMA kernel, the 8 blocks of every union entry are packed into one contiguous
+// 128 x 16 tile (zeros for missing blocks), so a stage is two TMA requests. Roles (192 threads):
+// warp 0 lane 0 issues the TMA loads of a stage (the packed A tile through a SWIZZLE_32B map ->
+// K-major canonical layout; the B slab as one 3-D box or four 64-column SWIZZLE_128B boxes ->
+// MN-major canonical layout); warp 1 lane 0 issues tcgen05.mma and
+// tcgen05.commit (which frees the stage when the MMA has read it); warps 2..5 wait for the
+// accumulator, read TMEM with tcgen05.ld (warp w reads lanes 32*(w%4)..+31) and store rows of C
+// (through the optional row map, so the Tier-2 unpermute stays fused). When the grid would be
+// smaller than the GPU, the union list is split across CTAs (split-K) and a second kernel sums the
+// partial tiles in a fixed order. Every mbarrier wait is bounded; a timeout sets an error flag and
+// the CTA still waits (bounded) for its own TMA loads before freeing TMEM and exiting.
+#include "ops.cuh"
+#include "blockcols.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+namespace xspmm_b200 {
+namespace {
+
+constexpr int TC_GROUP = 8;                        // block rows per tile (M = 128)
+constexpr int TC_BN = 256;                         // columns per tile = the MMA's N
+constexpr int TC_STAGES = 8;
+constexpr int A_STAGE = TC_GROUP * 512;            // 4 KB
+constexpr int B_BOX = 16 * 128;                    // 16 rows x 64 fp16 = 2 KB
+constexpr int B_STAGE = (TC_BN / 64) * B_BOX;      // 8 KB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;     // 12 KB (multiple of 1024)
+constexpr int TC_THREADS = 192;
+constexpr int TMEM_COLS = 256;
+constexpr long long WAIT_LIMIT = 1ll << 22;        // polls of an mbarrier before giving up
+constexpr size_t TC_SMEM = (size_t)TC_STAGES * STAGE_BYTES + 1024 + 256;
+
+// ---- PTX wrappers ---------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false (and the error flag) if the phase did not complete.
+__device__ bool mbar_wait(uint64_t* b, uint32_t parity, unsigned* err) {
+    for (long long i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait(b, parity)) return true;
+    flag_error(err, DERR_TIMEOUT);
+    return false;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D (TMEM) [+]= A (smem desc) x B (smem desc), kind::f16, cta_group::1, issued by one thread.
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+          "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptors (sm100 format: start>>4 [0,14), LBO>>4 [16,30), SBO>>4
+// [32,46), version 1 at [46,48), layout type [61,64)).
+// A: K-major, SWIZZLE_32B: rows of 32 B (16 fp16 = one MMA's K), 8-row atoms of 256 B.
+__device__ __forceinline__ uint64_t desc_a(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
+}
+// B: MN-major, SWIZZLE_128B: 64-column chunks of 16 rows x 128 B (2 KB apart = LBO), 8-row
+// groups 1 KB apart (SBO).
+__device__ __forceinline__ uint64_t desc_b(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(B_BOX >> 4) << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: D f32 (bit 4), A/B f16 (0), A K-major (bit 15 = 0), B
+// MN-major (bit 16 = 1), N >> 3 at [17,23), M >> 4 at [24,29).
+constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 16) | ((uint32_t)(TC_BN >> 3) << 17) |
+                              ((uint32_t)(128 >> 4) << 24);
+
+// ---- the kernel -----------------------------------------------------------------------------------
+template <typename IT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+bcsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const int64_t* __restrict__ gptr, const int32_t* __restrict__ gcol,
+                    float* __restrict__ out, const IT* __restrict__ row_map, int64_t M,
+                    int64_t N, int64_t m_pad, int splits, int ntiles, int b3d,
+                    unsigned* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * STAGE_BYTES);
+    uint64_t* empty = full + TC_STAGES;
+    uint64_t* accum = empty + TC_STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    int* issued_slot = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int bid = blockIdx.x;
+    const int split = bid % splits;
+    bid /= splits;
+    const int ntile = bid % ntiles;
+    const int g = bid / ntiles;
+    const int64_t u0 = gptr[g], ulen = gptr[g + 1] - u0;
+    const int64_t k0 = u0 + ulen * split / splits;
+    const int nk = (int)(u0 + ulen * (split + 1) / splits - k0);
+    const int n0 = ntile * TC_BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TC_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        *issued_slot = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // TMA producer: per stage one 4 KB packed A tile (union entry u = 128 rows x 16) and the
+        // 16 x 256 B slab (one 3-D box when N % 64 == 0, else four 64-column boxes). The warp
+        // loads 32 stages' union columns at once so lane 0 never waits on a global load between
+        // issues.
+        int i = 0;
+        bool stop = false;
+        for (int c = 0; c < nk && !stop; c += 32) {
+            const int col = c + lane < nk ? gcol[k0 + c + lane] : 0;
+            const int cnt = min(32, nk - c);
+            for (int t = 0; t < cnt; ++t) {
+                const int colt = __shfl_sync(0xffffffffu, col, t);
+                int ok = 1;
+                if (lane == 0) {
+                    const int s = i % TC_STAGES;
+                    if (i >= TC_STAGES && !mbar_wait(&empty[s], ((i / TC_STAGES) & 1) ^ 1, err)) {
+                        ok = 0;
+                    } else {
+                        mbar_expect_tx(&full[s], STAGE_BYTES);
+                        uint8_t* sA = smem + s * STAGE_BYTES;
+                        uint8_t* sB = sA + A_STAGE;
+                        tma_load_2d(sA, &tmA, 0, (int)((k0 + i) * 128), &full[s]);
+                        if (b3d) {
+                            tma_load_3d(sB, &tmB, 0, colt * 16, n0 / 64, &full[s]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < TC_BN / 64; ++j)
+                                tma_load_2d(sB + j * B_BOX, &tmB, n0 + 64 * j, colt * 16, &full[s]);
+                        }
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    stop = true;
+                    break;
+                }
+                ++i;
+            }
+        }
+        if (lane == 0) *issued_slot = i;
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            bool ok = true;
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % TC_STAGES;
+                if (!mbar_wait(&full[s], (i / TC_STAGES) & 1, err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+                tc_mma(tmem, desc_a(sa), desc_b(sa + A_STAGE), TC_IDESC, i > 0 ? 1u : 0u);
+                tc_commit(&empty[s]);
+            }
+            // commit even after a timeout: it arrives only once the MMAs already issued are
+            // done, so TMEM is never read or freed under them
+            if (nk > 0) tc_commit(accum);
+            else mbar_arrive(accum);
+            (void)ok;
+        }
+    } else {  // epilogue warps 2..5
+        const bool have = mbar_wait(accum, 0, err);
+        tc_fence_after();
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int64_t grow = (int64_t)g * 128 + q * 32 + lane;
+        float* dst = nullptr;
+        if (grow < M) {
+            if (splits > 1) {
+                dst = out + ((int64_t)split * m_pad + grow) * N;
+            } else {
+                const int64_t orow = row_map ? (int64_t)row_map[grow] : grow;
+                if (orow >= 0 && orow < M) dst = out + orow * N;
+                else flag_error(err, DERR_PERM_OUT_OF_RANGE);
+            }
+        }
+#pragma unroll 1
+        for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+            uint32_t v[32];
+            if (nk > 0 && have) {
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] = 0u;
+            }
+            const int64_t col = (int64_t)n0 + c0;
+            if (dst && col < N) {
+                if (col + 32 <= N) {
+                    float4* d4 = reinterpret_cast<float4*>(dst + col);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        d4[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                            __uint_as_float(v[4 * e + 2]),
+                                            __uint_as_float(v[4 * e + 3]));
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (col + e < N) dst[col + e] = __uint_as_float(v[e]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        if (lane == 0) {  // never leave a TMA load in flight behind us
+            const int issued = *issued_slot;
+            for (int i = 0; i < issued; ++i) {
+                const int s = i % TC_STAGES;
+                // the last completed phase of stage s: wait with its parity (bounded)
+                if (i + TC_STAGES >= issued) mbar_wait(&full[s], (i / TC_STAGES) & 1, err);
+            }
+        }
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// C[map(row)] = sum over splits of the partial tiles, in split order.
+template <typename IT>
+__global__ void tc_reduce_kernel(const float* __restrict__ part, float* __restrict__ C,
+                                 const IT* __restrict__ row_map, int64_t M, int64_t N,
+                                 int64_t m_pad, int splits, unsigned* err) {
+    const int64_t total = M * N;
+    for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < total;
+         i += (int64_t)gridDim.x * blockDim.x * 4) {
+        const int64_t r = i / N, c = i % N;  // N % 8 == 0, so a float4 never straddles rows
+        float4 s = reinterpret_cast<const float4*>(part + r * N + c)[0];
+        for (int k = 1; k < splits; ++k) {
+            const float4 p = reinterpret_cast<const float4*>(part + ((int64_t)k * m_pad + r) * N + c)[0];
+            s.x += p.x; s.y += p.y; s.z += p.z; s.w += p.w;
+        }
+        const int64_t orow = row_map ? (int64_t)row_map[r] : r;
+        if (orow < 0 || orow >= M) {
+            flag_error(err, DERR_PERM_OUT_OF_RANGE);
+            continue;
+        }
+        reinterpret_cast<float4*>(C + orow * N + c)[0] = s;
+    }
+}
+
+// Packs the A operand: for every union entry u, the 8 stacked blocks as one contiguous 128 x 16
+// tile (4 KB, row-major; zeros for a missing block), so a stage needs one TMA load for A.
+__global__ void tc_pack_kernel(const int64_t* __restrict__ gptr, int64_t ngroups,
+                               const int32_t* __restrict__ gblk, const __half* __restrict__ vals,
+                               __half* __restrict__ apk, int64_t bound) {
+    const int64_t total = min(gptr[ngroups], bound) * 256;  // 16-byte chunks
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < total;
+         c += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t u = c >> 8;
+        const int within = (int)(c & 255);  // 16 row-pairs... chunk index inside the 4 KB tile
+        const int b = within >> 5;          // block slot (32 chunks of 16 B per block)
+        const int blk = gblk[u * TC_GROUP + b];
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (blk >= 0) v = reinterpret_cast<const uint4*>(vals + (int64_t)blk * 256)[within & 31];
+        reinterpret_cast<uint4*>(apk + u * 2048)[within] = v;
+    }
+}
+
+// ---- group plan: union of block columns over 8 block rows -------------------------------------
+// One CTA per group: the block columns of its <= 8 block rows are marked in a shared-memory bitmap
+// window (all threads), the union size is the window's population, a block's slot in the union
+// is the population below its bit. Windows of 8192 columns are taken in turn.
+constexpr int GP_THREADS = 256;
+constexpr int GP_WORDS = 256;  // one 32-bit word per thread
+
+__device__ __forceinline__ int64_t cta_min64(int64_t v, int64_t* red) {
+    v = warp_min64(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int64_t r = red[0];
+    for (int w = 1; w < GP_THREADS / 32; ++w) r = min(r, red[w]);
+    __syncthreads();
+    return r;
+}
+__device__ __forceinline__ int64_t cta_max64(int64_t v, int64_t* red) {
+    v = warp_max64(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int64_t r = red[0];
+    for (int w = 1; w < GP_THREADS / 32; ++w) r = max(r, red[w]);
+    __syncthreads();
+    return r;
+}
+
+// Marks the window [wb, wb + GP_WORDS*32) with the block columns of entries [e0, e1); returns
+// this thread's word population, with the CTA's exclusive prefix of word populations in *pre
+// and the total in *total (all after a barrier).
+template <typename IT>
+__device__ void gp_mark(uint32_t* win, const IT* bci, int64_t e0, int64_t e1, int64_t wb,
+                        uint32_t* s_warp, uint32_t* pre_out, uint32_t* total_out) {
+    const int tid = threadIdx.x;
+    win[tid] = 0u;
+    __syncthreads();
+    const int64_t span = (int64_t)GP_WORDS * 32;
+    for (int64_t e = e0 + tid; e < e1; e += GP_THREADS) {
+        const int64_t d = (int64_t)bci[e] - wb;
+        if (d >= 0 && d < span) atomicOr(&win[d >> 5], 1u << (d & 31));
+    }
+    __syncthreads();
+    const uint32_t pc = __popc(win[tid]);
+    const uint32_t inc = warp_inclusive_sum(pc);
+    if ((tid & 31) == 31) s_warp[tid >> 5] = inc;
+    __syncthreads();
+    uint32_t off = 0, tot = 0;
+    for (int w = 0; w < GP_THREADS / 32; ++w) {
+        if (w < (tid >> 5)) off += s_warp[w];
+        tot += s_warp[w];
+    }
+    *pre_out = off + inc - pc;
+    *total_out = tot;
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(GP_THREADS)
+tc_group_count_kernel(const IT* __restrict__ brp, const IT* __restrict__ bci, int64_t nbr,
+                      int64_t ngroups, int64_t* __restrict__ cnt) {
+    __shared__ uint32_t win[GP_WORDS];
+    __shared__ uint32_t s_warp[GP_THREADS / 32];
+    __shared__ int64_t red[GP_THREADS / 32];
+    for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x) {
+        const int64_t e0 = brp[g * TC_GROUP], e1 = brp[min(nbr, (g + 1) * TC_GROUP)];
+        int64_t lo = INT64_MAX, hi = -1;
+        for (int64_t e = e0 + threadIdx.x; e < e1; e += GP_THREADS) {
+            const int64_t c = (int64_t)bci[e];
+            lo = min(lo, c);
+            hi = max(hi, c);
+        }
+        lo = cta_min64(lo, red);
+        hi = cta_max64(hi, red);
+        int64_t count = 0;
+        for (int64_t wb = lo; wb <= hi; wb += (int64_t)GP_WORDS * 32) {
+            uint32_t pre, tot;
+            gp_mark(win, bci, e0, e1, wb, s_warp, &pre, &tot);
+            count += tot;
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) cnt[g] = count;
+    }
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(GP_THREADS)
+tc_group_fill_kernel(const IT* __restrict__ brp, const IT* __restrict__ bci, int64_t nbr,
+                     int64_t ngroups, const int64_t* __restrict__ gptr,
+                     int32_t* __restrict__ gcol, int32_t* __restrict__ gblk) {
+    __shared__ uint32_t win[GP_WORDS];
+    __shared__ uint32_t pre_s[GP_WORDS];
+    __shared__ uint32_t s_warp[GP_THREADS / 32];
+    __shared__ int64_t red[GP_THREADS / 32];
+    const int tid = threadIdx.x;
+    for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x) {
+        const int64_t r0 = g * TC_GROUP, r1 = min(nbr, r0 + TC_GROUP);
+        const int64_t e0 = brp[r0], e1 = brp[r1];
+        const int64_t base = gptr[g];
+        int64_t lo = INT64_MAX, hi = -1;
+        for (int64_t e = e0 + tid; e < e1; e += GP_THREADS) {
+            const int64_t c = (int64_t)bci[e];
+            lo = min(lo, c);
+            hi = max(hi, c);
+        }
+        lo = cta_min64(lo, red);
+        hi = cta_max64(hi, red);
+        int64_t rank_base = 0;
+        for (int64_t wb = lo; wb <= hi; wb += (int64_t)GP_WORDS * 32) {
+            uint32_t pre, tot;
+            gp_mark(win, bci, e0, e1, wb, s_warp, &pre, &tot);
+            pre_s[tid] = pre;
+            {
+                uint32_t x = win[tid];
+                int64_t o = base + rank_base + pre;
+                while (x) {
+                    const int b = __ffs(x) - 1;
+                    gcol[o++] = (int32_t)(wb + (int64_t)tid * 32 + b);
+                    x &= x - 1;
+                }
+            }
+            __syncthreads();
+            const int64_t span = (int64_t)GP_WORDS * 32;
+            for (int64_t r = r0; r < r1; ++r) {
+                const int64_t j0 = brp[r], j1 = brp[r + 1];
+                for (int64_t j = j0 + tid; j < j1; j += GP_THREADS) {
+                    const int64_t d = (int64_t)bci[j] - wb;
+                    if (d < 0 || d >= span) continue;
+                    const int64_t rank =
+                        rank_base + pre_s[d >> 5] + __popc(win[d >> 5] & ((1u << (d & 31)) - 1u));
+                    gblk[(base + rank) * TC_GROUP + (r - r0)] = (int32_t)j;
+                }
+            }
+            rank_base += tot;
+            __syncthreads();
+        }
+    }
+}
+
+// ---- host side -----------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    XS_REQUIRE(fn != nullptr, XSPMM_STATUS_CUDA_ERROR, "cuTensorMapEncodeTiled unavailable");
+    return fn;
+}
+
+CUtensorMap make_map_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                        uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    CUtensorMap m;
+    std::memset(&m, 0, sizeof(m));
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+                                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    XS_REQUIRE(r == CUDA_SUCCESS, XSPMM_STATUS_CUDA_ERROR,
+               "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return m;
+}
+
+// B viewed as [N/64 chunks][K rows][64 columns] (strides 128 B and N*2 B): one box of 4 chunks x
+// 16 rows x 64 columns lands in shared memory as four 2 KB chunks, the MN-major SWIZZLE_128B
+// canonical layout with LBO = 2 KB. Returns false if the driver rejects the view.
+bool make_map_b3d(const void* B, int64_t N, int64_t K, CUtensorMap* out) {
+    std::memset(out, 0, sizeof(*out));
+    const cuuint64_t dims[3] = {64, (cuuint64_t)K, (cuuint64_t)(N / 64)};
+    const cuuint64_t strides[2] = {(cuuint64_t)N * 2, 128};
+    const cuuint32_t box[3] = {64, 16, (cuuint32_t)(TC_BN / 64)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B),
+                                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+unsigned gp_grid(Handle& h, int64_t ngroups) {
+    return (unsigned)std::max<int64_t>(1, std::min(ngroups, (int64_t)sm_count(h.device) * 8));
+}
+
+}  // namespace
+
+bool tc_supported(int64_t nbr, int64_t nbc, int64_t nnzb, const void* vals, const void* B,
+                  const void* C, int64_t N) {
+    return nbr > 0 && nbc > 0 && nnzb > 0 && N > 0 && N % 8 == 0 && nnzb * 16 < (int64_t(1) << 31) &&
+           nbc * 16 < (int64_t(1) << 31) && reinterpret_cast<uintptr_t>(vals) % 16 == 0 &&
+           reinterpret_cast<uintptr_t>(B) % 16 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0;
+}
+
+template <typename IT>
+void bcsr_spmm_tc(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
+                  const __half* vals, const __half* B, float* C, int64_t M, int64_t K, int64_t N,
+                  const IT* map) {
+    cudaStream_t s = h.stream;
+    const int64_t ngroups = ceil_div(nbr, TC_GROUP);
+    const int64_t bound = std::min(nnzb, ngroups * nbc);  // union entries, upper bound
+    DevBuf<int64_t> gptr(ngroups + 1, s);
+    DevBuf<int32_t> gcol(std::max<int64_t>(bound, 1), s), gblk(std::max<int64_t>(bound, 1) * TC_GROUP, s);
+    XS_CHECK_CUDA(cudaMemsetAsync(gblk.get(), 0xFF, gblk.n * sizeof(int32_t), s));
+    tc_group_count_kernel<IT><<<gp_grid(h, ngroups), GP_THREADS, 0, s>>>(rp, ci, nbr, ngroups,
+                                                                        gptr.get());
+    after_launch(h, "tc_group_count");
+    exclusive_scan<int64_t>(h, gptr.get(), gptr.get(), ngroups);
+    tc_group_fill_kernel<IT><<<gp_grid(h, ngroups), GP_THREADS, 0, s>>>(
+        rp, ci, nbr, ngroups, gptr.get(), gcol.get(), gblk.get());
+    after_launch(h, "tc_group_fill");
+
+    const int ntiles = (int)ceil_div(N, TC_BN);
+    const int64_t tiles = ngroups * ntiles;
+    const int64_t slots = (int64_t)sm_count(h.device) * 2;
+    const int64_t avg_union = std::max<int64_t>(1, bound / ngroups);
+    int splits = 1;
+    if (tiles < slots) splits = (int)std::min<int64_t>({ceil_div(slots, tiles), 16, std::max<int64_t>(1, avg_union / 32)});
+    XS_REQUIRE(tiles * splits < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "grid too large");
+    const int64_t m_pad = ngroups * 128;
+    DevBuf<float> part(splits > 1 ? (size_t)(splits * m_pad * N) : 0, s);
+
+    XS_REQUIRE(bound * 128 < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "union too large");
+    DevBuf<__half> apk((size_t)std::max<int64_t>(bound, 1) * 2048, s);
+    {
+        const unsigned grid = (unsigned)std::max<int64_t>(
+            1, std::min(ceil_div(bound * 256, 256), (int64_t)sm_count(h.device) * 16));
+        tc_pack_kernel<<<grid, 256, 0, s>>>(gptr.get(), ngroups, gblk.get(), vals, apk.get(), bound);
+        after_launch(h, "tc_pack");
+    }
+    const CUtensorMap tmA = make_map_2d(apk.get(), 16, (uint64_t)std::max<int64_t>(bound, 1) * 128,
+                                        32, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B);
+    int b3d = 0;
+    CUtensorMap tmB;
+    if (N % 64 == 0 && make_map_b3d(B, N, K, &tmB)) {
+        b3d = 1;
+    } else {
+        tmB = make_map_2d(B, (uint64_t)N, (uint64_t)K, (uint64_t)N * 2, 64, 16,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    auto kern = bcsr_spmm_tc_kernel<IT>;
+    XS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
+    kern<<<(unsigned)(tiles * splits), TC_THREADS, TC_SMEM, s>>>(
+        tmA, tmB, gptr.get(), gcol.get(), splits > 1 ? part.get() : C, map, M, N, m_pad, splits,
+        ntiles, b3d, h.d_err);
+    after_launch(h, "bcsr_spmm_tc");
+    if (splits > 1) {
+        const int64_t work = ceil_div(M * N, 4);
+        const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(ceil_div(work, 256), (int64_t)sm_count(h.device) * 16));
+        tc_reduce_kernel<IT><<<grid, 256, 0, s>>>(part.get(), C, map, M, N, m_pad, splits, h.d_err);
+        after_launch(h, "tc_reduce");
+    }
+}
+
+template void bcsr_spmm_tc<int32_t>(Handle&, int64_t, int64_t, int64_t, const int32_t*,
+                                    const int32_t*, const __half*, const __half*, float*, int64_t,
+                                    int64_t, int64_t, const int32_t*);
+template void bcsr_spmm_tc<int64_t>(Handle&, int64_t, int64_t, int64_t, const int64_t*,
+                                    const int64_t*, const __half*, const __half*, float*, int64_t,
+                                    int64_t, int64_t, const int64_t*);
+
+}  // namespace xspmm_b200
