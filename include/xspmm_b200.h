@@ -233,6 +233,68 @@ xspmm_status_t xspmm_spmm_csr_f32f32_i64(xspmm_handle_t h, int64_t M, int64_t K,
     const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
     int64_t N, int64_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
 
+/* ---------------------------------------------------------------------------------------------
+ * Plan: the Tier-2 stages run once, many products afterwards. The reference has no object for
+ * this; its Tier-2 call repeats clustering, permutation and conversion every time
+ * (src/cuda/unstructured_mtx_mul.cu:56-130) and it points callers who multiply one A by many B
+ * to Tier 1 "for amortizing clustering time over thousands of iterations" (README.md:127). A plan
+ * is that amortization done inside the library: it keeps the permutation, the permuted BCSR
+ * matrix and, where the tcgen05 kernel is chosen, A's stacked tensor-core tiles on the device.
+ *
+ * xspmm_plan_csr_*: the stages of xspmm_spmm_csr_* up to and including CSR->BCSR, with the same
+ *   arguments (hw_block_size must be 16). build_timings (may be NULL) receives clustering_ms,
+ *   permutation_ms and conversion_ms (CSR->BCSR plus the tensor-core tile packing); spmm_ms and
+ *   unpermutation_ms are 0. The caller's CSR arrays may be freed once the call returns.
+ * xspmm_plan_bcsr_*: adopts a BCSR matrix for Tier-1 products (the arguments of
+ *   xspmm_bcsr_spmm_*). The plan READS the caller's arrays at every product: keep them alive and
+ *   unchanged until xspmm_plan_destroy.
+ * xspmm_plan_execute: C (M x N, fp32, row-major, rows in the caller's order) = A * B, B (K x N,
+ *   row-major) of the plan's value type. Asynchronous on the handle's stream. Results equal
+ *   xspmm_spmm_csr_* / xspmm_bcsr_spmm_* on the same inputs and kernel choice.
+ * Plans belong to the handle they were built on and use its stream and kernel setting;
+ * xspmm_destroy fails with INVALID_ARGUMENT while any of its plans is alive.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct xspmm_plan_s* xspmm_plan_t;
+
+typedef struct xspmm_plan_info {
+    int64_t rows, cols;                           /* M, K */
+    int64_t block_rows, block_cols, nnz_blocks;   /* the 16 x 16 BCSR matrix */
+    int32_t clustered;                            /* rows permuted by the clustering */
+    int32_t value_bytes;                          /* 2 (f16) or 4 (f32) */
+    int32_t tcgen05_ready;                        /* stacked tiles for the tcgen05 kernel built */
+    int32_t reserved;
+    int64_t tcgen05_tiles;                        /* 128 x 16 tiles packed for it */
+    int64_t device_bytes;                         /* device memory the plan owns */
+} xspmm_plan_info_t;
+
+xspmm_status_t xspmm_plan_csr_f16f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t hw_block_size,
+    int enable_clustering, xspmm_plan_t* out, xspmm_timings_t* build_timings);
+xspmm_status_t xspmm_plan_csr_f16f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, int64_t hw_block_size,
+    int enable_clustering, xspmm_plan_t* out, xspmm_timings_t* build_timings);
+xspmm_status_t xspmm_plan_csr_f32f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t hw_block_size,
+    int enable_clustering, xspmm_plan_t* out, xspmm_timings_t* build_timings);
+xspmm_status_t xspmm_plan_csr_f32f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, int64_t hw_block_size,
+    int enable_clustering, xspmm_plan_t* out, xspmm_timings_t* build_timings);
+xspmm_status_t xspmm_plan_bcsr_f16f32_i32(xspmm_handle_t h, int32_t nbr, int32_t nbc,
+    int32_t nnzb, int32_t r_block, int32_t c_block, const int32_t* row_ptr, const int32_t* col_ind,
+    const void* values, int32_t M, int32_t K, xspmm_plan_t* out);
+xspmm_status_t xspmm_plan_bcsr_f16f32_i64(xspmm_handle_t h, int64_t nbr, int64_t nbc,
+    int64_t nnzb, int64_t r_block, int64_t c_block, const int64_t* row_ptr, const int64_t* col_ind,
+    const void* values, int64_t M, int64_t K, xspmm_plan_t* out);
+xspmm_status_t xspmm_plan_bcsr_f32f32_i32(xspmm_handle_t h, int32_t nbr, int32_t nbc,
+    int32_t nnzb, int32_t r_block, int32_t c_block, const int32_t* row_ptr, const int32_t* col_ind,
+    const void* values, int32_t M, int32_t K, xspmm_plan_t* out);
+xspmm_status_t xspmm_plan_bcsr_f32f32_i64(xspmm_handle_t h, int64_t nbr, int64_t nbc,
+    int64_t nnzb, int64_t r_block, int64_t c_block, const int64_t* row_ptr, const int64_t* col_ind,
+    const void* values, int64_t M, int64_t K, xspmm_plan_t* out);
+xspmm_status_t xspmm_plan_execute(xspmm_plan_t plan, const void* B, float* C, int64_t N);
+xspmm_status_t xspmm_plan_get_info(xspmm_plan_t plan, xspmm_plan_info_t* info);
+xspmm_status_t xspmm_plan_destroy(xspmm_plan_t plan);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -41,6 +41,22 @@ def test_null_handle_is_rejected_without_a_gpu():
     assert L.xspmm_get_launch_count(None, ctypes.byref(c)) == 1
 
 
+def test_plan_entry_points_reject_null_arguments_without_a_gpu():
+    L = _lib.lib()
+    plan = ctypes.c_void_p(123)
+    rc = L.xspmm_plan_csr_f16f32_i32(None, 16, 16, 0, None, None, None, 16, 1,
+                                     ctypes.byref(plan), None)
+    assert rc == 1 and plan.value is None  # output cleared before the handle is checked
+    assert L.xspmm_plan_bcsr_f32f32_i64(None, 1, 1, 0, 16, 16, None, None, None, 16, 16,
+                                        None) == 1
+    assert L.xspmm_plan_execute(None, None, None, 8) == 1
+    assert b"null plan" in L.xspmm_last_error()
+    info = _lib.PlanInfo()
+    assert L.xspmm_plan_get_info(None, ctypes.byref(info)) == 1
+    assert L.xspmm_plan_destroy(None) == 0  # destroying nothing is a no-op
+    assert ctypes.sizeof(_lib.PlanInfo) == 72
+
+
 def test_create_reports_a_status_instead_of_crashing():
     import torch
     if torch.cuda.is_available():

@@ -1,0 +1,162 @@
+"""GPU tests of the plan (xspmm_plan_*): the Tier-2 stages built once and executed many times.
+Products from a plan must equal the one-shot Tier-2 / Tier-1 calls bit for bit (same BCSR, same
+kernel) and the fp64 oracle within the fp16-input tolerance."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import xspmm_b200 as xs
+from tests.util import errors, fp32_block_emulation
+from xspmm_b200 import _lib, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_tier2(P, B, clustering):
+    rp, ci, v = P.row_ptr, P.col_ind, P.values
+    perm = None
+    if clustering:
+        perm = oracle.cluster_fast(rp, ci, P.M, P.K)
+        rp, ci, v = oracle.permute_rows(rp, ci, v, perm)
+    brp, bci, bv = oracle.csr_to_bcsr(rp, ci, v, P.M, P.K)
+    ref = oracle.bcsr_spmm_f64(P.M, P.K, B.shape[1], brp, bci, bv, B)
+    emu = fp32_block_emulation(P.M, B.shape[1], brp, bci, bv, B)
+    if perm is not None:
+        ref = oracle.unpermute_dense(ref, perm)
+        emu = oracle.unpermute_dense(emu, perm)
+    return ref, emu
+
+
+def _close(ref, emu, got):
+    e = errors(ref, got, 1e-3)
+    bound = max(1e-3, 2.0 * errors(ref, emu, 1e-3)["max_rel_guarded"])
+    assert e["max_rel_guarded"] <= bound, e
+
+
+@pytest.mark.parametrize("index_dtype", [torch.int32, torch.int64])
+def test_plan_csr_matches_tier2_and_oracle(executor, index_dtype):
+    P = synth.cfg2_hidden_block(seed=21, n=1024, N=64, block_density=0.03)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=index_dtype)
+    t = xs.SpMMTimings()
+    plan = xs.SpMMPlan(executor, A, 16, True, t)
+    info = plan.info()
+    assert info["clustered"] == 1 and info["rows"] == P.M and info["value_bytes"] == 2
+    assert t.clustering_ms > 0 and t.spmm_ms == 0
+    rng = np.random.default_rng(3)
+    for it in range(3):  # the same plan, different right-hand sides
+        B = rng.standard_normal((P.K, P.N)).astype(np.float16)
+        Bd = torch.as_tensor(B).to(executor.device)
+        C_plan = torch.full((P.M, P.N), float("nan"), device=executor.device)
+        C_once = torch.full((P.M, P.N), float("nan"), device=executor.device)
+        plan.execute(Bd, C_plan, P.N)
+        xs.spmm(executor, A, Bd, C_once, P.N, 16, True)
+        got = C_plan.cpu().numpy()
+        assert np.array_equal(got, C_once.cpu().numpy())
+        ref, emu = _oracle_tier2(P, B, True)
+        _close(ref, emu, got)
+    plan.close()
+
+
+def test_plan_csr_f32_without_clustering(executor):
+    rp, ci, v = synth.random_csr(333, 270, 0.05, seed=4, empty_row_frac=0.1)
+    v = np.asarray(v, np.float32)
+    A = xs.CSRMatrix.from_host(executor, 333, 270, rp, ci, v, index_dtype=torch.int64)
+    B = np.random.default_rng(5).standard_normal((270, 40)).astype(np.float32)
+    with xs.SpMMPlan(executor, A, 16, False) as plan:
+        assert plan.info()["clustered"] == 0
+        C = torch.full((333, 40), float("nan"), device=executor.device)
+        plan.execute(torch.as_tensor(B).to(executor.device), C, 40)
+        brp, bci, bv = oracle.csr_to_bcsr(rp, ci, v, 333, 270)
+        ref = oracle.bcsr_spmm_f64(333, 270, 40, brp, bci, bv, B)
+        assert errors(ref, C.cpu().numpy(), 1e-5)["max_rel_guarded"] <= 1e-5
+
+
+@pytest.mark.parametrize("kind", ["mma", "tc"])
+def test_plan_bcsr_matches_tier1(executor, kind):
+    P = synth.cfg3_pruned_llm(seed=22, M=512, K=1024, N=8)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int32)
+    Ab = xs.csr_to_bcsr(executor, A, 16, 16)
+    executor.set_tier1_kernel(kind)
+    try:
+        plan = xs.SpMMPlan.from_bcsr(Ab)
+        assert plan.info()["tcgen05_ready"] == (1 if kind == "tc" else 0)
+        rng = np.random.default_rng(6)
+        for N in (256, 72, 20):  # 20: not a multiple of 8, the tcgen05 plan falls back to mma
+            B = torch.as_tensor(rng.standard_normal((P.K, N)).astype(np.float16)).to(
+                executor.device)
+            C_plan = torch.full((P.M, N), float("nan"), device=executor.device)
+            C_once = torch.full((P.M, N), float("nan"), device=executor.device)
+            plan.execute(B, C_plan, N)
+            xs.spmm(Ab, B, C_once, N)
+            assert np.array_equal(C_plan.cpu().numpy(), C_once.cpu().numpy()), N
+        plan.close()
+    finally:
+        executor.set_tier1_kernel("auto")
+
+
+def test_plan_dense_structure_prepares_tcgen05_tiles(executor):
+    P = synth.cfg3_pruned_llm(seed=23, M=512, K=2048, N=256)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int32)
+    with xs.SpMMPlan(executor, A, 16, True) as plan:
+        info = plan.info()
+        assert info["tcgen05_ready"] == 1
+        assert 0 < info["tcgen05_tiles"] <= info["nnz_blocks"]
+        assert info["device_bytes"] >= info["tcgen05_tiles"] * 128 * 16 * 2
+        C = torch.full((P.M, P.N), float("nan"), device=executor.device)
+        plan.execute(torch.as_tensor(P.B).to(executor.device), C, P.N)
+        ref, emu = _oracle_tier2(P, P.B, True)
+        _close(ref, emu, C.cpu().numpy())
+
+
+def test_plan_empty_and_all_zero_matrices(executor):
+    # no rows: nothing to do
+    A0 = xs.CSRMatrix.from_host(executor, 0, 10, np.zeros(1, np.int32), np.zeros(0, np.int32),
+                                np.zeros(0, np.float16), index_dtype=torch.int32)
+    with xs.SpMMPlan(executor, A0, 16, True) as p0:
+        assert p0.info()["nnz_blocks"] == 0
+        p0.execute(torch.zeros((10, 8), dtype=torch.float16, device=executor.device),
+                   torch.zeros((0, 8), device=executor.device), 8)
+    # rows but no entries: C is all zeros
+    A1 = xs.CSRMatrix.from_host(executor, 37, 29, np.zeros(38, np.int32), np.zeros(0, np.int32),
+                                np.zeros(0, np.float16), index_dtype=torch.int32)
+    with xs.SpMMPlan(executor, A1, 16, True) as p1:
+        C = torch.full((37, 16), float("nan"), device=executor.device)
+        p1.execute(torch.ones((29, 16), dtype=torch.float16, device=executor.device), C, 16)
+        assert (C.cpu().numpy() == 0).all()
+
+
+def test_handle_with_live_plan_cannot_be_destroyed(executor):
+    ex = xs.CudaExecutor(executor.device_id)
+    rp, ci, v = synth.random_csr(64, 64, 0.1, seed=9)
+    A = xs.CSRMatrix.from_host(ex, 64, 64, rp, ci, np.asarray(v, np.float16),
+                               index_dtype=torch.int32)
+    plan = xs.SpMMPlan(ex, A, 16, True)
+    L = _lib.lib()
+    assert L.xspmm_destroy(ex._h) == 1
+    assert b"plans" in L.xspmm_last_error()
+    plan.close()
+    assert L.xspmm_destroy(ex._h) == 0
+    ex._h = None
+
+
+def test_plan_rejects_bad_arguments(executor):
+    rp, ci, v = synth.random_csr(64, 64, 0.1, seed=10)
+    A = xs.CSRMatrix.from_host(executor, 64, 64, rp, ci, np.asarray(v, np.float16),
+                               index_dtype=torch.int32)
+    with pytest.raises(xs.XSpMMError, match="UNSUPPORTED"):
+        xs.SpMMPlan(executor, A, 8, True)
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    assert L.xspmm_plan_bcsr_f16f32_i32(executor.handle, 4, 4, 0, 8, 8, None, None, None, 64, 64,
+                                        ctypes.byref(h)) == 2
+    with xs.SpMMPlan(executor, A, 16, True) as plan:
+        assert L.xspmm_plan_execute(plan._h, None, None, 8) == 1
+        with pytest.raises(ValueError):
+            plan.execute(torch.zeros((64, 8), device=executor.device),
+                         torch.zeros((64, 8), device=executor.device), 8)

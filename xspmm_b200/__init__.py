@@ -9,6 +9,7 @@ from .api import (  # noqa: F401
     BCSRMatrix,
     CSRMatrix,
     CudaExecutor,
+    SpMMPlan,
     SpMMTimings,
     apply_permutation,
     compute_1d_jaccard_clustering,

@@ -30,6 +30,15 @@ class Timings(ctypes.Structure):
         "total_pipeline_ms")]
 
 
+class PlanInfo(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+                ("block_rows", ctypes.c_int64), ("block_cols", ctypes.c_int64),
+                ("nnz_blocks", ctypes.c_int64), ("clustered", ctypes.c_int32),
+                ("value_bytes", ctypes.c_int32), ("tcgen05_ready", ctypes.c_int32),
+                ("reserved", ctypes.c_int32), ("tcgen05_tiles", ctypes.c_int64),
+                ("device_bytes", ctypes.c_int64)]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -47,6 +56,8 @@ def _sig(IT):
         "fill": [_P, IT, IT, IT, _P, _P, _P, IT, IT, _P, _P, _P],
         "unpermute": [_P, _P, _P, _P, IT, IT],
         "pipeline": [_P, IT, IT, IT, _P, _P, _P, _P, _P, IT, IT, ctypes.c_int, _P],
+        "plan_csr": [_P, IT, IT, IT, _P, _P, _P, IT, ctypes.c_int, ctypes.POINTER(_P), _P],
+        "plan_bcsr": [_P, IT, IT, IT, IT, IT, _P, _P, _P, IT, IT, ctypes.POINTER(_P)],
     }
 
 
@@ -81,12 +92,17 @@ def lib():
         for vt in ("f16f32", "f32f32"):
             getattr(L, f"xspmm_bcsr_spmm_{vt}_{suf}").argtypes = s["bcsr_spmm"]
             getattr(L, f"xspmm_spmm_csr_{vt}_{suf}").argtypes = s["pipeline"]
+            getattr(L, f"xspmm_plan_csr_{vt}_{suf}").argtypes = s["plan_csr"]
+            getattr(L, f"xspmm_plan_bcsr_{vt}_{suf}").argtypes = s["plan_bcsr"]
         getattr(L, f"xspmm_cluster_jaccard_{suf}").argtypes = s["cluster"]
         getattr(L, f"xspmm_csr_to_bcsr_count_{suf}").argtypes = s["count"]
         for v in ("f16", "f32"):
             getattr(L, f"xspmm_permute_rows_{v}_{suf}").argtypes = s["permute"]
             getattr(L, f"xspmm_csr_to_bcsr_fill_{v}_{suf}").argtypes = s["fill"]
             getattr(L, f"xspmm_unpermute_dense_{v}_{suf}").argtypes = s["unpermute"]
+    L.xspmm_plan_execute.argtypes = [_P, _P, _P, _I64]
+    L.xspmm_plan_get_info.argtypes = [_P, ctypes.POINTER(PlanInfo)]
+    L.xspmm_plan_destroy.argtypes = [_P]
     L.xspmm_permute_rows_noalloc_i32.argtypes = [_P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P,
                                                   _P, _P]
     _lib = L

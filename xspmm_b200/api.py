@@ -238,6 +238,84 @@ def spmm(*args, **kwargs):
     return _tier2(*args, **kwargs)
 
 
+class SpMMPlan:
+    """The Tier-2 stages done once for repeated products with the same A (xspmm_plan_* in
+    include/xspmm_b200.h). The reference recomputes them in every Tier-2 call
+    (src/cuda/unstructured_mtx_mul.cu:56-130) and leaves reuse to Tier-1 callers (README.md:127).
+
+    SpMMPlan(exec, A_csr, hw_block_size=16, optimize_pattern=True, timings=None) runs clustering,
+    permutation and CSR->BCSR (timings, if given, receives their times); SpMMPlan.from_bcsr(A)
+    adopts a BCSR matrix, whose arrays it keeps referenced. plan.execute(B, C, N) then computes
+    C = A * B with C's rows in A's original order."""
+
+    def __init__(self, exec: CudaExecutor | None = None, A: CSRMatrix | None = None,
+                 hw_block_size: int = 16, optimize_pattern: bool = True,
+                 timings: SpMMTimings | None = None, *, _handle=None, _keep=None,
+                 _value_dtype=None):
+        self._h = None
+        if _handle is not None:
+            self.exec, self._h, self._keep, self.value_dtype = exec, _handle, _keep, _value_dtype
+            return
+        _check_dev(exec, A.row_ptr)
+        IT = _it(A.index_dtype)
+        t = _lib.Timings()
+        h = ctypes.c_void_p()
+        fn = getattr(lib(), f"xspmm_plan_csr_{_VAL[A.value_dtype]}f32_{_IDX[A.index_dtype]}")
+        check(fn(exec.handle, IT(A.num_rows), IT(A.num_cols), IT(A.nnz), _p(A.row_ptr),
+                 _p(A.col_ind), _p(A.values), IT(hw_block_size), 1 if optimize_pattern else 0,
+                 ctypes.byref(h), ctypes.byref(t) if timings is not None else None))
+        self.exec, self._h, self._keep, self.value_dtype = exec, h, None, A.value_dtype
+        if timings is not None:
+            for f in ("clustering_ms", "permutation_ms", "conversion_ms", "spmm_ms",
+                      "unpermutation_ms", "total_pipeline_ms"):
+                setattr(timings, f, getattr(t, f))
+
+    @classmethod
+    def from_bcsr(cls, A: BCSRMatrix) -> "SpMMPlan":
+        exec = A.exec
+        IT = _it(A.index_dtype)
+        h = ctypes.c_void_p()
+        fn = getattr(lib(), f"xspmm_plan_bcsr_{_VAL[A.value_dtype]}f32_{_IDX[A.index_dtype]}")
+        check(fn(exec.handle, IT(A.num_block_rows), IT(A.num_block_cols), IT(A.num_blocks),
+                 IT(A.r_block), IT(A.c_block), _p(A.row_ptr), _p(A.col_ind), _p(A.values),
+                 IT(A.num_rows), IT(A.num_cols), ctypes.byref(h)))
+        return cls(exec, _handle=h, _keep=A, _value_dtype=A.value_dtype)
+
+    def execute(self, B: torch.Tensor, C: torch.Tensor, N: int) -> None:
+        if self._h is None:
+            raise ValueError("plan is closed")
+        if B.dtype != self.value_dtype:
+            raise ValueError("B must have the value type of A")
+        if C.dtype != torch.float32:
+            raise ValueError("C must be float32")
+        _check_dev(self.exec, B, C)
+        self.exec.handle  # binds torch's current stream to the handle
+        check(lib().xspmm_plan_execute(self._h, _p(B), _p(C), ctypes.c_int64(N)))
+
+    def info(self) -> dict:
+        inf = _lib.PlanInfo()
+        check(lib().xspmm_plan_get_info(self._h, ctypes.byref(inf)))
+        return {f: getattr(inf, f) for f, _ in _lib.PlanInfo._fields_ if f != "reserved"}
+
+    def close(self) -> None:
+        if self._h is not None:
+            self.exec.handle
+            check(lib().xspmm_plan_destroy(self._h))
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def compute_1d_jaccard_clustering(exec: CudaExecutor, A: CSRMatrix, dist_thresh: float,
                                   block_width: int, perm_out: torch.Tensor) -> None:
     """include/xspmm/clustering.hpp:19-25. perm_out: device tensor of A's index type, M entries."""

@@ -64,6 +64,7 @@ XS_API xspmm_status_t xspmm_destroy(xspmm_handle_t hh) {
     return guarded([&] {
         if (!hh) return;
         Handle& h = H(hh);
+        need(hh->live_plans == 0, "the handle still has plans; destroy them first");
         DeviceGuard g(h.device);
         cudaStreamSynchronize(h.stream);
         cudaFree(h.d_err);

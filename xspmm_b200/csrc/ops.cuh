@@ -24,6 +24,27 @@ void bcsr_spmm_tc(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* r
                   const __half* vals, const __half* B, float* C, int64_t M, int64_t K, int64_t N,
                   const IT* map);
 
+// What the tcgen05 kernel derives from A once: per group of 8 block rows the union of block
+// columns (gptr/gcol) and the stacked A tiles packed 128 x 16 per union entry, with their TMA map.
+struct TcPrep {
+    int64_t ngroups = 0, bound = 0;
+    DevBuf<int64_t> gptr;
+    DevBuf<int32_t> gcol;
+    DevBuf<__half> apk;  // 4 KB per union entry, laid out as the MMA reads it from shared memory
+};
+template <typename IT>
+void tc_prepare(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
+                const __half* vals, TcPrep& out);
+template <typename IT>
+void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M, int64_t K,
+                int64_t N, const IT* map);
+bool tc_preferred(int64_t nbr, int64_t nbc, int64_t nnzb);
+
+// The mma.sync Tier-1 kernel, without the automatic choice of tcgen05.
+template <typename IT>
+void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
+                       const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map);
+
 // Which Tier-1 fp16 kernel runs: the handle's setting (xspmm_set_tier1_kernel) if not auto, else
 // the environment XSPMM_TIER1_KERNEL = mma | tc | auto (default auto).
 enum class Tier1Kernel { Auto, Mma, Tc };
@@ -78,6 +99,7 @@ void spmm_csr_pipeline(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* r
 struct xspmm_handle_s {
     xspmm_b200::Handle h;
     bool destroyed = false;
+    int live_plans = 0;  // plans built on this handle and not yet destroyed
 };
 
 namespace xspmm_b200 {

@@ -1,4 +1,5 @@
-// pipeline.cu -- Tier-2: C = A * B for a CSR matrix A, with optional row clustering.
+// pipeline.cu -- Tier-2: C = A * B for a CSR matrix A, with optional row clustering, and the
+// plan that keeps the stages' results for repeated products.
 //
 // Same stages as the reference pipeline (src/cuda/unstructured_mtx_mul.cu:56-130):
 //   clustering (tau = 0.5, block width = hw_block_size, :83) -> row permutation (:88) ->
@@ -11,55 +12,125 @@
 //   * every stage runs on the device (the reference pulls A to the host for clustering and
 //     conversion, clustering_sylos_labini.cpp:70-73, conversion.cpp:22-26).
 // Timings are CUDA events on the handle's stream, read once at the end when requested.
-#include "ops.cuh"
+#include "plan.cuh"
 
 namespace xspmm_b200 {
+
+bool plan_wants_tc(const Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb) {
+    const Tier1Kernel choice = tier1_kernel_choice(h);
+    if (choice == Tier1Kernel::Mma || nbr == 0 || nbc == 0 || nnzb == 0) return false;
+    return choice == Tier1Kernel::Tc || tc_preferred(nbr, nbc, nnzb);
+}
+
+template <typename VT, typename IT>
+void plan_from_csr(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
+                   const IT* col_ind, const VT* values, int64_t hw, bool clustering, bool mark,
+                   Plan<VT, IT>& out) {
+    XS_REQUIRE(hw == 16, XSPMM_STATUS_UNSUPPORTED,
+               "hw_block_size must be 16 (the tensor-core block size)");
+    cudaStream_t s = h.stream;
+    auto ev = [&](int i) {
+        if (mark) XS_CHECK_CUDA(cudaEventRecord(h.ev[i], s));
+    };
+    out.M = M;
+    out.K = K;
+    out.value_bytes = (int)sizeof(VT);
+    ev(0);
+    const IT* arp = row_ptr;
+    const IT* aci = col_ind;
+    const VT* av = values;
+    DevBuf<IT> prp, pci;
+    DevBuf<VT> pv;
+    if (clustering && M > 0) {
+        out.perm = DevBuf<IT>(M, s);
+        cluster_jaccard<IT>(h, M, K, nnz, row_ptr, col_ind, 0.5f, hw, out.perm.get());
+        ev(1);
+        prp = DevBuf<IT>(M + 1, s);
+        pci = DevBuf<IT>(std::max<int64_t>(nnz, 1), s);
+        pv = DevBuf<VT>(std::max<int64_t>(nnz, 1), s);
+        permute_rows<VT, IT>(h, M, nnz, row_ptr, col_ind, values, out.perm.get(), prp.get(),
+                             pci.get(), pv.get(), false);
+        ev(2);
+        arp = prp.get();
+        aci = pci.get();
+        av = pv.get();
+        out.clustered = true;
+    } else {
+        ev(1);
+        ev(2);
+    }
+    out.nbr = ceil_div(M, 16);
+    out.nbc = ceil_div(K, 16);
+    out.brp = DevBuf<IT>(out.nbr + 1, s);
+    out.nnzb = csr_to_bcsr_count<IT>(h, M, K, nnz, arp, aci, 16, 16, out.brp.get());
+    out.bci = DevBuf<IT>(std::max<int64_t>(out.nnzb, 1), s);
+    out.bv = DevBuf<VT>(std::max<int64_t>(out.nnzb, 1) * 256, s);
+    csr_to_bcsr_fill<VT, IT>(h, M, K, nnz, arp, aci, av, 16, 16, out.brp.get(), out.bci.get(),
+                             out.bv.get());
+    ev(3);
+    out.rp = out.brp.get();
+    out.ci = out.bci.get();
+    out.v = out.bv.get();
+}
+
+template <typename VT, typename IT>
+void plan_from_bcsr(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* row_ptr,
+                    const IT* col_ind, const VT* values, int64_t M, int64_t K,
+                    Plan<VT, IT>& out) {
+    (void)h;
+    out.M = M;
+    out.K = K;
+    out.nbr = nbr;
+    out.nbc = nbc;
+    out.nnzb = nnzb;
+    out.value_bytes = (int)sizeof(VT);
+    out.rp = row_ptr;
+    out.ci = col_ind;
+    out.v = values;
+}
+
+template <typename VT, typename IT>
+void Plan<VT, IT>::prepare_tc(Handle& h) {
+    if constexpr (std::is_same<VT, __half>::value) {
+        if (tc_built || nbr == 0 || nbc == 0 || nnzb == 0) return;
+        XS_REQUIRE(nnzb * 16 < (int64_t(1) << 31) && nbc * 16 < (int64_t(1) << 31) &&
+                       reinterpret_cast<uintptr_t>(v) % 16 == 0,
+                   XSPMM_STATUS_UNSUPPORTED, "matrix not supported by the tcgen05 kernel");
+        tc_prepare<IT>(h, nbr, nbc, nnzb, rp, ci, v, tc);
+        tc_built = true;
+    } else {
+        (void)h;
+    }
+}
+
+template <typename VT, typename IT>
+void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
+    if (M == 0 || N == 0) return;
+    const VT* B = static_cast<const VT*>(Bv);
+    const IT* map = clustered ? perm.get() : nullptr;
+    if constexpr (std::is_same<VT, __half>::value) {
+        if (plan_wants_tc(h, nbr, nbc, nnzb) && tc_supported(nbr, nbc, nnzb, v, B, C, N)) {
+            prepare_tc(h);
+            tc_execute<IT>(h, tc, B, C, M, K, N, map);
+            return;
+        }
+        bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+    } else {
+        bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
+    }
+}
 
 template <typename VT, typename IT>
 void spmm_csr_pipeline(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
                        const IT* col_ind, const VT* values, const VT* B, float* C, int64_t N,
                        int64_t hw, bool clustering, xspmm_timings_t* timings) {
-    XS_REQUIRE(hw == 16, XSPMM_STATUS_UNSUPPORTED,
-               "hw_block_size must be 16 (the tensor-core block size)");
-    cudaStream_t s = h.stream;
-    cudaEvent_t* ev = h.ev;
-    auto mark = [&](int i) {
-        if (timings) XS_CHECK_CUDA(cudaEventRecord(ev[i], s));
-    };
-    mark(0);
-    const IT* arp = row_ptr;
-    const IT* aci = col_ind;
-    const VT* av = values;
-    DevBuf<IT> perm, prp, pci;
-    DevBuf<VT> pv;
-    if (clustering && M > 0) {
-        perm = DevBuf<IT>(M, s);
-        cluster_jaccard<IT>(h, M, K, nnz, row_ptr, col_ind, 0.5f, hw, perm.get());
-        mark(1);
-        prp = DevBuf<IT>(M + 1, s);
-        pci = DevBuf<IT>(std::max<int64_t>(nnz, 1), s);
-        pv = DevBuf<VT>(std::max<int64_t>(nnz, 1), s);
-        permute_rows<VT, IT>(h, M, nnz, row_ptr, col_ind, values, perm.get(), prp.get(), pci.get(),
-                             pv.get(), false);
-        mark(2);
-        arp = prp.get();
-        aci = pci.get();
-        av = pv.get();
-    } else {
-        mark(1);
-        mark(2);
-    }
-    const int64_t nbr = ceil_div(M, 16), nbc = ceil_div(K, 16);
-    DevBuf<IT> brp(nbr + 1, s);
-    const int64_t nnzb = csr_to_bcsr_count<IT>(h, M, K, nnz, arp, aci, 16, 16, brp.get());
-    DevBuf<IT> bci(std::max<int64_t>(nnzb, 1), s);
-    DevBuf<VT> bv(std::max<int64_t>(nnzb, 1) * 256, s);
-    csr_to_bcsr_fill<VT, IT>(h, M, K, nnz, arp, aci, av, 16, 16, brp.get(), bci.get(), bv.get());
-    mark(3);
-    bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, brp.get(), bci.get(), bv.get(), B, C, M, K, N,
-                      (clustering && M > 0) ? perm.get() : nullptr);
-    mark(4);
+    Plan<VT, IT> plan;
+    plan_from_csr<VT, IT>(h, M, K, nnz, row_ptr, col_ind, values, hw, clustering,
+                          timings != nullptr, plan);
+    plan.execute(h, B, C, N);
     if (timings) {
+        cudaEvent_t* ev = h.ev;
+        XS_CHECK_CUDA(cudaEventRecord(ev[4], h.stream));
         XS_CHECK_CUDA(cudaEventSynchronize(ev[4]));
         float t[4];
         for (int i = 0; i < 4; ++i) XS_CHECK_CUDA(cudaEventElapsedTime(&t[i], ev[i], ev[i + 1]));
@@ -75,6 +146,11 @@ void spmm_csr_pipeline(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* r
 }
 
 #define XS_INST_PIPE(VT, IT)                                                                      \
+    template struct Plan<VT, IT>;                                                                 \
+    template void plan_from_csr<VT, IT>(Handle&, int64_t, int64_t, int64_t, const IT*, const IT*, \
+                                        const VT*, int64_t, bool, bool, Plan<VT, IT>&);           \
+    template void plan_from_bcsr<VT, IT>(Handle&, int64_t, int64_t, int64_t, const IT*,           \
+                                         const IT*, const VT*, int64_t, int64_t, Plan<VT, IT>&);  \
     template void spmm_csr_pipeline<VT, IT>(Handle&, int64_t, int64_t, int64_t, const IT*,        \
                                             const IT*, const VT*, const VT*, float*, int64_t,     \
                                             int64_t, bool, xspmm_timings_t*);

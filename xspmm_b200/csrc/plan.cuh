@@ -1,0 +1,82 @@
+// plan.cuh -- what the SpMM derives from A once, kept on the device for repeated products.
+//
+// The reference recomputes clustering, permutation and CSR->BCSR on every Tier-2 call
+// (src/cuda/unstructured_mtx_mul.cu:56-130) and leaves reuse to callers of Tier 1 (README.md:127,
+// "amortizing clustering time over thousands of iterations"). A plan holds the result of those
+// stages -- the clustering permutation, the permuted BCSR matrix and, for the tcgen05 kernel, the
+// stacked 128 x 16 A tiles -- so that each product afterwards is the Tier-1 kernel alone.
+// The Tier-2 entry point builds a plan, executes it once and drops it.
+#pragma once
+#include <memory>
+#include <type_traits>
+
+#include "ops.cuh"
+
+namespace xspmm_b200 {
+
+struct PlanBase {
+    int64_t M = 0, K = 0, nbr = 0, nbc = 0, nnzb = 0;
+    bool clustered = false;
+    int value_bytes = 0;
+    virtual ~PlanBase() = default;
+    // C (M x N, fp32, row-major) = A * B (K x N, row-major, the plan's value type), rows of C in
+    // the caller's order.
+    virtual void execute(Handle& h, const void* B, float* C, int64_t N) = 0;
+    // Builds what the tcgen05 kernel needs now instead of at the first product that takes it.
+    virtual void prepare_tc(Handle& h) = 0;
+    virtual bool tc_ready() const = 0;
+    virtual int64_t tc_tiles() const = 0;
+    virtual int64_t device_bytes() const = 0;
+    virtual void rebind_stream(cudaStream_t s) = 0;
+};
+
+template <typename VT, typename IT>
+struct Plan final : PlanBase {
+    DevBuf<IT> perm, brp, bci;  // owned when built from CSR
+    DevBuf<VT> bv;
+    const IT* rp = nullptr;     // the BCSR arrays the product reads (owned or the caller's)
+    const IT* ci = nullptr;
+    const VT* v = nullptr;
+    TcPrep tc;
+    bool tc_built = false;
+
+    void execute(Handle& h, const void* B, float* C, int64_t N) override;
+    void prepare_tc(Handle& h) override;
+    bool tc_ready() const override { return tc_built; }
+    int64_t tc_tiles() const override { return tc_built ? tc.bound : 0; }
+    int64_t device_bytes() const override {
+        return (int64_t)(perm.n + brp.n + bci.n) * (int64_t)sizeof(IT) +
+               (int64_t)bv.n * (int64_t)sizeof(VT) +
+               (int64_t)(tc.gptr.n * sizeof(int64_t) + tc.gcol.n * sizeof(int32_t) +
+                         tc.apk.n * sizeof(__half));
+    }
+    void rebind_stream(cudaStream_t s) override {
+        perm.s = brp.s = bci.s = s;
+        bv.s = s;
+        tc.gptr.s = s;
+        tc.gcol.s = s;
+        tc.apk.s = s;
+    }
+};
+
+// Stage events: ev[first] before clustering, ev[first+1] after it, ev[first+2] after the
+// permutation, ev[first+3] after the conversion (recorded only when mark is true).
+template <typename VT, typename IT>
+void plan_from_csr(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
+                   const IT* col_ind, const VT* values, int64_t hw, bool clustering, bool mark,
+                   Plan<VT, IT>& out);
+
+template <typename VT, typename IT>
+void plan_from_bcsr(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* row_ptr,
+                    const IT* col_ind, const VT* values, int64_t M, int64_t K, Plan<VT, IT>& out);
+
+// Whether the automatic Tier-1 choice (or the handle's forced kernel) would take tcgen05 for
+// this matrix at some N.
+bool plan_wants_tc(const Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb);
+
+}  // namespace xspmm_b200
+
+struct xspmm_plan_s {
+    xspmm_handle_s* owner = nullptr;
+    std::unique_ptr<xspmm_b200::PlanBase> p;
+};

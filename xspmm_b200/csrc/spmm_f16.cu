@@ -222,7 +222,7 @@ Tier1Kernel tier1_kernel_choice(const Handle& h) {
 
 // tcgen05 stacks 8 block rows per MMA over the union of their block columns, so it pays when the
 // block grid is dense (little zero padding) and block rows are long (B tiles reused 8 times).
-static bool tc_preferred(int64_t nbr, int64_t nbc, int64_t nnzb) {
+bool tc_preferred(int64_t nbr, int64_t nbc, int64_t nnzb) {
     const double density = (double)nnzb / ((double)nbr * (double)nbc);
     return density >= 0.25 && nnzb >= 32 * nbr;
 }
@@ -238,6 +238,13 @@ static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb
         bcsr_spmm_tc<IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
         return;
     }
+    bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+}
+
+template <typename IT>
+void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
+                       const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map) {
+    if (nbr == 0 || N == 0 || M == 0) return;
     XS_REQUIRE(ceil_div(N, 64) <= 65535, XSPMM_STATUS_UNSUPPORTED, "N above 4,194,240 columns");
     const bool aligned = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(v) % 16 == 0) &&
@@ -253,6 +260,13 @@ static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb
         else launch<IT, 4, false>(h, nbr, rp, ci, v, B, C, M, K, N, map);
     }
 }
+
+template void bcsr_spmm_mma_f16<int32_t>(Handle&, int64_t, const int32_t*, const int32_t*,
+                                         const __half*, const __half*, float*, int64_t, int64_t,
+                                         int64_t, const int32_t*);
+template void bcsr_spmm_mma_f16<int64_t>(Handle&, int64_t, const int64_t*, const int64_t*,
+                                         const __half*, const __half*, float*, int64_t, int64_t,
+                                         int64_t, const int64_t*);
 
 template <>
 void bcsr_spmm<__half, int32_t>(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb,

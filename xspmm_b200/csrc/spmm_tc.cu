@@ -16,16 +16,19 @@
 // dispatcher only picks this kernel for dense block structure.
 //
 // Before the MMA kernel, the 8 blocks of every union entry are packed into one contiguous
-// 128 x 16 tile (zeros for missing blocks), so a stage is two TMA requests. Roles (192 threads):
-// warp 0 lane 0 issues the TMA loads of a stage (the packed A tile through a SWIZZLE_32B map ->
-// K-major canonical layout; the B slab as one 3-D box or four 64-column SWIZZLE_128B boxes ->
-// MN-major canonical layout); warp 1 lane 0 issues tcgen05.mma and
-// tcgen05.commit (which frees the stage when the MMA has read it); warps 2..5 wait for the
-// accumulator, read TMEM with tcgen05.ld (warp w reads lanes 32*(w%4)..+31) and store rows of C
-// (through the optional row map, so the Tier-2 unpermute stays fused). When the grid would be
+// 128 x 16 tile (zeros for missing blocks), already in the shared-memory image of the K-major
+// SWIZZLE_32B canonical layout, so a stage is two requests: the A tile as one 4 KB bulk copy (a
+// tensor map with 32-byte rows would split it into 128 requests) and the B slab as one 3-D box
+// or four 64-column SWIZZLE_128B boxes (MN-major canonical layout). Roles (160 threads, two CTAs
+// per SM): warp 0 allocates TMEM and its lane 0 issues tcgen05.mma and tcgen05.commit (which
+// frees a stage once the MMA has read it); warps 1..4 are four producers taking the stages in
+// turn (one issuing thread cannot keep the tensor pipe busy with 12 KB stages; four can), and
+// afterwards the epilogue: each waits for the accumulator, reads its TMEM lane quarter
+// (warp % 4) with tcgen05.ld and stores rows of C (through the optional row map, so the Tier-2
+// unpermute stays fused). When the grid would be
 // smaller than the GPU, the union list is split across CTAs (split-K) and a second kernel sums the
 // partial tiles in a fixed order. Every mbarrier wait is bounded; a timeout sets an error flag and
-// the CTA still waits (bounded) for its own TMA loads before freeing TMEM and exiting.
+// the CTA still waits (bounded) for its own loads before freeing TMEM and exiting.
 #include "ops.cuh"
 #include "blockcols.cuh"
 
@@ -46,10 +49,13 @@ constexpr int A_STAGE = TC_GROUP * 512;            // 4 KB
 constexpr int B_BOX = 16 * 128;                    // 16 rows x 64 fp16 = 2 KB
 constexpr int B_STAGE = (TC_BN / 64) * B_BOX;      // 8 KB
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE;     // 12 KB (multiple of 1024)
-constexpr int TC_THREADS = 192;
+constexpr int TC_PRODUCERS = 4;                   // warps 1..4 issue loads, then store C
+constexpr int TC_THREADS = 32 * (1 + TC_PRODUCERS);
+static_assert(TC_STAGES % TC_PRODUCERS == 0, "each producer owns fixed stage slots");
 constexpr int TMEM_COLS = 256;
 constexpr long long WAIT_LIMIT = 1ll << 22;        // polls of an mbarrier before giving up
 constexpr size_t TC_SMEM = (size_t)TC_STAGES * STAGE_BYTES + 1024 + 256;
+static_assert(2 * TC_STAGES * 8 + 8 + 4 + 4 * TC_PRODUCERS <= 256, "barrier area");
 
 // ---- PTX wrappers ---------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -98,6 +104,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+// Plain bulk copy (no tensor map): size and both addresses multiples of 16 bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
@@ -157,7 +172,7 @@ constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 16) | ((uint32_t)(TC_BN >> 3) <
 // ---- the kernel -----------------------------------------------------------------------------------
 template <typename IT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-bcsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUtensorMap tmB,
                     const int64_t* __restrict__ gptr, const int32_t* __restrict__ gcol,
                     float* __restrict__ out, const IT* __restrict__ row_map, int64_t M,
                     int64_t N, int64_t m_pad, int splits, int ntiles, int b3d,
@@ -169,7 +184,7 @@ bcsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     uint64_t* empty = full + TC_STAGES;
     uint64_t* accum = empty + TC_STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-    int* issued_slot = reinterpret_cast<int*>(tmem_slot + 1);
+    int* issued_slot = reinterpret_cast<int*>(tmem_slot + 1);  // per producer
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int bid = blockIdx.x;
@@ -188,8 +203,9 @@ bcsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
-        *issued_slot = 0;
+        for (int p = 0; p < TC_PRODUCERS; ++p) issued_slot[p] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -204,16 +220,35 @@ bcsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // TMA producer: per stage one 4 KB packed A tile (union entry u = 128 rows x 16) and the
-        // 16 x 256 B slab (one 3-D box when N % 64 == 0, else four 64-column boxes). The warp
-        // loads 32 stages' union columns at once so lane 0 never waits on a global load between
-        // issues.
-        int i = 0;
+        if (lane == 0) {  // MMA issuer
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % TC_STAGES;
+                if (!mbar_wait(&full[s], (i / TC_STAGES) & 1, err)) break;
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+                tc_mma(tmem, desc_a(sa), desc_b(sa + A_STAGE), TC_IDESC, i > 0 ? 1u : 0u);
+                tc_commit(&empty[s]);
+            }
+            // commit even after a timeout: it arrives only once the MMAs already issued are
+            // done, so TMEM is never read or freed under them
+            if (nk > 0) tc_commit(accum);
+            else mbar_arrive(accum);
+        }
+    } else {
+        // Warps 1..4: loads, then the epilogue. Producer p issues the stages i = p (mod 4), so it
+        // alone refills the slots s = p (mod 4) (the stage count is a multiple of 4) and its
+        // waits on them stay in phase order. A single issuing thread cannot keep the tensor pipe
+        // fed with 12 KB stages; four can. Per stage: one 4 KB bulk copy of the packed A tile
+        // and the 16 x 256 B slab (one 3-D box when N % 64 == 0, else four 64-column boxes).
+        const int p = warp - 1;
+        int issued = 0;
         bool stop = false;
-        for (int c = 0; c < nk && !stop; c += 32) {
-            const int col = c + lane < nk ? gcol[k0 + c + lane] : 0;
-            const int cnt = min(32, nk - c);
+        for (int c = p; c < nk && !stop; c += 32 * TC_PRODUCERS) {
+            const int ic = c + lane * TC_PRODUCERS;
+            const int col = ic < nk ? gcol[k0 + ic] : 0;
+            const int cnt = min(32, (nk - c + TC_PRODUCERS - 1) / TC_PRODUCERS);
             for (int t = 0; t < cnt; ++t) {
+                const int i = c + t * TC_PRODUCERS;
                 const int colt = __shfl_sync(0xffffffffu, col, t);
                 int ok = 1;
                 if (lane == 0) {
@@ -224,7 +259,7 @@ bcsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         mbar_expect_tx(&full[s], STAGE_BYTES);
                         uint8_t* sA = smem + s * STAGE_BYTES;
                         uint8_t* sB = sA + A_STAGE;
-                        tma_load_2d(sA, &tmA, 0, (int)((k0 + i) * 128), &full[s]);
+                        bulk_load(sA, apk + (k0 + i) * (A_STAGE / 2), A_STAGE, &full[s]);
                         if (b3d) {
                             tma_load_3d(sB, &tmB, 0, colt * 16, n0 / 64, &full[s]);
                         } else {
@@ -238,34 +273,15 @@ bcsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     stop = true;
                     break;
                 }
-                ++i;
+                ++issued;
             }
         }
-        if (lane == 0) *issued_slot = i;
-    } else if (warp == 1) {
-        if (lane == 0) {  // MMA issuer
-            bool ok = true;
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % TC_STAGES;
-                if (!mbar_wait(&full[s], (i / TC_STAGES) & 1, err)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-                tc_mma(tmem, desc_a(sa), desc_b(sa + A_STAGE), TC_IDESC, i > 0 ? 1u : 0u);
-                tc_commit(&empty[s]);
-            }
-            // commit even after a timeout: it arrives only once the MMAs already issued are
-            // done, so TMEM is never read or freed under them
-            if (nk > 0) tc_commit(accum);
-            else mbar_arrive(accum);
-            (void)ok;
-        }
-    } else {  // epilogue warps 2..5
+        if (lane == 0) issued_slot[p] = issued;
+
+        // epilogue: TMEM lane quarter warp % 4 -> rows of C
         const bool have = mbar_wait(accum, 0, err);
         tc_fence_after();
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int q = warp & 3;
         const int64_t grow = (int64_t)g * 128 + q * 32 + lane;
         float* dst = nullptr;
         if (grow < M) {
@@ -302,19 +318,17 @@ bcsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 }
             }
         }
+        if (lane == 0) {  // never leave a load of ours in flight behind us (bounded waits)
+            const int last = p + (issued - 1) * TC_PRODUCERS;
+            for (int j = 0; j < issued; ++j) {
+                const int i = p + j * TC_PRODUCERS;
+                if (i + TC_STAGES > last) mbar_wait(&full[i % TC_STAGES], (i / TC_STAGES) & 1, err);
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
-        if (lane == 0) {  // never leave a TMA load in flight behind us
-            const int issued = *issued_slot;
-            for (int i = 0; i < issued; ++i) {
-                const int s = i % TC_STAGES;
-                // the last completed phase of stage s: wait with its parity (bounded)
-                if (i + TC_STAGES >= issued) mbar_wait(&full[s], (i / TC_STAGES) & 1, err);
-            }
-        }
-        __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(TMEM_COLS)
@@ -354,12 +368,15 @@ __global__ void tc_pack_kernel(const int64_t* __restrict__ gptr, int64_t ngroups
     for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < total;
          c += (int64_t)gridDim.x * blockDim.x) {
         const int64_t u = c >> 8;
-        const int within = (int)(c & 255);  // 16 row-pairs... chunk index inside the 4 KB tile
+        const int within = (int)(c & 255);  // 16-byte chunk of the tile: row within>>1, half within&1
         const int b = within >> 5;          // block slot (32 chunks of 16 B per block)
         const int blk = gblk[u * TC_GROUP + b];
         uint4 v = make_uint4(0, 0, 0, 0);
         if (blk >= 0) v = reinterpret_cast<const uint4*>(vals + (int64_t)blk * 256)[within & 31];
-        reinterpret_cast<uint4*>(apk + u * 2048)[within] = v;
+        // stored as a SWIZZLE_32B TMA load would leave it in shared memory (16-byte half h of row
+        // r at r * 32 + ((h ^ ((r >> 2) & 1)) * 16)), so one plain bulk copy stages the tile
+        const int r = within >> 1, h = within & 1;
+        reinterpret_cast<uint4*>(apk + u * 2048)[(r << 1) | (h ^ ((r >> 2) & 1))] = v;
     }
 }
 
@@ -562,43 +579,48 @@ bool tc_supported(int64_t nbr, int64_t nbc, int64_t nnzb, const void* vals, cons
 }
 
 template <typename IT>
-void bcsr_spmm_tc(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
-                  const __half* vals, const __half* B, float* C, int64_t M, int64_t K, int64_t N,
-                  const IT* map) {
+void tc_prepare(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
+                const __half* vals, TcPrep& out) {
     cudaStream_t s = h.stream;
     const int64_t ngroups = ceil_div(nbr, TC_GROUP);
     const int64_t bound = std::min(nnzb, ngroups * nbc);  // union entries, upper bound
-    DevBuf<int64_t> gptr(ngroups + 1, s);
-    DevBuf<int32_t> gcol(std::max<int64_t>(bound, 1), s), gblk(std::max<int64_t>(bound, 1) * TC_GROUP, s);
+    XS_REQUIRE(bound * 128 < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "union too large");
+    out.ngroups = ngroups;
+    out.bound = bound;
+    out.gptr = DevBuf<int64_t>(ngroups + 1, s);
+    out.gcol = DevBuf<int32_t>(std::max<int64_t>(bound, 1), s);
+    DevBuf<int32_t> gblk(std::max<int64_t>(bound, 1) * TC_GROUP, s);
     XS_CHECK_CUDA(cudaMemsetAsync(gblk.get(), 0xFF, gblk.n * sizeof(int32_t), s));
     tc_group_count_kernel<IT><<<gp_grid(h, ngroups), GP_THREADS, 0, s>>>(rp, ci, nbr, ngroups,
-                                                                        gptr.get());
+                                                                        out.gptr.get());
     after_launch(h, "tc_group_count");
-    exclusive_scan<int64_t>(h, gptr.get(), gptr.get(), ngroups);
+    exclusive_scan<int64_t>(h, out.gptr.get(), out.gptr.get(), ngroups);
     tc_group_fill_kernel<IT><<<gp_grid(h, ngroups), GP_THREADS, 0, s>>>(
-        rp, ci, nbr, ngroups, gptr.get(), gcol.get(), gblk.get());
+        rp, ci, nbr, ngroups, out.gptr.get(), out.gcol.get(), gblk.get());
     after_launch(h, "tc_group_fill");
+    out.apk = DevBuf<__half>((size_t)std::max<int64_t>(bound, 1) * 2048, s);
+    const unsigned grid = (unsigned)std::max<int64_t>(
+        1, std::min(ceil_div(bound * 256, 256), (int64_t)sm_count(h.device) * 16));
+    tc_pack_kernel<<<grid, 256, 0, s>>>(out.gptr.get(), ngroups, gblk.get(), vals, out.apk.get(),
+                                        bound);
+    after_launch(h, "tc_pack");
+}
 
+template <typename IT>
+void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M, int64_t K,
+                int64_t N, const IT* map) {
+    cudaStream_t s = h.stream;
     const int ntiles = (int)ceil_div(N, TC_BN);
-    const int64_t tiles = ngroups * ntiles;
+    const int64_t tiles = p.ngroups * ntiles;
     const int64_t slots = (int64_t)sm_count(h.device) * 2;
-    const int64_t avg_union = std::max<int64_t>(1, bound / ngroups);
+    const int64_t avg_union = std::max<int64_t>(1, p.bound / p.ngroups);
     int splits = 1;
-    if (tiles < slots) splits = (int)std::min<int64_t>({ceil_div(slots, tiles), 16, std::max<int64_t>(1, avg_union / 32)});
+    if (tiles < slots)  // fill the GPU once (never a partial second wave)
+        splits = (int)std::max<int64_t>(
+            1, std::min<int64_t>({slots / tiles, 16, std::max<int64_t>(1, avg_union / 32)}));
     XS_REQUIRE(tiles * splits < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "grid too large");
-    const int64_t m_pad = ngroups * 128;
+    const int64_t m_pad = p.ngroups * 128;
     DevBuf<float> part(splits > 1 ? (size_t)(splits * m_pad * N) : 0, s);
-
-    XS_REQUIRE(bound * 128 < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "union too large");
-    DevBuf<__half> apk((size_t)std::max<int64_t>(bound, 1) * 2048, s);
-    {
-        const unsigned grid = (unsigned)std::max<int64_t>(
-            1, std::min(ceil_div(bound * 256, 256), (int64_t)sm_count(h.device) * 16));
-        tc_pack_kernel<<<grid, 256, 0, s>>>(gptr.get(), ngroups, gblk.get(), vals, apk.get(), bound);
-        after_launch(h, "tc_pack");
-    }
-    const CUtensorMap tmA = make_map_2d(apk.get(), 16, (uint64_t)std::max<int64_t>(bound, 1) * 128,
-                                        32, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B);
     int b3d = 0;
     CUtensorMap tmB;
     if (N % 64 == 0 && make_map_b3d(B, N, K, &tmB)) {
@@ -610,22 +632,36 @@ void bcsr_spmm_tc(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* r
     auto kern = bcsr_spmm_tc_kernel<IT>;
     XS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
     kern<<<(unsigned)(tiles * splits), TC_THREADS, TC_SMEM, s>>>(
-        tmA, tmB, gptr.get(), gcol.get(), splits > 1 ? part.get() : C, map, M, N, m_pad, splits,
-        ntiles, b3d, h.d_err);
+        p.apk.get(), tmB, p.gptr.get(), p.gcol.get(), splits > 1 ? part.get() : C, map, M, N, m_pad,
+        splits, ntiles, b3d, h.d_err);
     after_launch(h, "bcsr_spmm_tc");
     if (splits > 1) {
         const int64_t work = ceil_div(M * N, 4);
-        const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(ceil_div(work, 256), (int64_t)sm_count(h.device) * 16));
+        const unsigned grid = (unsigned)std::max<int64_t>(
+            1, std::min(ceil_div(work, 256), (int64_t)sm_count(h.device) * 16));
         tc_reduce_kernel<IT><<<grid, 256, 0, s>>>(part.get(), C, map, M, N, m_pad, splits, h.d_err);
         after_launch(h, "tc_reduce");
     }
 }
 
-template void bcsr_spmm_tc<int32_t>(Handle&, int64_t, int64_t, int64_t, const int32_t*,
-                                    const int32_t*, const __half*, const __half*, float*, int64_t,
-                                    int64_t, int64_t, const int32_t*);
-template void bcsr_spmm_tc<int64_t>(Handle&, int64_t, int64_t, int64_t, const int64_t*,
-                                    const int64_t*, const __half*, const __half*, float*, int64_t,
-                                    int64_t, int64_t, const int64_t*);
+template <typename IT>
+void bcsr_spmm_tc(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
+                  const __half* vals, const __half* B, float* C, int64_t M, int64_t K, int64_t N,
+                  const IT* map) {
+    TcPrep p;
+    tc_prepare<IT>(h, nbr, nbc, nnzb, rp, ci, vals, p);
+    tc_execute<IT>(h, p, B, C, M, K, N, map);
+}
+
+#define XS_INST_TC(IT)                                                                            \
+    template void tc_prepare<IT>(Handle&, int64_t, int64_t, int64_t, const IT*, const IT*,        \
+                                 const __half*, TcPrep&);                                         \
+    template void tc_execute<IT>(Handle&, const TcPrep&, const __half*, float*, int64_t, int64_t, \
+                                 int64_t, const IT*);                                             \
+    template void bcsr_spmm_tc<IT>(Handle&, int64_t, int64_t, int64_t, const IT*, const IT*,      \
+                                   const __half*, const __half*, float*, int64_t, int64_t,        \
+                                   int64_t, const IT*);
+XS_INST_TC(int32_t)
+XS_INST_TC(int64_t)
 
 }  // namespace xspmm_b200
