@@ -6,7 +6,8 @@
 //
 // Mapping (block rows stacked to M = 128): a CTA owns a group of 8 consecutive block rows and a
 // 256-column tile of C. The group's block columns are merged into one sorted union list (the
-// "group plan", built on the device per call). For every union column u one MMA
+// "group plan", built on the device once per matrix by a plan, or per call by the stateless
+// Tier-1 entry point). For every union column u one MMA
 //   D[128 x 256] += A_u[128 x 16] . B[16u .. 16u+15, n0 .. n0+255]
 // is issued, where A_u stacks the 8 block rows' blocks at column u (zeros where a block row has
 // no block there). One B tile therefore feeds 8 block
@@ -17,18 +18,24 @@
 //
 // Before the MMA kernel, the 8 blocks of every union entry are packed into one contiguous
 // 128 x 16 tile (zeros for missing blocks), already in the shared-memory image of the K-major
-// SWIZZLE_32B canonical layout, so a stage is two requests: the A tile as one 4 KB bulk copy (a
-// tensor map with 32-byte rows would split it into 128 requests) and the B slab as one 3-D box
-// or four 64-column SWIZZLE_128B boxes (MN-major canonical layout). Roles (160 threads, two CTAs
-// per SM): warp 0 allocates TMEM and its lane 0 issues tcgen05.mma and tcgen05.commit (which
-// frees a stage once the MMA has read it); warps 1..4 are four producers taking the stages in
-// turn (one issuing thread cannot keep the tensor pipe busy with 12 KB stages; four can), and
-// afterwards the epilogue: each waits for the accumulator, reads its TMEM lane quarter
-// (warp % 4) with tcgen05.ld and stores rows of C (through the optional row map, so the Tier-2
-// unpermute stays fused). When the grid would be
-// smaller than the GPU, the union list is split across CTAs (split-K) and a second kernel sums the
-// partial tiles in a fixed order. Every mbarrier wait is bounded; a timeout sets an error flag and
-// the CTA still waits (bounded) for its own loads before freeing TMEM and exiting.
+// SWIZZLE_32B canonical layout, so one plain bulk copy stages it (a tensor map with 32-byte rows
+// would split it into 128 requests). A pipeline stage holds two union entries: their two A tiles
+// (one 8 KB bulk copy -- consecutive entries are adjacent) and their two 16 x 256 B slabs (one
+// 3-D box each when N % 64 == 0, else four 64-column SWIZZLE_128B boxes; MN-major canonical
+// layout). Two MMAs per stage share one tcgen05.commit: a commit after every 16-deep MMA leaves
+// the tensor pipe idle about half of the time.
+//
+// Roles (160 threads, two CTAs per SM): warp 0 allocates TMEM and its lane 0 issues tcgen05.mma
+// and tcgen05.commit (which frees a stage once its MMAs have read it); warps 1..4 are four
+// producers taking the stages in turn (one issuing thread cannot keep the tensor pipe busy),
+// and afterwards the epilogue: each reads its TMEM lane quarter (warp % 4) with tcgen05.ld.
+// A whole tile is stored to C directly, every lane one row, through the optional row map (so
+// the Tier-2 unpermute stays fused). When the grid would not fill the GPU, the union list is
+// split (split-K) over the CTAs of a thread-block cluster: each writes its partial tile to an
+// L2-resident workspace in a store-coalesced order, and after a cluster barrier each CTA sums
+// its share of the rows over the partials in rank order (deterministic) and stores them. Every
+// mbarrier wait is bounded; a timeout sets an error flag and the CTA still waits (bounded) for
+// its own loads before freeing TMEM and exiting.
 #include "ops.cuh"
 #include "blockcols.cuh"
 
@@ -44,18 +51,20 @@ namespace {
 
 constexpr int TC_GROUP = 8;                        // block rows per tile (M = 128)
 constexpr int TC_BN = 256;                         // columns per tile = the MMA's N
-constexpr int TC_STAGES = 8;
-constexpr int A_STAGE = TC_GROUP * 512;            // 4 KB
+constexpr int TC_KPS = 2;                          // union entries (MMAs) per stage
+constexpr int TC_STAGES = 4;
+constexpr int A_TILE = TC_GROUP * 512;             // 4 KB: one union entry's stacked A
 constexpr int B_BOX = 16 * 128;                    // 16 rows x 64 fp16 = 2 KB
-constexpr int B_STAGE = (TC_BN / 64) * B_BOX;      // 8 KB
-constexpr int STAGE_BYTES = A_STAGE + B_STAGE;     // 12 KB (multiple of 1024)
+constexpr int B_SLAB = (TC_BN / 64) * B_BOX;       // 8 KB: one union entry's B rows
+constexpr int A_STAGE = TC_KPS * A_TILE;           // 8 KB
+constexpr int STAGE_BYTES = TC_KPS * (A_TILE + B_SLAB);  // 24 KB (multiple of 1024)
 constexpr int TC_PRODUCERS = 4;                   // warps 1..4 issue loads, then store C
 constexpr int TC_THREADS = 32 * (1 + TC_PRODUCERS);
 static_assert(TC_STAGES % TC_PRODUCERS == 0, "each producer owns fixed stage slots");
 constexpr int TMEM_COLS = 256;
 constexpr long long WAIT_LIMIT = 1ll << 22;        // polls of an mbarrier before giving up
 constexpr size_t TC_SMEM = (size_t)TC_STAGES * STAGE_BYTES + 1024 + 256;
-static_assert(2 * TC_STAGES * 8 + 8 + 4 + 4 * TC_PRODUCERS <= 256, "barrier area");
+static_assert(2 * TC_STAGES * 8 + 8 + 4 <= 256, "barrier area");
 
 // ---- PTX wrappers ---------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -84,7 +93,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait: false (and the error flag) if the phase did not complete.
-__device__ bool mbar_wait(uint64_t* b, uint32_t parity, unsigned* err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, unsigned* err) {
     for (long long i = 0; i < WAIT_LIMIT; ++i)
         if (mbar_try_wait(b, parity)) return true;
     flag_error(err, DERR_TIMEOUT);
@@ -114,6 +123,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
             "r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+// Cluster-wide barrier (all threads of all CTAs of the cluster). Every path through the kernel
+// reaches each of these the same number of times after bounded work, so it always completes.
+__device__ __forceinline__ void cluster_sync_all() {
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -170,12 +186,57 @@ constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 16) | ((uint32_t)(TC_BN >> 3) <
                               ((uint32_t)(128 >> 4) << 24);
 
 // ---- the kernel -----------------------------------------------------------------------------------
+// Split-K reduction of one CTA's rows: C[map(g*128 + r0 + rr), n0 + 4*ce ..] = sum over the
+// S partials (rank order) of element (r0 + rr, ce), for the `total` = nr x nce items. Items are
+// taken B at a time per thread, with all their S loads issued before any is used.
+template <int SMAX, int B, typename IT>
+__device__ __forceinline__ void tc_reduce_rows(const float4* __restrict__ tile_ws,
+                                               float* __restrict__ C, const IT* __restrict__ row_map,
+                                               int g, int n0, int r0, int nr, int total, int64_t M,
+                                               int64_t N, unsigned* err, int S = SMAX) {
+#pragma unroll 1
+    for (int it0 = threadIdx.x; it0 < total; it0 += B * TC_THREADS) {
+        float4 acc[B];
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            const int it = it0 + u * TC_THREADS;
+            acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (it >= total) continue;
+            const int rr = it % nr, ce = it / nr;
+            float4 v[SMAX];
+#pragma unroll
+            for (int k = 0; k < SMAX; ++k)
+                if (k < S) v[k] = __ldcg(tile_ws + (size_t)k * 8192 + ce * 128 + r0 + rr);
+            acc[u] = v[0];
+#pragma unroll
+            for (int k = 1; k < SMAX; ++k)
+                if (k < S) {
+                    acc[u].x += v[k].x; acc[u].y += v[k].y; acc[u].z += v[k].z; acc[u].w += v[k].w;
+                }
+        }
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            const int it = it0 + u * TC_THREADS;
+            if (it >= total) continue;
+            const int rr = it % nr, ce = it / nr;
+            const int64_t grow = (int64_t)g * 128 + r0 + rr;
+            if (grow >= M) continue;
+            const int64_t orow = row_map ? (int64_t)row_map[grow] : grow;
+            if (orow < 0 || orow >= M) {
+                flag_error(err, DERR_PERM_OUT_OF_RANGE);
+                continue;
+            }
+            *reinterpret_cast<float4*>(C + orow * N + n0 + ce * 4) = acc[u];
+        }
+    }
+}
+
 template <typename IT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUtensorMap tmB,
                     const int64_t* __restrict__ gptr, const int32_t* __restrict__ gcol,
-                    float* __restrict__ out, const IT* __restrict__ row_map, int64_t M,
-                    int64_t N, int64_t m_pad, int splits, int ntiles, int b3d,
+                    float* __restrict__ C, const IT* __restrict__ row_map, int64_t M,
+                    int64_t N, int splits, int ntiles, int b3d, float4* __restrict__ ws,
                     unsigned* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -184,7 +245,6 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
     uint64_t* empty = full + TC_STAGES;
     uint64_t* accum = empty + TC_STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-    int* issued_slot = reinterpret_cast<int*>(tmem_slot + 1);  // per producer
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int bid = blockIdx.x;
@@ -203,7 +263,6 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
-        for (int p = 0; p < TC_PRODUCERS; ++p) issued_slot[p] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
     }
@@ -219,14 +278,24 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    bool have = false;  // the accumulator is complete (set by warps 1..4)
+    // Stage j holds union entries j*KPS .. j*KPS+KPS-1 (fewer in the last stage): one MMA each,
+    // and one commit per stage -- a commit after every 16-deep MMA leaves the tensor pipe idle
+    // about half the time.
+    const int nst = (nk + TC_KPS - 1) / TC_KPS;
     if (warp == 0) {
         if (lane == 0) {  // MMA issuer
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % TC_STAGES;
-                if (!mbar_wait(&full[s], (i / TC_STAGES) & 1, err)) break;
+            for (int j = 0; j < nst; ++j) {
+                const int s = j % TC_STAGES;
+                if (!mbar_wait(&full[s], (j / TC_STAGES) & 1, err)) break;
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-                tc_mma(tmem, desc_a(sa), desc_b(sa + A_STAGE), TC_IDESC, i > 0 ? 1u : 0u);
+                const int ne = min(TC_KPS, nk - j * TC_KPS);
+#pragma unroll
+                for (int kk = 0; kk < TC_KPS; ++kk)
+                    if (kk < ne)
+                        tc_mma(tmem, desc_a(sa + kk * A_TILE), desc_b(sa + A_STAGE + kk * B_SLAB),
+                               TC_IDESC, (j > 0 || kk > 0) ? 1u : 0u);
                 tc_commit(&empty[s]);
             }
             // commit even after a timeout: it arrives only once the MMAs already issued are
@@ -235,37 +304,49 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
             else mbar_arrive(accum);
         }
     } else {
-        // Warps 1..4: loads, then the epilogue. Producer p issues the stages i = p (mod 4), so it
+        // Warps 1..4: loads, then the epilogue. Producer p issues the stages j = p (mod 4), so it
         // alone refills the slots s = p (mod 4) (the stage count is a multiple of 4) and its
         // waits on them stay in phase order. A single issuing thread cannot keep the tensor pipe
-        // fed with 12 KB stages; four can. Per stage: one 4 KB bulk copy of the packed A tile
-        // and the 16 x 256 B slab (one 3-D box when N % 64 == 0, else four 64-column boxes).
+        // fed; four can. Per stage: one bulk copy of the stage's packed A tiles (consecutive in
+        // memory) and per entry the 16 x 256 B slab (one 3-D box when N % 64 == 0, else four
+        // 64-column boxes). The warp loads the union columns of 32 / KPS stages at once.
         const int p = warp - 1;
+        constexpr int SPC = 32 / TC_KPS;  // stages per prefetch chunk
         int issued = 0;
         bool stop = false;
-        for (int c = p; c < nk && !stop; c += 32 * TC_PRODUCERS) {
-            const int ic = c + lane * TC_PRODUCERS;
-            const int col = ic < nk ? gcol[k0 + ic] : 0;
-            const int cnt = min(32, (nk - c + TC_PRODUCERS - 1) / TC_PRODUCERS);
+        for (int c = p; c < nst && !stop; c += SPC * TC_PRODUCERS) {
+            const int e = (c + (lane / TC_KPS) * TC_PRODUCERS) * TC_KPS + lane % TC_KPS;
+            const int col = e < nk ? gcol[k0 + e] : 0;
+            const int cnt = min(SPC, (nst - c + TC_PRODUCERS - 1) / TC_PRODUCERS);
             for (int t = 0; t < cnt; ++t) {
-                const int i = c + t * TC_PRODUCERS;
-                const int colt = __shfl_sync(0xffffffffu, col, t);
+                const int j = c + t * TC_PRODUCERS;
+                int colt[TC_KPS];
+#pragma unroll
+                for (int kk = 0; kk < TC_KPS; ++kk)
+                    colt[kk] = __shfl_sync(0xffffffffu, col, t * TC_KPS + kk);
                 int ok = 1;
                 if (lane == 0) {
-                    const int s = i % TC_STAGES;
-                    if (i >= TC_STAGES && !mbar_wait(&empty[s], ((i / TC_STAGES) & 1) ^ 1, err)) {
+                    const int s = j % TC_STAGES;
+                    const int ne = min(TC_KPS, nk - j * TC_KPS);
+                    if (j >= TC_STAGES && !mbar_wait(&empty[s], ((j / TC_STAGES) & 1) ^ 1, err)) {
                         ok = 0;
                     } else {
-                        mbar_expect_tx(&full[s], STAGE_BYTES);
+                        mbar_expect_tx(&full[s], (uint32_t)(ne * (A_TILE + B_SLAB)));
                         uint8_t* sA = smem + s * STAGE_BYTES;
                         uint8_t* sB = sA + A_STAGE;
-                        bulk_load(sA, apk + (k0 + i) * (A_STAGE / 2), A_STAGE, &full[s]);
-                        if (b3d) {
-                            tma_load_3d(sB, &tmB, 0, colt * 16, n0 / 64, &full[s]);
-                        } else {
+                        bulk_load(sA, apk + (k0 + (int64_t)j * TC_KPS) * (A_TILE / 2),
+                                  (uint32_t)(ne * A_TILE), &full[s]);
 #pragma unroll
-                            for (int j = 0; j < TC_BN / 64; ++j)
-                                tma_load_2d(sB + j * B_BOX, &tmB, n0 + 64 * j, colt * 16, &full[s]);
+                        for (int kk = 0; kk < TC_KPS; ++kk) {
+                            if (kk >= ne) break;
+                            if (b3d) {
+                                tma_load_3d(sB + kk * B_SLAB, &tmB, 0, colt[kk] * 16, n0 / 64, &full[s]);
+                            } else {
+#pragma unroll
+                                for (int q = 0; q < TC_BN / 64; ++q)
+                                    tma_load_2d(sB + kk * B_SLAB + q * B_BOX, &tmB, n0 + 64 * q,
+                                                colt[kk] * 16, &full[s]);
+                            }
                         }
                     }
                 }
@@ -276,54 +357,103 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
                 ++issued;
             }
         }
-        if (lane == 0) issued_slot[p] = issued;
 
-        // epilogue: TMEM lane quarter warp % 4 -> rows of C
-        const bool have = mbar_wait(accum, 0, err);
+        // wait for the accumulator; then make sure none of this producer's loads is still in
+        // flight (bounded; they all completed unless a wait timed out) before the stage buffers
+        // are reused for the reduction
+        have = mbar_wait(accum, 0, err);
         tc_fence_after();
-        const int q = warp & 3;
-        const int64_t grow = (int64_t)g * 128 + q * 32 + lane;
-        float* dst = nullptr;
-        if (grow < M) {
-            if (splits > 1) {
-                dst = out + ((int64_t)split * m_pad + grow) * N;
-            } else {
-                const int64_t orow = row_map ? (int64_t)row_map[grow] : grow;
-                if (orow >= 0 && orow < M) dst = out + orow * N;
-                else flag_error(err, DERR_PERM_OUT_OF_RANGE);
+        if (issued > 0) {  // this producer's slots: its last STAGES/4 stages
+            const int last = p + (issued - 1) * TC_PRODUCERS;
+#pragma unroll
+            for (int t = 0; t < TC_STAGES / TC_PRODUCERS; ++t) {
+                const int j = last - t * TC_PRODUCERS;
+                if (j >= p) mbar_wait(&full[j % TC_STAGES], (j / TC_STAGES) & 1, err);
             }
         }
-#pragma unroll 1
-        for (int c0 = 0; c0 < TC_BN; c0 += 32) {
-            uint32_t v[32];
-            if (nk > 0 && have) {
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] = 0u;
+        __syncwarp();
+    }
+    __syncwarp();
+
+    if (splits == 1) {
+        // Epilogue of a whole tile: each epilogue warp reads its TMEM lane quarter (warp % 4),
+        // 32 columns at a time, and every lane stores its row (through the optional row map,
+        // so the Tier-2 unpermute stays fused).
+        if (warp >= 1) {
+            const int q = warp & 3;
+            const int64_t grow = (int64_t)g * 128 + q * 32 + lane;
+            float* dst = nullptr;
+            if (grow < M) {
+                const int64_t orow = row_map ? (int64_t)row_map[grow] : grow;
+                if (orow >= 0 && orow < M) dst = C + orow * N;
+                else flag_error(err, DERR_PERM_OUT_OF_RANGE);
             }
-            const int64_t col = (int64_t)n0 + c0;
-            if (dst && col < N) {
-                if (col + 32 <= N) {
-                    float4* d4 = reinterpret_cast<float4*>(dst + col);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        d4[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                                            __uint_as_float(v[4 * e + 2]),
-                                            __uint_as_float(v[4 * e + 3]));
+#pragma unroll 1
+            for (int c0 = 0; c0 < TC_BN && n0 + c0 < N; c0 += 32) {
+                uint32_t v[32];
+                if (nk > 0 && have) {
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (col + e < N) dst[col + e] = __uint_as_float(v[e]);
+                    for (int e = 0; e < 32; ++e) v[e] = 0u;
+                }
+                const int64_t col = (int64_t)n0 + c0;
+                if (dst) {
+                    if (col + 32 <= N) {
+                        float4* d4 = reinterpret_cast<float4*>(dst + col);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            d4[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                                __uint_as_float(v[4 * e + 2]),
+                                                __uint_as_float(v[4 * e + 3]));
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (col + e < N) dst[col + e] = __uint_as_float(v[e]);
+                    }
                 }
             }
         }
-        if (lane == 0) {  // never leave a load of ours in flight behind us (bounded waits)
-            const int last = p + (issued - 1) * TC_PRODUCERS;
-            for (int j = 0; j < issued; ++j) {
-                const int i = p + j * TC_PRODUCERS;
-                if (i + TC_STAGES > last) mbar_wait(&full[i % TC_STAGES], (i / TC_STAGES) & 1, err);
+    } else {
+        // Split tile: the `splits` CTAs of the cluster each hold a partial 128 x 256 sum. Each
+        // writes its partial to the workspace straight from TMEM, in the order [32-column chunk]
+        // [float4 e][row][4], so one warp store covers 32 consecutive rows' float4 e: 512
+        // contiguous bytes. After a cluster barrier (which publishes those stores to the
+        // cluster), CTA k adds rows [k*128/S, (k+1)*128/S) over the S partials in rank order (a
+        // fixed order: the result does not depend on timing) and stores them to C through the
+        // row map. The partials stay in L2.
+        const int S = splits;
+        const int tile = blockIdx.x / S;
+        float4* mine = ws + ((size_t)tile * S + split) * 8192;
+        if (warp >= 1) {
+            const int q = warp & 3;
+            const int row = q * 32 + lane;
+#pragma unroll 1
+            for (int ch = 0; ch < TC_BN / 32 && n0 + ch * 32 < N; ++ch) {
+                uint32_t v[32];
+                if (nk > 0 && have) {
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ch * 32), v);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) v[e] = 0u;
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    mine[(ch * 8 + e) * 128 + row] =
+                        make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                    __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
             }
+        }
+        cluster_sync_all();
+        {
+            // all 5 warps; up to 16 loads of 16 B in flight per thread (an L2 round trip each)
+            const int r0 = split * 128 / S, r1 = (split + 1) * 128 / S, nr = r1 - r0;
+            const int nce = (int)min((int64_t)(TC_BN / 4), (N - n0 + 3) / 4);  // float4 columns
+            const int total = nr * nce;
+            const float4* tile_ws = ws + (size_t)tile * S * 8192;
+            if (S == 2) tc_reduce_rows<2, 8>(tile_ws, C, row_map, g, n0, r0, nr, total, M, N, err);
+            else if (S <= 4) tc_reduce_rows<4, 4>(tile_ws, C, row_map, g, n0, r0, nr, total, M, N, err, S);
+            else tc_reduce_rows<8, 2>(tile_ws, C, row_map, g, n0, r0, nr, total, M, N, err, S);
         }
     }
     tc_fence_before();
@@ -333,29 +463,6 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(TMEM_COLS)
                      : "memory");
-    }
-}
-
-// C[map(row)] = sum over splits of the partial tiles, in split order.
-template <typename IT>
-__global__ void tc_reduce_kernel(const float* __restrict__ part, float* __restrict__ C,
-                                 const IT* __restrict__ row_map, int64_t M, int64_t N,
-                                 int64_t m_pad, int splits, unsigned* err) {
-    const int64_t total = M * N;
-    for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < total;
-         i += (int64_t)gridDim.x * blockDim.x * 4) {
-        const int64_t r = i / N, c = i % N;  // N % 8 == 0, so a float4 never straddles rows
-        float4 s = reinterpret_cast<const float4*>(part + r * N + c)[0];
-        for (int k = 1; k < splits; ++k) {
-            const float4 p = reinterpret_cast<const float4*>(part + ((int64_t)k * m_pad + r) * N + c)[0];
-            s.x += p.x; s.y += p.y; s.z += p.z; s.w += p.w;
-        }
-        const int64_t orow = row_map ? (int64_t)row_map[r] : r;
-        if (orow < 0 || orow >= M) {
-            flag_error(err, DERR_PERM_OUT_OF_RANGE);
-            continue;
-        }
-        reinterpret_cast<float4*>(C + orow * N + c)[0] = s;
     }
 }
 
@@ -578,6 +685,45 @@ bool tc_supported(int64_t nbr, int64_t nbc, int64_t nnzb, const void* vals, cons
            reinterpret_cast<uintptr_t>(B) % 16 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0;
 }
 
+// Stand-in with the SpMM kernel's block size and shared memory, for occupancy queries: the
+// runtime counts a kernel that allocates TMEM as one CTA per SM, but two of these CTAs (256 TMEM
+// columns each) do run side by side.
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_occupancy_stand_in(int* p) {
+    if (p) p[threadIdx.x] = 0;
+}
+
+// CTAs of the tcgen05 kernel resident at once when launched in clusters of `cs` (cached per
+// device and cluster size).
+int64_t tc_resident_ctas(int device, int cs) {
+    const void* kern = reinterpret_cast<const void*>(tc_occupancy_stand_in);
+    static std::mutex mu;
+    static int64_t cache[64][9] = {};
+    if (device < 0 || device >= 64 || cs < 1 || cs > 8) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache[device][cs] == 0) {
+        XS_CHECK_CUDA(cudaFuncSetAttribute(tc_occupancy_stand_in,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(cs * 64));
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = TC_SMEM;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)cs;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = -1;
+        }
+        cache[device][cs] = n > 0 ? (int64_t)n * cs : -1;
+    }
+    return cache[device][cs];
+}
+
 template <typename IT>
 void tc_prepare(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
                 const __half* vals, TcPrep& out) {
@@ -612,15 +758,27 @@ void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M
     cudaStream_t s = h.stream;
     const int ntiles = (int)ceil_div(N, TC_BN);
     const int64_t tiles = p.ngroups * ntiles;
-    const int64_t slots = (int64_t)sm_count(h.device) * 2;
+    auto kern = bcsr_spmm_tc_kernel<IT>;
+    XS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
     const int64_t avg_union = std::max<int64_t>(1, p.bound / p.ngroups);
+    // Split-K factor: the CTAs of a tile form one cluster, and clusters are placed whole inside
+    // a GPC, so the number resident at once depends on the cluster size. Pick the split that
+    // minimises (waves) x (union entries per CTA + a fixed cost of ~30 entries for the prologue
+    // and the epilogue), at most 8 and never slices shorter than 32 union entries.
     int splits = 1;
-    if (tiles < slots)  // fill the GPU once (never a partial second wave)
-        splits = (int)std::max<int64_t>(
-            1, std::min<int64_t>({slots / tiles, 16, std::max<int64_t>(1, avg_union / 32)}));
+    double best = 0.0;
+    for (int sp = 1; sp <= 8; ++sp) {
+        if (sp > 1 && avg_union / sp < 32) break;
+        const int64_t resident = tc_resident_ctas(h.device, sp);
+        if (resident <= 0) continue;
+        const int64_t waves = ceil_div(tiles * sp, resident);
+        const double cost = (double)waves * ((double)avg_union / sp + 30.0);
+        if (sp == 1 || cost < best * 0.97) {
+            best = cost;
+            splits = sp;
+        }
+    }
     XS_REQUIRE(tiles * splits < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "grid too large");
-    const int64_t m_pad = p.ngroups * 128;
-    DevBuf<float> part(splits > 1 ? (size_t)(splits * m_pad * N) : 0, s);
     int b3d = 0;
     CUtensorMap tmB;
     if (N % 64 == 0 && make_map_b3d(B, N, K, &tmB)) {
@@ -629,19 +787,25 @@ void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M
         tmB = make_map_2d(B, (uint64_t)N, (uint64_t)K, (uint64_t)N * 2, 64, 16,
                           CU_TENSOR_MAP_SWIZZLE_128B);
     }
-    auto kern = bcsr_spmm_tc_kernel<IT>;
-    XS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
-    kern<<<(unsigned)(tiles * splits), TC_THREADS, TC_SMEM, s>>>(
-        p.apk.get(), tmB, p.gptr.get(), p.gcol.get(), splits > 1 ? part.get() : C, map, M, N, m_pad,
-        splits, ntiles, b3d, h.d_err);
+    // split-K partials: 128 x 256 fp32 per CTA (L2-resident between the two phases)
+    DevBuf<float4> ws(splits > 1 ? (size_t)tiles * splits * 8192 : 0, s);
+    // the CTAs of one tile (its split-K slices) form a cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(tiles * splits));
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = TC_SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = splits > 1 ? 1 : 0;
+    XS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, (const __half*)p.apk.get(), tmB,
+                                     (const int64_t*)p.gptr.get(), (const int32_t*)p.gcol.get(), C,
+                                     map, M, N, splits, ntiles, b3d, ws.get(), h.d_err));
     after_launch(h, "bcsr_spmm_tc");
-    if (splits > 1) {
-        const int64_t work = ceil_div(M * N, 4);
-        const unsigned grid = (unsigned)std::max<int64_t>(
-            1, std::min(ceil_div(work, 256), (int64_t)sm_count(h.device) * 16));
-        tc_reduce_kernel<IT><<<grid, 256, 0, s>>>(part.get(), C, map, M, N, m_pad, splits, h.d_err);
-        after_launch(h, "tc_reduce");
-    }
 }
 
 template <typename IT>
