@@ -29,8 +29,9 @@
 // pattern size in 32 classes (sizes 1..31 exact, 32 = "32 or more"), so a size window is a
 // contiguous slice.
 //
-// Gathering: a column of p whose inverted list is short ("light") is walked whole once, and
-// every eligible row on it gets one hit on a per-row counter, so |q n p| over light columns is a
+// Gathering: for a column of p whose inverted list is short ("light") the size window of (2) is
+// walked once (and, when p grows, the classes the widened window newly admits), and every
+// eligible row on it gets one hit on a per-row counter, so |q n p| over light columns is a
 // counter read -- no dependent load of the candidate's pattern. Long lists ("heavy", the hub
 // columns of power-law matrices) are walked only when the light columns of p are fewer than
 // |p| - m + 1, and then only over the size window of (2); a candidate's hits in heavy columns are
@@ -64,8 +65,10 @@ struct ClusterArgs {
     int32_t* U;             // [M] unclustered rows by position
     int32_t* pos;           // [M] position of a row in U, -1 once clustered
     int32_t* cnt;           // [M] light-column hits this pass (| HEAVY_MARK); 0 between passes
-    int32_t* cstamp;        // [nbc] pass in which a heavy column joined the window-gathered set
-    int32_t* cslot;         // [nbc] next size class to gather for that column
+    int32_t* cstamp;        // [nbc] pass in which the column was first walked / joined the
+                            //       window-gathered heavy set
+    int32_t* cslot;         // [nbc] next size class to walk / gather for that column
+    int32_t* hstamp;        // [nbc] pass in which the column was classified heavy
     uint32_t* pbits;        // [ceil(nbc/32)] pattern of the current cluster
     int32_t* plist;         // [nbc] columns of p, in insertion order
     int32_t* hlist;         // [nbc] heavy columns of p
@@ -175,7 +178,7 @@ struct Shared {
     int64_t col_beg[CL_THREADS];      // flattened walks of heavy windows
     int64_t col_off[CL_THREADS + 1];
     int n, out, k, pass, seed, stop;
-    int pcount, nproc, nheavy, hg, ncand, nkeep, nr, smax, limit, grown, need, cur;
+    int pcount, nproc, nheavy, hg, ncand, nkeep, nr, smax, limit, grown, need, cur, wshi;
     int64_t m, ub;
     int crow[2][CAND_CAP];            // pending candidates (double-buffered): row,
     int clen[2][CAND_CAP];            //   pattern size,
@@ -243,7 +246,7 @@ __device__ __forceinline__ void append_candidate(Shared& sh, ClusterArgs& a, int
 }
 
 // Walks the entries of up to CL_THREADS inverted-list slices (one per thread) spread over the
-// whole CTA (used for the long lists of heavy columns).
+// whole CTA.
 template <typename F>
 __device__ void flat_walk(Shared& sh, const int2* ient, int64_t e_beg, int64_t e_cnt, F&& f) {
     const int tid = threadIdx.x;
@@ -359,6 +362,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
             if (tid == 0) {
                 sh.pcount = (int)slen;
                 sh.nproc = 0;
+                sh.wshi = -1;
                 sh.nheavy = 0;
                 sh.hg = 0;
                 sh.ncand = 0;
@@ -381,32 +385,64 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     const int64_t m = sh.m, ub = sh.ub;
                     const int limit = sh.limit;
                     const int pc = sh.pcount;
-                    // (1) New columns of p. A light list is walked whole by one warp and every
-                    // eligible row on it gets one hit, so |q n p| over light columns is a
-                    // counter; heavy lists are set aside.
-                    for (int t = sh.nproc + warp; t < pc; t += CL_THREADS / 32) {
-                        const int b = a.plist[t];
-                        const int64_t lo = a.iptr[(int64_t)b * NCLS];
-                        const int64_t hi = a.iptr[(int64_t)(b + 1) * NCLS];
-                        if (hi - lo > HEAVY) {
-                            if (lane == 0) a.hlist[atomicAdd(&sh.nheavy, 1)] = b;
-                            continue;
+                    const int slo = slot_of(m), shi = slot_of(ub < NCLS ? ub : NCLS);
+                    // (1) Columns of p with a short ("light") list: one warp walks the size
+                    // window [m, ub] of the list and every eligible row on it gets one hit, so
+                    // |q n p| over light columns is a counter for every row the window admits
+                    // (a row's size class is the same in all of its columns). Each column keeps
+                    // the first class it has not walked; when p grows the window only widens
+                    // upwards, so old columns walk just the newly admitted classes and no
+                    // (column, row) pair is counted twice. Heavy lists are set aside.
+                    // A column is heavy when its window slice is long at the time it joins p
+                    // (hub columns against small patterns); against a large pattern the window
+                    // sits in high size classes and even hub columns are light.
+                    // Columns are taken CL_THREADS at a time, one per thread, and their slices
+                    // walked as one flattened range by the whole CTA: a pattern of hundreds of
+                    // columns costs a few round trips, not a few per column.
+                    const int t_first = shi != sh.wshi ? 0 : sh.nproc;
+                    const int nproc0 = sh.nproc;
+                    for (int c0 = t_first; c0 < pc; c0 += CL_THREADS) {
+                        const int t = c0 + tid;
+                        int64_t e_beg = 0, e_cnt = 0;
+                        if (t < pc) {
+                            const int b = a.plist[t];
+                            const int64_t* ib = a.iptr + (int64_t)b * NCLS;
+                            bool light = true;
+                            if (t >= nproc0) {
+                                if (ib[shi + 1] - ib[slo] > HEAVY) {
+                                    a.hstamp[b] = pass;
+                                    a.hlist[atomicAdd(&sh.nheavy, 1)] = b;
+                                    light = false;
+                                }
+                            } else if (a.hstamp[b] == pass) {
+                                light = false;
+                            }
+                            if (light) {
+                                const int from = a.cstamp[b] == pass ? max(a.cslot[b], slo) : slo;
+                                a.cstamp[b] = pass;
+                                a.cslot[b] = shi + 1;
+                                if (from <= shi) {
+                                    e_beg = ib[from];
+                                    e_cnt = ib[shi + 1] - e_beg;
+                                }
+                            }
                         }
-                        for (int64_t e = lo + lane; e < hi; e += 32) {
-                            const int2 en = a.ient[e];
+                        flat_walk(sh, a.ient, e_beg, e_cnt, [&](int2 en) {
                             const int pr = st.p(en.x);
-                            if (pr < 0 || pr >= limit) continue;
+                            if (pr < 0 || pr >= limit) return;
                             if (atomicAdd(&a.cnt[en.x], 1) == 0)
                                 append_candidate(sh, a, en.x, en.y, pr);
-                        }
+                        });
                     }
                     __syncthreads();
-                    if (tid == 0) sh.nproc = pc;
+                    if (tid == 0) {
+                        sh.nproc = pc;
+                        sh.wshi = shi;
+                    }
                     // (2) Heavy columns are needed only when the light ones are fewer than
                     // |p| - m + 1; then take the cheapest ones over the size window [m, ub].
                     const int nheavy = sh.nheavy;
                     const int want = sh.need - (pc - nheavy) - sh.hg;
-                    const int slo = slot_of(m), shi = slot_of(ub < NCLS ? ub : NCLS);
                     if (want > 0) {
                         if (tid == 0) sh.nr = 0;
                         __syncthreads();
@@ -480,7 +516,16 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     int r, len, pr;
                     cand_get(sh, a, buf, c, r, len, pr);
                     int64_t inter = a.cnt[r] & LIGHT_MASK;
+                    // Light hits are exact; each heavy column adds at most one. The distance is
+                    // non-increasing in the intersection (fixed |p| + |q|), so a candidate that
+                    // fails even with every heavy column counted is rejected without reading its
+                    // pattern.
+                    bool hopeless = false;
                     if (nheavy > 0) {
+                        const int64_t imax = min(inter + (int64_t)nheavy, (int64_t)len);
+                        hopeless = jaccard_distance(imax, pcount + (int64_t)len - imax) > a.tau;
+                    }
+                    if (nheavy > 0 && !hopeless) {
                         const int64_t q0 = a.qptr[r], q1 = a.qptr[r + 1];
                         if ((int64_t)nheavy * 4 >= len) {  // scan q against all of p
                             inter = 0;
@@ -494,7 +539,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                         }
                     }
                     const int64_t uni = pcount + (int64_t)len - inter;
-                    const bool acc = jaccard_distance(inter, uni) <= a.tau;
+                    const bool acc = !hopeless && jaccard_distance(inter, uni) <= a.tau;
                     const bool grow = acc && len > inter;
                     flag_set(sh, a, c, acc ? (grow ? 2 : 1) : 0);
                     if (grow) atomicMax(&sh.smax, pr);
@@ -656,10 +701,11 @@ __global__ void init_rows_kernel(int32_t* U, int32_t* pos, int32_t* cnt, int32_t
     }
 }
 
-__global__ void init_cols_kernel(int32_t* cstamp, uint32_t* pbits, int32_t nbc) {
+__global__ void init_cols_kernel(int32_t* cstamp, int32_t* hstamp, uint32_t* pbits, int32_t nbc) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nbc;
          i += (int64_t)gridDim.x * blockDim.x) {
         cstamp[i] = -1;
+        hstamp[i] = -1;
         if ((i & 31) == 0) pbits[i >> 5] = 0u;
     }
 }
@@ -785,7 +831,8 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     // State of the greedy loop.
     int sort_cap = 1;
     while (sort_cap < M) sort_cap <<= 1;
-    DevBuf<int32_t> U(M, s), pos(M, s), cnt(M, s), cstamp(nb, s), cslot(nb, s), plist(nb, s),
+    DevBuf<int32_t> U(M, s), pos(M, s), cnt(M, s), cstamp(nb, s), cslot(nb, s), hstamp(nb, s),
+        plist(nb, s),
         hlist(nb, s), glist(nb, s), crow(2 * M, s), clen(2 * M, s), cpos(2 * M, s), holes(M, s),
         perm32(M, s);
     DevBuf<uint32_t> pbits(ceil_div(nb, 32), s);
@@ -793,7 +840,8 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     DevBuf<uint64_t> racc(std::max<int64_t>(M, nb), s), gsort(sort_cap, s);
     init_rows_kernel<<<grid_1d(h, M, 256), 256, 0, s>>>(U.get(), pos.get(), cnt.get(), (int32_t)M);
     after_launch(h, "cluster_init_rows");
-    init_cols_kernel<<<grid_1d(h, nb, 256), 256, 0, s>>>(cstamp.get(), pbits.get(), (int32_t)nb);
+    init_cols_kernel<<<grid_1d(h, nb, 256), 256, 0, s>>>(cstamp.get(), hstamp.get(), pbits.get(),
+                                                           (int32_t)nb);
     after_launch(h, "cluster_init_cols");
 
     ClusterArgs a;
@@ -808,6 +856,7 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     a.cnt = cnt.get();
     a.cstamp = cstamp.get();
     a.cslot = cslot.get();
+    a.hstamp = hstamp.get();
     a.pbits = pbits.get();
     a.plist = plist.get();
     a.hlist = hlist.get();
