@@ -519,6 +519,134 @@ def run_tier1_compare(args):
         ex.set_tier1_kernel("auto")
 
 
+def run_sharded(args):
+    """One matrix (cfg4 banded or cfg5 R-MAT at full size) split by block rows over the ranks
+    (balanced by nonzero blocks), B broadcast once over NCCL, then the steady-state Tier-1 product
+    timed on every rank (max over ranks). Clustering runs once on rank 0 and its permutation is
+    broadcast. Strong scaling: the total work is fixed. One JSON line from rank 0."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import xspmm_b200 as xs
+    from xspmm_b200 import synth
+    from xspmm_b200.shard import BlockRowShard, broadcast_b, partition_block_rows
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    if args.sharded == "cfg4":
+        P, N, label = synth.cfg4_banded(N=64), 64, "cfg4_banded_2M"
+    else:
+        P, N, label = synth.cfg5_rmat(N=128), 128, "cfg5_rmat_2^20"
+    ex = xs.CudaExecutor(local)
+    A = xs.CSRMatrix.from_host(ex, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int32)
+    stream = torch.cuda.current_stream(dev)
+    # clustering once (rank 0), permutation broadcast
+    perm = torch.empty(P.M, dtype=torch.int32, device=dev)
+    c0, c1 = ev(), ev()
+    barrier()
+    c0.record(stream)
+    if rank == 0:
+        xs.compute_1d_jaccard_clustering(ex, A, 0.5, 16, perm)
+    c1.record(stream)
+    if world > 1:
+        dist.broadcast(perm, src=0)
+    torch.cuda.synchronize()
+    cluster_ms = c0.elapsed_time(c1)
+    v0, v1 = ev(), ev()
+    v0.record(stream)
+    Ap = xs.apply_permutation(ex, A, perm)
+    Ab = xs.csr_to_bcsr(ex, Ap, 16, 16)
+    v1.record(stream)
+    torch.cuda.synchronize()
+    convert_ms = v0.elapsed_time(v1)
+    del Ap
+    nnzb_before = xs.csr_to_bcsr(ex, A, 16, 16).num_blocks
+    bounds = partition_block_rows(Ab.row_ptr.cpu().numpy(), world)
+    shard = BlockRowShard(Ab, int(bounds[rank]), int(bounds[rank + 1]))
+    B = (torch.as_tensor(P.B).to(dev) if rank == 0
+         else torch.zeros(P.B.shape, dtype=torch.float16, device=dev))
+    barrier()
+    b0, b1 = ev(), ev()
+    b0.record(stream)
+    if world > 1:
+        broadcast_b(B, src=0)
+    b1.record(stream)
+    torch.cuda.synchronize()
+    bcast_ms = b0.elapsed_time(b1)
+    C = torch.empty((shard.num_rows, N), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        shard.execute(B, C, N)
+    torch.cuda.synchronize()
+    starts = [ev() for _ in range(args.steps)]
+    ends = [ev() for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        starts[i].record(stream)
+        shard.execute(B, C, N)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    assert torch.isfinite(C).all().item()
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    blocks_t = torch.tensor([shard.nnz_blocks], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        all_blocks = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(world)]
+        dist.all_gather(all_blocks, blocks_t)
+        per_rank_blocks = [int(x.item()) for x in all_blocks]
+    else:
+        per_rank_blocks = [shard.nnz_blocks]
+    shard.close()
+    if rank == 0:
+        t = ms_t.item()
+        pk = peaks()
+        eff = 2.0 * P.nnz * N / (t * 1e-3) / 1e12
+        padded = 2.0 * Ab.num_blocks * 256 * N / (t * 1e-3) / 1e12
+        alg_bytes = Ab.num_blocks * (512 + 4) + (Ab.num_block_rows + 1) * 4 + P.K * N * 2 + P.M * N * 4
+        print(json.dumps({
+            "metric": "SpMM effective TFLOPS (2*nnz*N/s), Tier-1 block-row sharded, B resident",
+            "value": round(eff, 4), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t, 4), "higher_is_better": True,
+            "scaling": "strong", "dtype": "f16", "data": "synthetic (seeded generator)",
+            "config": {"workload": label, "M": P.M, "K": P.K, "N": N, "nnz": P.nnz,
+                       "nnzb_before_clustering": nnzb_before, "nnzb": Ab.num_blocks,
+                       "partition": "block rows balanced by nonzero blocks",
+                       "per_rank_blocks": per_rank_blocks,
+                       "l2": "flushed before every step (256 MiB write)"},
+            "padded_tflops": round(padded, 3),
+            "padded_frac_of_bf16_peak": round(padded / pk["bf16_tflops"], 5),
+            "hbm_frac_whole_job": round(alg_bytes / (t * 1e-3) / 1e9 / (pk["hbm_gbs"] * world), 4),
+            "b_broadcast_ms": round(bcast_ms, 4), "clustering_ms": round(cluster_ms, 2),
+            "conversion_ms": round(convert_ms, 3), "clocks": clocks,
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -532,9 +660,16 @@ def main():
                     help="mma.sync vs tcgen05 Tier-1 on the pruned-LLM config, N sweep")
     ap.add_argument("--compare-n", default="16,64,256,1024,4096")
     ap.add_argument("--compare-kernels", default="mma,tc")
+    ap.add_argument("--sharded", choices=["cfg4", "cfg5"],
+                    help="one full-size matrix split by block rows over the ranks (Tier-1)")
     args = ap.parse_args()
     if args.tier1_compare:
         run_tier1_compare(args)
+        return
+    if args.sharded:
+        if args.warmup < 3:
+            args.warmup = 3
+        run_sharded(args)
         return
     if args.warmup < 3 and args.impl == "xspmm":
         args.warmup = 3
