@@ -43,7 +43,12 @@ bool tc_preferred(int64_t nbr, int64_t nbc, int64_t nnzb);
 // The mma.sync Tier-1 kernel, without the automatic choice of tcgen05.
 template <typename IT>
 void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
-                       const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map);
+                       const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map,
+                       const int32_t* order);
+// Execution order of block rows for the mma.sync kernel: sorted by first block column.
+template <typename IT>
+void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT* ci,
+                     DevBuf<int32_t>& order);
 
 // Which Tier-1 fp16 kernel runs: the handle's setting (xspmm_set_tier1_kernel) if not auto, else
 // the environment XSPMM_TIER1_KERNEL = mma | tc | auto (default auto).

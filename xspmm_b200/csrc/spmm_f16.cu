@@ -9,15 +9,18 @@
 // and uses 64-bit value offsets (the reference's int32 i*256 overflows past 2^31 values).
 //
 // Work split: a CTA owns one block row and a TN = 64*WARPS column tile; each warp owns 64 columns
-// (8 n8 tiles, 32 fp32 accumulators per thread). Each block's product is formed by the tensor core
-// in a zeroed fragment and added to the accumulators with IEEE round-to-nearest adds, so a long
-// block row does not collect one accumulator truncation per block. Per block the CTA stages the 16x16 A block
+// (8 n8 tiles, 32 fp32 accumulators per thread). The products of up to 8 consecutive blocks
+// accumulate in the tensor core in a zeroed fragment, which is then added to the accumulators
+// with IEEE round-to-nearest adds, so a long block row collects one accumulator truncation per
+// group of blocks, not per block. Per block the CTA stages the 16x16 A block
 // (512 B) and the 16 x TN slab of B rows 16*col .. 16*col+15 into shared memory with 16-byte
 // cp.async, STAGES deep. A is read with ldmatrix.x4 (rows XOR-swizzled by (row>>2)&1), B with
 // ldmatrix.x4.trans (16-byte chunks XOR-swizzled by k&7), both conflict-free. When N is not a
 // multiple of 8 the B rows are not 16-byte aligned and the slab is loaded with guarded scalar
 // loads instead.
 #include "ops.cuh"
+
+#include <cub/device/device_radix_sort.cuh>
 
 #include <cstdlib>
 #include <cstring>
@@ -65,7 +68,8 @@ __global__ void __launch_bounds__(WARPS * 32)
 bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_ind,
                          const __half* __restrict__ vals, const __half* __restrict__ B,
                          float* __restrict__ C, const IT* __restrict__ row_map, int64_t M,
-                         int64_t K, int64_t N, unsigned* __restrict__ err) {
+                         int64_t K, int64_t N, const int32_t* __restrict__ order,
+                         unsigned* __restrict__ err) {
     constexpr int TN = 64 * WARPS;
     constexpr int A_BYTES = 512;
     constexpr int ROW_BYTES = TN * 2;
@@ -75,12 +79,29 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
     constexpr int THREADS = WARPS * 32;
     extern __shared__ __align__(128) uint8_t smem[];
 
-    const int64_t br = blockIdx.x;
+    const int64_t br = order ? (int64_t)order[blockIdx.x] : (int64_t)blockIdx.x;
     const int64_t n0 = (int64_t)blockIdx.y * TN;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t jb = row_ptr[br];
     const int nblk = (int)(row_ptr[br + 1] - jb);
     const bool warp_active = n0 + warp * 64 < N;
+
+    // B slab chunks: every thread always copies the same ITER (row k, 16-byte chunk ch) pairs of
+    // a slab, so their offsets are computed once and a stage costs one multiply-add per chunk.
+    constexpr int ITER = 16 * CPR / THREADS;
+    static_assert(16 * CPR % THREADS == 0, "slab chunks divide evenly over the threads");
+    int64_t b_src[ITER];
+    int b_dst[ITER], b_k[ITER];
+    bool b_col_ok[ITER];
+#pragma unroll
+    for (int it = 0; it < ITER; ++it) {
+        const int c = threadIdx.x + it * THREADS;
+        const int k = c / CPR, ch = c % CPR;
+        b_k[it] = k;
+        b_src[it] = (int64_t)k * N + n0 + ch * 8;
+        b_dst[it] = k * ROW_BYTES + ((ch ^ (k & 7)) * 16);
+        b_col_ok[it] = n0 + ch * 8 < N;
+    }
 
     auto load_stage = [&](int stage, int64_t j) {
         uint8_t* sA = smem + stage * STAGE_BYTES;
@@ -99,16 +120,21 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
                 *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(t);
             }
         }
-        for (int c = threadIdx.x; c < 16 * CPR; c += THREADS) {
-            const int k = c / CPR, ch = c % CPR;
-            const int64_t grow = bc * 16 + k;
-            const int64_t gcol = n0 + ch * 8;
-            uint8_t* dst = sB + k * ROW_BYTES + ((ch ^ (k & 7)) * 16);
-            if constexpr (ALIGNED) {
-                const bool ok = grow < K && gcol < N;
-                cp_async16(dst, ok ? (const void*)(B + grow * N + gcol) : (const void*)B,
+        if constexpr (ALIGNED) {
+            const __half* Bb = B + bc * 16 * N;
+            const int64_t krem = K - bc * 16;  // rows of this slab inside B
+#pragma unroll
+            for (int it = 0; it < ITER; ++it) {
+                const bool ok = b_col_ok[it] && b_k[it] < krem;
+                cp_async16(sB + b_dst[it], ok ? (const void*)(Bb + b_src[it]) : (const void*)B,
                            ok ? 16 : 0);
-            } else {
+            }
+        } else {
+            for (int c = threadIdx.x; c < 16 * CPR; c += THREADS) {
+                const int k = c / CPR, ch = c % CPR;
+                const int64_t grow = bc * 16 + k;
+                const int64_t gcol = n0 + ch * 8;
+                uint8_t* dst = sB + k * ROW_BYTES + ((ch ^ (k & 7)) * 16);
                 __align__(16) __half t[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e)
@@ -118,11 +144,15 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
         }
     };
 
-    float acc[8][4];
+    // Products of up to GROUP consecutive blocks accumulate in the tensor core (fragment p); each
+    // group's sum is then added to the running sum with IEEE round-to-nearest adds, so a long
+    // block row collects one accumulator truncation per group of blocks, not per block.
+    constexpr int GROUP = 8;
+    float acc[8][4], p[8][4];
 #pragma unroll
     for (int t = 0; t < 8; ++t)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
+        for (int e = 0; e < 4; ++e) acc[t][e] = p[t][e] = 0.0f;
 
 #pragma unroll
     for (int s = 0; s < STAGES - 1; ++s) {
@@ -134,7 +164,7 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
     const int mi = lane >> 3, rin = lane & 7;
     const int a_row = rin + 8 * (mi & 1);
     const int a_off = a_row * 32 + (((mi >> 1) ^ ((a_row >> 2) & 1)) * 16);
-    const int b_k = rin + 8 * (mi & 1);
+    const int b_kk = rin + 8 * (mi & 1);
 
     for (int i = 0; i < nblk; ++i) {
         cp_async_wait<STAGES - 2>();
@@ -148,18 +178,18 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
             for (int j = 0; j < 4; ++j) {
                 const int chunk = (warp * 64 + j * 16) / 8 + (mi >> 1);
                 uint32_t b[4];
-                ldmatrix_x4_trans(b, sB + b_k * ROW_BYTES + ((chunk ^ (b_k & 7)) * 16));
-                // One block's 16-term products go through the tensor core into a zeroed
-                // fragment; the running sum is kept with round-to-nearest FADD. Accumulating in
-                // the MMA itself would add one truncation per block to every output.
-                float p0[4] = {0.f, 0.f, 0.f, 0.f}, p1[4] = {0.f, 0.f, 0.f, 0.f};
-                mma_16816(p0, a, b[0], b[1]);
-                mma_16816(p1, a, b[2], b[3]);
+                ldmatrix_x4_trans(b, sB + b_kk * ROW_BYTES + ((chunk ^ (b_kk & 7)) * 16));
+                mma_16816(p[2 * j], a, b[0], b[1]);
+                mma_16816(p[2 * j + 1], a, b[2], b[3]);
+            }
+            if ((i + 1) % GROUP == 0 || i + 1 == nblk) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    acc[2 * j][e] = __fadd_rn(acc[2 * j][e], p0[e]);
-                    acc[2 * j + 1][e] = __fadd_rn(acc[2 * j + 1][e], p1[e]);
-                }
+                for (int t = 0; t < 8; ++t)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[t][e] = __fadd_rn(acc[t][e], p[t][e]);
+                        p[t][e] = 0.0f;
+                    }
             }
         }
         const int nx = i + STAGES - 1;
@@ -196,13 +226,13 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
 
 template <typename IT, int WARPS, bool ALIGNED>
 void launch(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v, const __half* B,
-            float* C, int64_t M, int64_t K, int64_t N, const IT* map) {
+            float* C, int64_t M, int64_t K, int64_t N, const IT* map, const int32_t* order) {
     constexpr int TN = 64 * WARPS;
     constexpr int smem = STAGES * (512 + 16 * TN * 2);
     static_assert(smem <= 48 * 1024, "stage ring must fit the default dynamic smem limit");
     auto kern = bcsr_spmm_f16_mma_kernel<IT, WARPS, ALIGNED>;
     dim3 grid((unsigned)nbr, (unsigned)ceil_div(N, TN));
-    kern<<<grid, WARPS * 32, smem, h.stream>>>(rp, ci, v, B, C, map, M, K, N, h.d_err);
+    kern<<<grid, WARPS * 32, smem, h.stream>>>(rp, ci, v, B, C, map, M, K, N, order, h.d_err);
     after_launch(h, "bcsr_spmm_f16_mma");
 }
 
@@ -238,12 +268,13 @@ static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb
         bcsr_spmm_tc<IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
         return;
     }
-    bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+    bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map, nullptr);
 }
 
 template <typename IT>
 void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
-                       const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map) {
+                       const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map,
+                       const int32_t* order) {
     if (nbr == 0 || N == 0 || M == 0) return;
     XS_REQUIRE(ceil_div(N, 64) <= 65535, XSPMM_STATUS_UNSUPPORTED, "N above 4,194,240 columns");
     const bool aligned = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
@@ -251,22 +282,66 @@ void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const
                          (reinterpret_cast<uintptr_t>(C) % 8 == 0);
     const int warps = N <= 64 ? 1 : (N <= 128 ? 2 : 4);
     if (aligned) {
-        if (warps == 1) launch<IT, 1, true>(h, nbr, rp, ci, v, B, C, M, K, N, map);
-        else if (warps == 2) launch<IT, 2, true>(h, nbr, rp, ci, v, B, C, M, K, N, map);
-        else launch<IT, 4, true>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+        if (warps == 1) launch<IT, 1, true>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
+        else if (warps == 2) launch<IT, 2, true>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
+        else launch<IT, 4, true>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
     } else {
-        if (warps == 1) launch<IT, 1, false>(h, nbr, rp, ci, v, B, C, M, K, N, map);
-        else if (warps == 2) launch<IT, 2, false>(h, nbr, rp, ci, v, B, C, M, K, N, map);
-        else launch<IT, 4, false>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+        if (warps == 1) launch<IT, 1, false>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
+        else if (warps == 2) launch<IT, 2, false>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
+        else launch<IT, 4, false>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
     }
 }
 
 template void bcsr_spmm_mma_f16<int32_t>(Handle&, int64_t, const int32_t*, const int32_t*,
                                          const __half*, const __half*, float*, int64_t, int64_t,
-                                         int64_t, const int32_t*);
+                                         int64_t, const int32_t*, const int32_t*);
 template void bcsr_spmm_mma_f16<int64_t>(Handle&, int64_t, const int64_t*, const int64_t*,
                                          const __half*, const __half*, float*, int64_t, int64_t,
-                                         int64_t, const int64_t*);
+                                         int64_t, const int64_t*, const int32_t*);
+
+// Block rows sorted by their first block column (empty rows last): the execution order a plan
+// gives the mma.sync kernel, so that CTAs running together gather nearby rows of B and the gather
+// hits L2. The product of each block row does not depend on the order.
+template <typename IT>
+__global__ void first_col_keys_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci,
+                                      int64_t nbr, int64_t nbc, uint32_t* __restrict__ keys,
+                                      int32_t* __restrict__ rows) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < nbr;
+         r += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = rp[r];
+        keys[r] = rp[r + 1] > b ? (uint32_t)ci[b] : (uint32_t)nbc;
+        rows[r] = (int32_t)r;
+    }
+}
+
+template <typename IT>
+void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT* ci,
+                     DevBuf<int32_t>& order) {
+    XS_REQUIRE(nbr < (int64_t(1) << 31) && nbc < (int64_t(1) << 32), XSPMM_STATUS_UNSUPPORTED,
+               "block grid too large to order");
+    cudaStream_t s = h.stream;
+    order = DevBuf<int32_t>(std::max<int64_t>(nbr, 1), s);
+    if (nbr == 0) return;
+    DevBuf<uint32_t> k_in(nbr, s), k_out(nbr, s);
+    DevBuf<int32_t> r_in(nbr, s);
+    const unsigned grid = (unsigned)std::max<int64_t>(
+        1, std::min(ceil_div(nbr, 256), (int64_t)sm_count(h.device) * 8));
+    first_col_keys_kernel<IT><<<grid, 256, 0, s>>>(rp, ci, nbr, nbc, k_in.get(), r_in.get());
+    after_launch(h, "first_col_keys");
+    int end_bit = 1;
+    while (end_bit < 32 && (uint64_t(1) << end_bit) <= (uint64_t)nbc) ++end_bit;
+    size_t tmp_bytes = 0;
+    XS_CHECK_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp_bytes, k_in.get(), k_out.get(),
+                                                  r_in.get(), order.get(), (int)nbr, 0, end_bit, s));
+    DevBuf<uint8_t> tmp(std::max<size_t>(tmp_bytes, 1), s);
+    XS_CHECK_CUDA(cub::DeviceRadixSort::SortPairs(tmp.get(), tmp_bytes, k_in.get(), k_out.get(),
+                                                  r_in.get(), order.get(), (int)nbr, 0, end_bit, s));
+    h.launches += 1;
+}
+template void block_row_order<int32_t>(Handle&, int64_t, int64_t, const int32_t*, const int32_t*,
+                                       DevBuf<int32_t>&);
+template void block_row_order<int64_t>(Handle&, int64_t, int64_t, const int64_t*, const int64_t*,
+                                       DevBuf<int32_t>&);
 
 template <>
 void bcsr_spmm<__half, int32_t>(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb,
