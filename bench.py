@@ -577,72 +577,85 @@ def run_sharded(args):
     convert_ms = v0.elapsed_time(v1)
     del Ap
     nnzb_before = xs.csr_to_bcsr(ex, A, 16, 16).num_blocks
-    bounds = partition_block_rows(Ab.row_ptr.cpu().numpy(), world)
-    shard = BlockRowShard(Ab, int(bounds[rank]), int(bounds[rank + 1]))
-    B = (torch.as_tensor(P.B).to(dev) if rank == 0
-         else torch.zeros(P.B.shape, dtype=torch.float16, device=dev))
-    barrier()
-    b0, b1 = ev(), ev()
-    b0.record(stream)
-    if world > 1:
-        broadcast_b(B, src=0)
-    b1.record(stream)
-    torch.cuda.synchronize()
-    bcast_ms = b0.elapsed_time(b1)
-    C = torch.empty((shard.num_rows, N), dtype=torch.float32, device=dev)
+    row_ptr_host = Ab.row_ptr.cpu().numpy()
+    B_full = torch.as_tensor(P.B).to(dev) if rank == 0 else None
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    for _ in range(args.warmup):
-        shard.execute(B, C, N)
-    torch.cuda.synchronize()
-    starts = [ev() for _ in range(args.steps)]
-    ends = [ev() for _ in range(args.steps)]
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    barrier()
-    torch.cuda.synchronize()
-    for i in range(args.steps):
-        flush.fill_(float(i))
-        starts[i].record(stream)
-        shard.execute(B, C, N)
-        ends[i].record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clocks = sampler.stop()
-    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
-    assert torch.isfinite(C).all().item()
-    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    blocks_t = torch.tensor([shard.nnz_blocks], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-        all_blocks = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(world)]
-        dist.all_gather(all_blocks, blocks_t)
-        per_rank_blocks = [int(x.item()) for x in all_blocks]
-    else:
-        per_rank_blocks = [shard.nnz_blocks]
-    shard.close()
-    if rank == 0:
-        t = ms_t.item()
-        pk = peaks()
-        eff = 2.0 * P.nnz * N / (t * 1e-3) / 1e12
-        padded = 2.0 * Ab.num_blocks * 256 * N / (t * 1e-3) / 1e12
-        alg_bytes = Ab.num_blocks * (512 + 4) + (Ab.num_block_rows + 1) * 4 + P.K * N * 2 + P.M * N * 4
-        print(json.dumps({
-            "metric": "SpMM effective TFLOPS (2*nnz*N/s), Tier-1 block-row sharded, B resident",
-            "value": round(eff, 4), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(t, 4), "higher_is_better": True,
-            "scaling": "strong", "dtype": "f16", "data": "synthetic (seeded generator)",
-            "config": {"workload": label, "M": P.M, "K": P.K, "N": N, "nnz": P.nnz,
-                       "nnzb_before_clustering": nnzb_before, "nnzb": Ab.num_blocks,
-                       "partition": "block rows balanced by nonzero blocks",
-                       "per_rank_blocks": per_rank_blocks,
-                       "l2": "flushed before every step (256 MiB write)"},
-            "padded_tflops": round(padded, 3),
-            "padded_frac_of_bf16_peak": round(padded / pk["bf16_tflops"], 5),
-            "hbm_frac_whole_job": round(alg_bytes / (t * 1e-3) / 1e9 / (pk["hbm_gbs"] * world), 4),
-            "b_broadcast_ms": round(bcast_ms, 4), "clustering_ms": round(cluster_ms, 2),
-            "conversion_ms": round(convert_ms, 3), "clocks": clocks,
-        }), flush=True)
+    sizes = [g for g in (1, 2, 4, 8, 16) if g <= world] if args.scaling_sweep else [world]
+    for g in sizes:
+        # ranks [0, g) form the group; the others wait at the barrier below
+        group = dist.new_group(ranks=list(range(g))) if world > 1 and g > 1 else None
+        if rank < g:
+            bounds = partition_block_rows(row_ptr_host, g)
+            shard = BlockRowShard(Ab, int(bounds[rank]), int(bounds[rank + 1]))
+            B = B_full.clone() if rank == 0 else torch.zeros(P.B.shape, dtype=torch.float16,
+                                                              device=dev)
+            b0, b1 = ev(), ev()
+            b0.record(stream)
+            if g > 1:
+                broadcast_b(B, src=0, group=group)
+            b1.record(stream)
+            torch.cuda.synchronize()
+            bcast_ms = b0.elapsed_time(b1)
+            C = torch.empty((shard.num_rows, N), dtype=torch.float32, device=dev)
+            for _ in range(args.warmup):
+                shard.execute(B, C, N)
+            torch.cuda.synchronize()
+            starts = [ev() for _ in range(args.steps)]
+            ends = [ev() for _ in range(args.steps)]
+            sampler = ClockSampler(local)
+            sampler.start()
+            time.sleep(0.3)
+            if g > 1:
+                dist.barrier(group=group)
+            torch.cuda.synchronize()
+            for i in range(args.steps):
+                flush.fill_(float(i))
+                starts[i].record(stream)
+                shard.execute(B, C, N)
+                ends[i].record(stream)
+            torch.cuda.synchronize()
+            if g > 1:
+                dist.barrier(group=group)
+            clocks = sampler.stop()
+            ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
+            assert torch.isfinite(C).all().item()
+            ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            blocks_t = torch.tensor([shard.nnz_blocks], dtype=torch.float64, device=dev)
+            if g > 1:
+                dist.all_reduce(ms_t, op=dist.ReduceOp.MAX, group=group)
+                all_blocks = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(g)]
+                dist.all_gather(all_blocks, blocks_t, group=group)
+                per_rank_blocks = [int(x.item()) for x in all_blocks]
+            else:
+                per_rank_blocks = [shard.nnz_blocks]
+            shard.close()
+            del C, B
+            if rank == 0:
+                t = ms_t.item()
+                pk = peaks()
+                eff = 2.0 * P.nnz * N / (t * 1e-3) / 1e12
+                padded = 2.0 * Ab.num_blocks * 256 * N / (t * 1e-3) / 1e12
+                alg_bytes = (Ab.num_blocks * (512 + 4) + (Ab.num_block_rows + 1) * 4 +
+                             P.K * N * 2 + P.M * N * 4)
+                print(json.dumps({
+                    "metric": "SpMM effective TFLOPS (2*nnz*N/s), Tier-1 block-row sharded, "
+                              "B resident",
+                    "value": round(eff, 4), "unit": "TFLOPS", "n_gpus": g, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": round(t, 4), "higher_is_better": True,
+                    "scaling": "strong", "dtype": "f16", "data": "synthetic (seeded generator)",
+                    "config": {"workload": label, "M": P.M, "K": P.K, "N": N, "nnz": P.nnz,
+                               "nnzb_before_clustering": nnzb_before, "nnzb": Ab.num_blocks,
+                               "partition": "block rows balanced by nonzero blocks",
+                               "per_rank_blocks": per_rank_blocks,
+                               "l2": "flushed before every step (256 MiB write)"},
+                    "padded_tflops": round(padded, 3),
+                    "padded_frac_of_bf16_peak": round(padded / pk["bf16_tflops"], 5),
+                    "hbm_frac_whole_job": round(alg_bytes / (t * 1e-3) / 1e9 / (pk["hbm_gbs"] * g), 4),
+                    "b_broadcast_ms": round(bcast_ms, 4), "clustering_ms": round(cluster_ms, 2),
+                    "conversion_ms": round(convert_ms, 3), "clocks": clocks,
+                }), flush=True)
+        if world > 1:
+            dist.barrier()
     if world > 1:
         dist.destroy_process_group()
 
@@ -662,6 +675,8 @@ def main():
     ap.add_argument("--compare-kernels", default="mma,tc")
     ap.add_argument("--sharded", choices=["cfg4", "cfg5"],
                     help="one full-size matrix split by block rows over the ranks (Tier-1)")
+    ap.add_argument("--scaling-sweep", action="store_true",
+                    help="with --sharded: also time the first 1, 2, 4, ... ranks of the launch")
     args = ap.parse_args()
     if args.tier1_compare:
         run_tier1_compare(args)

@@ -160,3 +160,41 @@ def test_plan_rejects_bad_arguments(executor):
         with pytest.raises(ValueError):
             plan.execute(torch.zeros((64, 8), device=executor.device),
                          torch.zeros((64, 8), device=executor.device), 8)
+
+
+@pytest.mark.parametrize("index_dtype", [torch.int32, torch.int64])
+def test_plan_splits_long_block_rows(executor, index_dtype):
+    """Block rows longer than a work slice (here 512 blocks) are cut into slices whose partial
+    sums are added in a fixed order; C must match the oracle and be the same on every run."""
+    P = synth.cfg3_pruned_llm(seed=24, M=96, K=8192, N=8)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=index_dtype)
+    executor.set_tier1_kernel("mma")
+    try:
+        with xs.SpMMPlan(executor, A, 16, False) as plan:
+            N = 72
+            B = np.random.default_rng(7).standard_normal((P.K, N)).astype(np.float16)
+            Bd = torch.as_tensor(B).to(executor.device)
+            C1 = torch.full((P.M, N), float("nan"), device=executor.device)
+            C2 = torch.full((P.M, N), float("nan"), device=executor.device)
+            plan.execute(Bd, C1, N)
+            plan.execute(Bd, C2, N)
+            assert torch.equal(C1, C2)
+            P.B = B
+            P.N = N
+            ref, emu = _oracle_tier2(P, B, False)
+            _close(ref, emu, C1.cpu().numpy())
+    finally:
+        executor.set_tier1_kernel("auto")
+
+
+def test_plan_power_law_rows(executor):
+    """R-MAT graph with hub rows through a plan (the work list orders rows and splits hubs)."""
+    P = synth.cfg5_rmat(seed=3, scale=13, N=64)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int32)
+    with xs.SpMMPlan(executor, A, 16, False) as plan:
+        C = torch.full((P.M, P.N), float("nan"), device=executor.device)
+        plan.execute(torch.as_tensor(P.B).to(executor.device), C, P.N)
+        ref, emu = _oracle_tier2(P, P.B, False)
+        _close(ref, emu, C.cpu().numpy())

@@ -58,7 +58,8 @@ def fp32_block_emulation(M, N, brp, bci, bv, B, rb=16, cb=16):
     running sum. Used to bound the error any fp32-accumulating implementation has on long rows."""
     nbr = len(brp) - 1
     K = B.shape[0]
-    Bp = np.zeros((len(bci) and (int(np.max(bci)) + 1) * cb or cb, N), dtype=np.float32)
+    nbk = max((K + cb - 1) // cb, int(np.max(bci)) + 1 if len(bci) else 1)
+    Bp = np.zeros((nbk * cb, N), dtype=np.float32)
     Bp[:K] = B.astype(np.float32)
     C = np.zeros((nbr * rb, N), dtype=np.float32)
     lens = np.diff(brp)

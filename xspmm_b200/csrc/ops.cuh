@@ -41,10 +41,27 @@ void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M
 bool tc_preferred(int64_t nbr, int64_t nbc, int64_t nnzb);
 
 // The mma.sync Tier-1 kernel, without the automatic choice of tcgen05.
+// Work list of the mma.sync kernel built once by a plan: block rows in execution order, long
+// block rows cut into slices whose partial sums are reduced in a fixed order afterwards.
+struct MmaItem {
+    int64_t jb;    // first block
+    int32_t br;    // block row
+    int32_t nblk;  // blocks in this item
+    int32_t slot;  // workspace slot of a slice of a split row, -1 for a whole row
+    int32_t pad;
+};
+struct MmaWork {
+    DevBuf<MmaItem> items;
+    DevBuf<int32_t> long_rows, first_slot;
+    int64_t nitems = 0, nlong = 0, nslots = 0;
+};
+template <typename IT>
+void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,
+                    const IT* ci, bool by_first_col, MmaWork& out);
 template <typename IT>
 void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
                        const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map,
-                       const int32_t* order);
+                       const MmaWork* work);
 // Execution order of block rows for the mma.sync kernel: sorted by first block column.
 template <typename IT>
 void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT* ci,

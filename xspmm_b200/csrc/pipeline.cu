@@ -117,12 +117,13 @@ void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
         // When B is well beyond what L2 holds, run the block rows in order of their first
         // block column so that CTAs in flight together gather nearby rows of B.
         const bool big_b = (double)K * (double)N * sizeof(__half) > 48.0 * (1 << 20);
-        if (big_b && !order_built && nbr > 0) {
-            block_row_order<IT>(h, nbr, nbc, rp, ci, order);
-            order_built = true;
+        if (nbr > 0 && (!work_built || (big_b && !work_sorted))) {
+            work = MmaWork();
+            mma_work_build<IT>(h, nbr, nbc, nnzb, rp, ci, big_b, work);
+            work_built = true;
+            work_sorted = big_b;
         }
-        bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map,
-                              big_b && order_built ? order.get() : nullptr);
+        bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map, work_built ? &work : nullptr);
     } else {
         bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
     }

@@ -39,8 +39,9 @@ struct Plan final : PlanBase {
     const VT* v = nullptr;
     TcPrep tc;
     bool tc_built = false;
-    DevBuf<int32_t> order;  // block-row execution order for the mma.sync kernel
-    bool order_built = false;
+    MmaWork work;  // work list of the mma.sync kernel (order, split long rows)
+    bool work_built = false;
+    bool work_sorted = false;
 
     void execute(Handle& h, const void* B, float* C, int64_t N) override;
     void prepare_tc(Handle& h) override;
@@ -48,14 +49,17 @@ struct Plan final : PlanBase {
     int64_t tc_tiles() const override { return tc_built ? tc.bound : 0; }
     int64_t device_bytes() const override {
         return (int64_t)(perm.n + brp.n + bci.n) * (int64_t)sizeof(IT) +
-               (int64_t)order.n * (int64_t)sizeof(int32_t) +
+               (int64_t)work.items.n * (int64_t)sizeof(MmaItem) +
+               (int64_t)(work.long_rows.n + work.first_slot.n) * (int64_t)sizeof(int32_t) +
                (int64_t)bv.n * (int64_t)sizeof(VT) +
                (int64_t)(tc.gptr.n * sizeof(int64_t) + tc.gcol.n * sizeof(int32_t) +
                          tc.apk.n * sizeof(__half));
     }
     void rebind_stream(cudaStream_t s) override {
         perm.s = brp.s = bci.s = s;
-        order.s = s;
+        work.items.s = s;
+        work.long_rows.s = s;
+        work.first_slot.s = s;
         bv.s = s;
         tc.gptr.s = s;
         tc.gcol.s = s;

@@ -24,6 +24,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <vector>
 
 namespace xspmm_b200 {
 namespace {
@@ -68,8 +69,8 @@ __global__ void __launch_bounds__(WARPS * 32)
 bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_ind,
                          const __half* __restrict__ vals, const __half* __restrict__ B,
                          float* __restrict__ C, const IT* __restrict__ row_map, int64_t M,
-                         int64_t K, int64_t N, const int32_t* __restrict__ order,
-                         unsigned* __restrict__ err) {
+                         int64_t K, int64_t N, const MmaItem* __restrict__ items,
+                         float* __restrict__ ws, unsigned* __restrict__ err) {
     constexpr int TN = 64 * WARPS;
     constexpr int A_BYTES = 512;
     constexpr int ROW_BYTES = TN * 2;
@@ -79,11 +80,23 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
     constexpr int THREADS = WARPS * 32;
     extern __shared__ __align__(128) uint8_t smem[];
 
-    const int64_t br = order ? (int64_t)order[blockIdx.x] : (int64_t)blockIdx.x;
+    // Work item: a block row, or a slice of a long block row whose partial sum goes to
+    // workspace slot `slot` (16 x N floats) and is reduced afterwards in a fixed order.
+    int64_t br, jb;
+    int nblk, slot = -1;
+    if (items) {
+        const MmaItem it = items[blockIdx.x];
+        br = it.br;
+        jb = it.jb;
+        nblk = it.nblk;
+        slot = it.slot;
+    } else {
+        br = blockIdx.x;
+        jb = row_ptr[br];
+        nblk = (int)(row_ptr[br + 1] - jb);
+    }
     const int64_t n0 = (int64_t)blockIdx.y * TN;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t jb = row_ptr[br];
-    const int nblk = (int)(row_ptr[br + 1] - jb);
     const bool warp_active = n0 + warp * 64 < N;
 
     // B slab chunks: every thread always copies the same ITER (row k, 16-byte chunk ch) pairs of
@@ -202,6 +215,16 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
     const int g = lane >> 2, q = lane & 3;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
+        if (slot >= 0) {  // partial of a split block row: all 16 rows, no row map
+            float* prow = ws + ((int64_t)slot * 16 + g + 8 * half) * N;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const int64_t col = n0 + warp * 64 + t * 8 + 2 * q;
+                if (col < N) prow[col] = acc[t][2 * half];
+                if (col + 1 < N) prow[col + 1] = acc[t][2 * half + 1];
+            }
+            continue;
+        }
         const int64_t r = br * 16 + g + 8 * half;
         if (r >= M) continue;
         const int64_t orow = row_map ? (int64_t)row_map[r] : r;
@@ -226,13 +249,14 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
 
 template <typename IT, int WARPS, bool ALIGNED>
 void launch(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v, const __half* B,
-            float* C, int64_t M, int64_t K, int64_t N, const IT* map, const int32_t* order) {
+            float* C, int64_t M, int64_t K, int64_t N, const IT* map, const MmaItem* items,
+            float* ws) {
     constexpr int TN = 64 * WARPS;
     constexpr int smem = STAGES * (512 + 16 * TN * 2);
     static_assert(smem <= 48 * 1024, "stage ring must fit the default dynamic smem limit");
     auto kern = bcsr_spmm_f16_mma_kernel<IT, WARPS, ALIGNED>;
-    dim3 grid((unsigned)nbr, (unsigned)ceil_div(N, TN));
-    kern<<<grid, WARPS * 32, smem, h.stream>>>(rp, ci, v, B, C, map, M, K, N, order, h.d_err);
+    dim3 grid((unsigned)nbr, (unsigned)ceil_div(N, TN));  // nbr = number of work items
+    kern<<<grid, WARPS * 32, smem, h.stream>>>(rp, ci, v, B, C, map, M, K, N, items, ws, h.d_err);
     after_launch(h, "bcsr_spmm_f16_mma");
 }
 
@@ -271,33 +295,72 @@ static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb
     bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map, nullptr);
 }
 
+// C[map(16 br + i), n] = sum over the slots of split block row br, in slot order.
+template <typename IT>
+__global__ void mma_split_reduce_kernel(const float* __restrict__ ws,
+                                        const int32_t* __restrict__ long_rows,
+                                        const int32_t* __restrict__ first_slot, int64_t nlong,
+                                        float* __restrict__ C, const IT* __restrict__ row_map,
+                                        int64_t M, int64_t N, unsigned* __restrict__ err) {
+    const int64_t total = nlong * 16 * N;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t l = e / (16 * N), rem = e % (16 * N);
+        const int i = (int)(rem / N);
+        const int64_t n = rem % N;
+        const int64_t r = (int64_t)long_rows[l] * 16 + i;
+        if (r >= M) continue;
+        const int s0 = first_slot[l], s1 = first_slot[l + 1];
+        float acc = ws[((int64_t)s0 * 16 + i) * N + n];
+        for (int sl = s0 + 1; sl < s1; ++sl) acc = __fadd_rn(acc, ws[((int64_t)sl * 16 + i) * N + n]);
+        const int64_t orow = row_map ? (int64_t)row_map[r] : r;
+        if (orow < 0 || orow >= M) {
+            flag_error(err, DERR_PERM_OUT_OF_RANGE);
+            continue;
+        }
+        C[orow * N + n] = acc;
+    }
+}
+
 template <typename IT>
 void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
                        const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map,
-                       const int32_t* order) {
+                       const MmaWork* work) {
     if (nbr == 0 || N == 0 || M == 0) return;
+    const int64_t nwork = work ? work->nitems : nbr;
+    const MmaItem* items = work ? work->items.get() : nullptr;
+    DevBuf<float> wsb(work && work->nslots > 0 ? (size_t)(work->nslots * 16 * N) : 0, h.stream);
+    float* ws = wsb.get();
     XS_REQUIRE(ceil_div(N, 64) <= 65535, XSPMM_STATUS_UNSUPPORTED, "N above 4,194,240 columns");
     const bool aligned = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(v) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(C) % 8 == 0);
     const int warps = N <= 64 ? 1 : (N <= 128 ? 2 : 4);
     if (aligned) {
-        if (warps == 1) launch<IT, 1, true>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
-        else if (warps == 2) launch<IT, 2, true>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
-        else launch<IT, 4, true>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
+        if (warps == 1) launch<IT, 1, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
+        else if (warps == 2) launch<IT, 2, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
+        else launch<IT, 4, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
     } else {
-        if (warps == 1) launch<IT, 1, false>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
-        else if (warps == 2) launch<IT, 2, false>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
-        else launch<IT, 4, false>(h, nbr, rp, ci, v, B, C, M, K, N, map, order);
+        if (warps == 1) launch<IT, 1, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
+        else if (warps == 2) launch<IT, 2, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
+        else launch<IT, 4, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
+    }
+    if (work && work->nlong > 0) {
+        const int64_t total = work->nlong * 16 * N;
+        const unsigned grid = (unsigned)std::max<int64_t>(
+            1, std::min(ceil_div(total, 256), (int64_t)sm_count(h.device) * 16));
+        mma_split_reduce_kernel<IT><<<grid, 256, 0, h.stream>>>(
+            ws, work->long_rows.get(), work->first_slot.get(), work->nlong, C, map, M, N, h.d_err);
+        after_launch(h, "mma_split_reduce");
     }
 }
 
 template void bcsr_spmm_mma_f16<int32_t>(Handle&, int64_t, const int32_t*, const int32_t*,
                                          const __half*, const __half*, float*, int64_t, int64_t,
-                                         int64_t, const int32_t*, const int32_t*);
+                                         int64_t, const int32_t*, const MmaWork*);
 template void bcsr_spmm_mma_f16<int64_t>(Handle&, int64_t, const int64_t*, const int64_t*,
                                          const __half*, const __half*, float*, int64_t, int64_t,
-                                         int64_t, const int64_t*, const int32_t*);
+                                         int64_t, const int64_t*, const MmaWork*);
 
 // Block rows sorted by their first block column (empty rows last): the execution order a plan
 // gives the mma.sync kernel, so that CTAs running together gather nearby rows of B and the gather
@@ -338,8 +401,66 @@ void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT
                                                   r_in.get(), order.get(), (int)nbr, 0, end_bit, s));
     h.launches += 1;
 }
+template <typename IT>
+void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,
+                    const IT* ci, bool by_first_col, MmaWork& out) {
+    cudaStream_t s = h.stream;
+    std::vector<int32_t> order(nbr);
+    if (by_first_col) {
+        DevBuf<int32_t> d_order;
+        block_row_order<IT>(h, nbr, nbc, rp, ci, d_order);
+        XS_CHECK_CUDA(cudaMemcpyAsync(order.data(), d_order.get(), nbr * sizeof(int32_t),
+                                      cudaMemcpyDeviceToHost, s));
+    } else {
+        for (int64_t r = 0; r < nbr; ++r) order[r] = (int32_t)r;
+    }
+    std::vector<IT> hrp(nbr + 1);
+    XS_CHECK_CUDA(cudaMemcpyAsync(hrp.data(), rp, (nbr + 1) * sizeof(IT), cudaMemcpyDeviceToHost, s));
+    XS_CHECK_CUDA(cudaStreamSynchronize(s));
+    // Slices of at most `chunk` blocks: one CTA walks its blocks in sequence, so a block row of
+    // thousands of blocks (the hub rows of a power-law graph) would otherwise set the time of the
+    // whole product.
+    const int64_t chunk = std::max<int64_t>(128, ceil_div(nnzb, (int64_t)sm_count(h.device) * 64));
+    std::vector<MmaItem> items;
+    std::vector<int32_t> long_rows, first_slot;
+    items.reserve(nbr);
+    int32_t slot = 0;
+    for (int64_t t = 0; t < nbr; ++t) {
+        const int32_t r = order[t];
+        const int64_t j0 = (int64_t)hrp[r], len = (int64_t)hrp[r + 1] - j0;
+        if (len <= chunk) {
+            items.push_back(MmaItem{j0, r, (int32_t)len, -1, 0});
+            continue;
+        }
+        long_rows.push_back(r);
+        first_slot.push_back(slot);
+        for (int64_t o = 0; o < len; o += chunk)
+            items.push_back(MmaItem{j0 + o, r, (int32_t)std::min(chunk, len - o), slot++, 0});
+    }
+    first_slot.push_back(slot);
+    XS_REQUIRE(items.size() < (size_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "too many work items");
+    out.nitems = (int64_t)items.size();
+    out.nlong = (int64_t)long_rows.size();
+    out.nslots = slot;
+    out.items = DevBuf<MmaItem>(std::max<size_t>(items.size(), 1), s);
+    XS_CHECK_CUDA(cudaMemcpyAsync(out.items.get(), items.data(), items.size() * sizeof(MmaItem),
+                                  cudaMemcpyHostToDevice, s));
+    out.long_rows = DevBuf<int32_t>(std::max<size_t>(long_rows.size(), 1), s);
+    out.first_slot = DevBuf<int32_t>(first_slot.size(), s);
+    if (!long_rows.empty())
+        XS_CHECK_CUDA(cudaMemcpyAsync(out.long_rows.get(), long_rows.data(),
+                                      long_rows.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    XS_CHECK_CUDA(cudaMemcpyAsync(out.first_slot.get(), first_slot.data(),
+                                  first_slot.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    XS_CHECK_CUDA(cudaStreamSynchronize(s));  // the host vectors go out of scope
+}
+
 template void block_row_order<int32_t>(Handle&, int64_t, int64_t, const int32_t*, const int32_t*,
                                        DevBuf<int32_t>&);
+template void mma_work_build<int32_t>(Handle&, int64_t, int64_t, int64_t, const int32_t*,
+                                      const int32_t*, bool, MmaWork&);
+template void mma_work_build<int64_t>(Handle&, int64_t, int64_t, int64_t, const int64_t*,
+                                      const int64_t*, bool, MmaWork&);
 template void block_row_order<int64_t>(Handle&, int64_t, int64_t, const int64_t*, const int64_t*,
                                        DevBuf<int32_t>&);
 
