@@ -396,43 +396,74 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     // A column is heavy when its window slice is long at the time it joins p
                     // (hub columns against small patterns); against a large pattern the window
                     // sits in high size classes and even hub columns are light.
-                    // Columns are taken CL_THREADS at a time, one per thread, and their slices
-                    // walked as one flattened range by the whole CTA: a pattern of hundreds of
-                    // columns costs a few round trips, not a few per column.
                     const int t_first = shi != sh.wshi ? 0 : sh.nproc;
                     const int nproc0 = sh.nproc;
-                    for (int c0 = t_first; c0 < pc; c0 += CL_THREADS) {
-                        const int t = c0 + tid;
-                        int64_t e_beg = 0, e_cnt = 0;
-                        if (t < pc) {
-                            const int b = a.plist[t];
-                            const int64_t* ib = a.iptr + (int64_t)b * NCLS;
-                            bool light = true;
-                            if (t >= nproc0) {
-                                if (ib[shi + 1] - ib[slo] > HEAVY) {
-                                    a.hstamp[b] = pass;
-                                    a.hlist[atomicAdd(&sh.nheavy, 1)] = b;
-                                    light = false;
-                                }
-                            } else if (a.hstamp[b] == pass) {
-                                light = false;
+                    // Column t of p: its slice of the window still to walk ([e_beg, e_beg +
+                    // e_cnt)), or none if it is heavy. A column that joined p since the last walk
+                    // (t >= nproc0) has not been walked in this pass: its slice starts at slo.
+                    struct Col {
+                        int b, kind;  // kind: 0 light, 1 heavy (new), 2 heavy (known)
+                        int64_t e_beg, e_cnt;
+                    };
+                    auto column = [&](int t) {
+                        Col c{a.plist[t], 0, 0, 0};
+                        const int64_t* ib = a.iptr + (int64_t)c.b * NCLS;
+                        int from = slo;
+                        if (t >= nproc0) {
+                            if (ib[shi + 1] - ib[slo] > HEAVY) {
+                                c.kind = 1;
+                                return c;
                             }
-                            if (light) {
-                                const int from = a.cstamp[b] == pass ? max(a.cslot[b], slo) : slo;
-                                a.cstamp[b] = pass;
-                                a.cslot[b] = shi + 1;
-                                if (from <= shi) {
-                                    e_beg = ib[from];
-                                    e_cnt = ib[shi + 1] - e_beg;
-                                }
+                        } else {
+                            if (a.hstamp[c.b] == pass) {
+                                c.kind = 2;
+                                return c;
                             }
+                            if (a.cstamp[c.b] == pass) from = max(a.cslot[c.b], slo);
                         }
-                        flat_walk(sh, a.ient, e_beg, e_cnt, [&](int2 en) {
-                            const int pr = st.p(en.x);
-                            if (pr < 0 || pr >= limit) return;
-                            if (atomicAdd(&a.cnt[en.x], 1) == 0)
-                                append_candidate(sh, a, en.x, en.y, pr);
-                        });
+                        if (from <= shi) {
+                            c.e_beg = ib[from];
+                            c.e_cnt = ib[shi + 1] - c.e_beg;
+                        }
+                        return c;
+                    };
+                    auto record = [&](const Col& c) {
+                        if (c.kind == 1) {
+                            a.hstamp[c.b] = pass;
+                            a.hlist[atomicAdd(&sh.nheavy, 1)] = c.b;
+                        } else if (c.kind == 0) {
+                            a.cstamp[c.b] = pass;
+                            a.cslot[c.b] = shi + 1;
+                        }
+                    };
+                    auto hit = [&](int2 en) {
+                        const int pr = st.p(en.x);
+                        if (pr < 0 || pr >= limit) return;
+                        if (atomicAdd(&a.cnt[en.x], 1) == 0) append_candidate(sh, a, en.x, en.y, pr);
+                    };
+                    if (pc - t_first <= 2 * (CL_THREADS / 32)) {
+                        // few columns: one warp per column, no CTA-wide scan
+                        for (int t = t_first + warp; t < pc; t += CL_THREADS / 32) {
+                            const Col c = column(t);
+                            __syncwarp();
+                            if (lane == 0) record(c);
+                            for (int64_t e = c.e_beg + lane; e < c.e_beg + c.e_cnt; e += 32)
+                                hit(a.ient[e]);
+                        }
+                    } else {
+                        // many columns (large patterns): CL_THREADS at a time, one per thread,
+                        // their slices walked as one flattened range by the whole CTA
+                        for (int c0 = t_first; c0 < pc; c0 += CL_THREADS) {
+                            const int t = c0 + tid;
+                            int64_t e_beg = 0, e_cnt = 0;
+                            if (t < pc) {
+                                const Col c = column(t);
+                                record(c);
+                                e_beg = c.e_beg;
+                                e_cnt = c.e_cnt;
+                            }
+                            flat_walk(sh, a.ient, e_beg, e_cnt, hit);
+                        }
                     }
                     __syncthreads();
                     if (tid == 0) {

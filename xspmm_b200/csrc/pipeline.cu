@@ -117,7 +117,10 @@ void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
         // When B is well beyond what L2 holds, run the block rows in order of their first
         // block column so that CTAs in flight together gather nearby rows of B.
         const bool big_b = (double)K * (double)N * sizeof(__half) > 48.0 * (1 << 20);
-        if (nbr > 0 && (!work_built || (big_b && !work_sorted))) {
+        // A single product of a small matrix does not repay building the list (one host
+        // round trip); a large one does (long rows would serialize on one CTA).
+        const bool want_work = !one_shot || nnzb >= (int64_t(1) << 18);
+        if (want_work && nbr > 0 && (!work_built || (big_b && !work_sorted))) {
             work = MmaWork();
             mma_work_build<IT>(h, nbr, nbc, nnzb, rp, ci, big_b, work);
             work_built = true;
@@ -134,6 +137,7 @@ void spmm_csr_pipeline(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* r
                        const IT* col_ind, const VT* values, const VT* B, float* C, int64_t N,
                        int64_t hw, bool clustering, xspmm_timings_t* timings) {
     Plan<VT, IT> plan;
+    plan.one_shot = true;
     plan_from_csr<VT, IT>(h, M, K, nnz, row_ptr, col_ind, values, hw, clustering,
                           timings != nullptr, plan);
     plan.execute(h, B, C, N);

@@ -42,6 +42,7 @@ struct Plan final : PlanBase {
     MmaWork work;  // work list of the mma.sync kernel (order, split long rows)
     bool work_built = false;
     bool work_sorted = false;
+    bool one_shot = false;  // built for a single product (the Tier-2 call)
 
     void execute(Handle& h, const void* B, float* C, int64_t N) override;
     void prepare_tc(Handle& h) override;
