@@ -43,6 +43,11 @@ METRIC = "SpMM effective TFLOPS (2*nnz*N/s), Tier-2 pipeline with clustering + c
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+# DRAM bytes (read + write) of one cluster_kernel launch on the cfg2 workload, from the ncu capture
+# summarised in profiles/cluster_kernel_cfg2.md (1.265 MB read + 9.5 KB written).
+CLUSTER_TRAFFIC_BYTES = 1264896 + 9472
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -357,8 +362,14 @@ def run_gpu(args):
                 "bound": "hbm", "achieved": round(achieved, 2),
                 "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 5),
-                "traffic": None, "peak_source": pk["source"],
-                "note": "dominant stage of the timed step; achieved = algorithmic bytes / stage time"}
+                "traffic": CLUSTER_TRAFFIC_BYTES if dom == "clustering_ms" else None,
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                   "cluster_kernel launch on this workload "
+                                   "(profiles/cluster_kernel_cfg2.md)") if dom == "clustering_ms" else None,
+                "peak_source": pk["source"],
+                "note": "dominant stage of the timed step; achieved = algorithmic bytes / stage time; "
+                        "latency-bound (one CTA, serial across clusters), so the fraction is small "
+                        "by construction"}
     t1_bytes = bytes_stage["spmm_ms"]
     tier1 = {
         "ms": round(t1_max, 4),
