@@ -188,15 +188,46 @@ struct Shared {
     int holes[HOLE_CAP];              // first HOLE_CAP holes of the pass
 };
 
-// Rows' positions and U live in shared memory when they fit (SU), else in global memory.
-template <bool SU>
+// Rows' positions and U live in shared memory when they fit (SU), else in global memory. The
+// per-row hit counters live in shared memory too when there is room and a light count fits in 15
+// bits (SC): two 16-bit counters per word (bit 15 = found through a heavy column), so a hit is a
+// shared-memory atomic instead of an L2 round trip.
+template <bool SU, bool SC>
 struct RowState {
     int32_t* U;
     int32_t* pos;
+    int32_t* gcnt;   // global counters (SC false)
+    uint32_t* scnt;  // shared counters (SC true)
     __device__ __forceinline__ int u(int i) const { return U[i]; }
     __device__ __forceinline__ void set_u(int i, int v) const { U[i] = v; }
     __device__ __forceinline__ int p(int r) const { return pos[r]; }
     __device__ __forceinline__ void set_p(int r, int v) const { pos[r] = v; }
+    // one light hit; returns the previous value (0: first time the row is touched this pass)
+    __device__ __forceinline__ int cnt_add(int r) const {
+        if constexpr (SC) {
+            const int sft = (r & 1) * 16;
+            return (int)((atomicAdd(&scnt[r >> 1], 1u << sft) >> sft) & 0xFFFFu);
+        } else {
+            return atomicAdd(&gcnt[r], 1);
+        }
+    }
+    // marks a row found through a heavy column; returns the previous value
+    __device__ __forceinline__ int cnt_heavy(int r) const {
+        if constexpr (SC) {
+            const int sft = (r & 1) * 16;
+            return (int)((atomicOr(&scnt[r >> 1], 0x8000u << sft) >> sft) & 0xFFFFu);
+        } else {
+            return atomicOr(&gcnt[r], HEAVY_MARK);
+        }
+    }
+    __device__ __forceinline__ int cnt_light(int r) const {
+        if constexpr (SC) return (int)((scnt[r >> 1] >> ((r & 1) * 16)) & 0x7FFFu);
+        else return gcnt[r] & LIGHT_MASK;
+    }
+    __device__ __forceinline__ void cnt_clear(int r) const {
+        if constexpr (SC) atomicAnd(&scnt[r >> 1], ~(0xFFFFu << ((r & 1) * 16)));
+        else gcnt[r] = 0;
+    }
 };
 
 __device__ __forceinline__ void cand_get(const Shared& sh, const ClusterArgs& a, int buf, int c,
@@ -278,14 +309,18 @@ __device__ __forceinline__ bool pattern_has(const int32_t* qcol, int64_t b, int6
     return false;
 }
 
-template <bool SU>
+template <bool SU, bool SC>
 __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
+    static_assert(SU || !SC, "shared counters need U/pos in shared memory");
     __shared__ Shared sh;
     extern __shared__ int32_t dyn[];
-    RowState<SU> st;
+    RowState<SU, SC> st;
+    st.gcnt = a.cnt;
+    st.scnt = nullptr;
     if constexpr (SU) {
         st.U = dyn;
         st.pos = dyn + a.M;
+        if constexpr (SC) st.scnt = reinterpret_cast<uint32_t*>(dyn + 2 * a.M);
     } else {
         st.U = a.U;
         st.pos = a.pos;
@@ -296,6 +331,8 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
             st.U[i] = i;
             st.pos[i] = i;
         }
+        if constexpr (SC)
+            for (int i = tid; i < (a.M + 1) / 2; i += CL_THREADS) st.scnt[i] = 0u;
     }
     if (tid == 0) {
         sh.n = a.M;
@@ -439,7 +476,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     auto hit = [&](int2 en) {
                         const int pr = st.p(en.x);
                         if (pr < 0 || pr >= limit) return;
-                        if (atomicAdd(&a.cnt[en.x], 1) == 0) append_candidate(sh, a, en.x, en.y, pr);
+                        if (st.cnt_add(en.x) == 0) append_candidate(sh, a, en.x, en.y, pr);
                     };
                     if (pc - t_first <= 2 * (CL_THREADS / 32)) {
                         // few columns: one warp per column, no CTA-wide scan
@@ -524,7 +561,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             if ((int64_t)en.y < m) return;
                             const int pr = st.p(en.x);
                             if (pr < 0 || pr >= limit) return;
-                            if (atomicOr(&a.cnt[en.x], HEAVY_MARK) == 0)
+                            if (st.cnt_heavy(en.x) == 0)
                                 append_candidate(sh, a, en.x, en.y, pr);
                         });
                     }
@@ -546,7 +583,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                 for (int c = tid; c < ncand; c += CL_THREADS) {
                     int r, len, pr;
                     cand_get(sh, a, buf, c, r, len, pr);
-                    int64_t inter = a.cnt[r] & LIGHT_MASK;
+                    int64_t inter = st.cnt_light(r);
                     // Light hits are exact; each heavy column adds at most one. The distance is
                     // non-increasing in the intersection (fixed |p| + |q|), so a candidate that
                     // fails even with every heavy column counted is rejected without reading its
@@ -587,7 +624,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     if (pr < smax) {
                         cand_set(sh, a, buf ^ 1, atomicAdd(&sh.nkeep, 1), r, len, pr);
                     } else {
-                        a.cnt[r] = 0;
+                        st.cnt_clear(r);
                         if (flag_get(sh, a, c)) {
                             const int slot = atomicAdd(&sh.nr, 1);
                             const uint64_t kv = ((uint64_t)(uint32_t)pr << 32) | (uint32_t)r;
@@ -903,13 +940,21 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     a.tau = tau;
     a.t_lo = (1.0 - (double)tau) - 1.0 / (double)(1 << 22);
     a.err = h.d_err;
-    if (M <= SMEM_ROWS) {
-        const size_t dyn = (size_t)M * 2 * sizeof(int32_t);
-        XS_CHECK_CUDA(cudaFuncSetAttribute(cluster_kernel<true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
-        cluster_kernel<true><<<1, CL_THREADS, dyn, s>>>(a);
+    int smem_optin = 0;
+    XS_CHECK_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                                         h.device));
+    const size_t dyn_u = (size_t)M * 2 * sizeof(int32_t);
+    const size_t dyn_c = dyn_u + (size_t)((M + 1) / 2) * sizeof(uint32_t);
+    if (M <= SMEM_ROWS && nbc < 32768 && dyn_c + sizeof(Shared) + 1024 <= (size_t)smem_optin) {
+        XS_CHECK_CUDA(cudaFuncSetAttribute(cluster_kernel<true, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_c));
+        cluster_kernel<true, true><<<1, CL_THREADS, dyn_c, s>>>(a);
+    } else if (M <= SMEM_ROWS) {
+        XS_CHECK_CUDA(cudaFuncSetAttribute(cluster_kernel<true, false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_u));
+        cluster_kernel<true, false><<<1, CL_THREADS, dyn_u, s>>>(a);
     } else {
-        cluster_kernel<false><<<1, CL_THREADS, 0, s>>>(a);
+        cluster_kernel<false, false><<<1, CL_THREADS, 0, s>>>(a);
     }
     after_launch(h, "cluster_greedy");
     store_perm_kernel<IT><<<grid_1d(h, M, 256), 256, 0, s>>>(perm32.get(), perm, M);
