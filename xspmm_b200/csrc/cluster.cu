@@ -69,6 +69,8 @@ struct ClusterArgs {
                             //       window-gathered heavy set
     int32_t* cslot;         // [nbc] next size class to walk / gather for that column
     int32_t* hstamp;        // [nbc] pass in which the column was classified heavy
+    const longlong2* qslice;  // [pattern entries] slice of the entry's inverted list over the
+                              //   size window of a pattern of the row's own size
     uint32_t* pbits;        // [ceil(nbc/32)] pattern of the current cluster
     int32_t* plist;         // [nbc] columns of p, in insertion order
     int32_t* hlist;         // [nbc] heavy columns of p
@@ -276,6 +278,24 @@ __device__ __forceinline__ void append_candidate(Shared& sh, ClusterArgs& a, int
     else flag_error(a.err, DERR_INTERNAL);
 }
 
+// One warp walks the inverted-list entries [e_beg, e_end), four loads in flight per lane (the
+// entries are L2 round trips; issuing them one after another would serialize them).
+template <typename F>
+__device__ __forceinline__ void warp_walk(const int2* ient, int64_t e_beg, int64_t e_end, int lane,
+                                          F&& f) {
+    for (int64_t e0 = e_beg; e0 < e_end; e0 += 128) {
+        int2 en[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t e = e0 + lane + 32 * u;
+            if (e < e_end) en[u] = ient[e];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (e0 + lane + 32 * u < e_end) f(en[u]);
+    }
+}
+
 // Walks the entries of up to CL_THREADS inverted-list slices (one per thread) spread over the
 // whole CTA.
 template <typename F>
@@ -287,13 +307,22 @@ __device__ void flat_walk(Shared& sh, const int2* ient, int64_t e_beg, int64_t e
     if (tid == CL_THREADS - 1) sh.col_off[CL_THREADS] = off + e_cnt;
     __syncthreads();
     const int64_t total = sh.total64;
-    for (int64_t fi = tid; fi < total; fi += CL_THREADS) {
-        int lo = 0, hi = CL_THREADS - 1;  // last slice with col_off <= fi (a non-empty one)
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (sh.col_off[mid] <= fi) lo = mid; else hi = mid - 1;
+    for (int64_t f0 = tid; f0 < total; f0 += 4 * CL_THREADS) {
+        int2 en[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t fi = f0 + (int64_t)u * CL_THREADS;
+            if (fi >= total) break;
+            int lo = 0, hi = CL_THREADS - 1;  // last slice with col_off <= fi (a non-empty one)
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (sh.col_off[mid] <= fi) lo = mid; else hi = mid - 1;
+            }
+            en[u] = ient[sh.col_beg[lo] + (fi - sh.col_off[lo])];
         }
-        f(ient[sh.col_beg[lo] + (fi - sh.col_off[lo])]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (f0 + (int64_t)u * CL_THREADS < total) f(en[u]);
     }
     __syncthreads();
 }
@@ -339,30 +368,93 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
         sh.out = 0;
         sh.pass = 0;
         sh.stop = 0;
+        sh.ncand = 0;  // the first walk of a pass appends to these before its first barrier
+        sh.nheavy = 0;
+        sh.cur = 0;
     }
     __syncthreads();
 
     while (sh.n > 0 && !sh.stop) {
-        if (tid == 0) {
-            const int seed = st.u(sh.n - 1);
-            if (seed < 0 || seed >= a.M || sh.out >= a.M) {
-                flag_error(a.err, DERR_INTERNAL);
-                sh.stop = 1;
+        // Pass start without a barrier: every thread reads the seed (U.back()) and its pattern,
+        // and the first walk of p's columns runs straight from the seed's pattern entries and
+        // their precomputed window slices, so the chain of dependent loads before the first
+        // barrier is seed -> pattern -> inverted-list slice -> counter. The seed is at position
+        // n = |U| - 1, outside every candidate test (pos < limit = n).
+        const int pass = sh.pass;
+        const int n_old = sh.n;
+        const int out0 = sh.out;
+        const int seed = st.u(n_old - 1);
+        if (seed < 0 || seed >= a.M || out0 >= a.M) {  // uniform: all threads read the same state
+            if (tid == 0) flag_error(a.err, DERR_INTERNAL);
+            break;
+        }
+        const int n = n_old - 1;
+        const int64_t s0 = a.qptr[seed];
+        const int64_t slen = a.qptr[seed + 1] - s0;
+        if (slen > 0) {
+            const int64_t m0 = min_inter(a.t_lo, slen), ub0 = max_len(a.t_lo, slen);
+            const int slo0 = slot_of(m0), shi0 = slot_of(ub0 < NCLS ? ub0 : NCLS);
+            auto first_hit = [&](int2 en) {
+                const int pr = st.p(en.x);
+                if (pr < 0 || pr >= n) return;
+                if (st.cnt_add(en.x) == 0) append_candidate(sh, a, en.x, en.y, pr);
+            };
+            // column t of the seed: record it in p, classify it, return its window slice
+            auto first_column = [&](int t, bool writer, int64_t& e_beg, int64_t& e_cnt) {
+                const int b = a.qcol[s0 + t];
+                const longlong2 sl = a.qslice[s0 + t];
+                e_beg = sl.x;
+                e_cnt = sl.y - sl.x;
+                const bool heavy = e_cnt > HEAVY;
+                if (writer) {
+                    atomicOr(&a.pbits[b >> 5], 1u << (b & 31));
+                    a.plist[t] = b;
+                    if (heavy) {
+                        a.hstamp[b] = pass;
+                        a.hlist[atomicAdd(&sh.nheavy, 1)] = b;
+                    } else {
+                        a.cstamp[b] = pass;
+                        a.cslot[b] = shi0 + 1;
+                    }
+                }
+                if (heavy) e_cnt = 0;
+            };
+            if (slen <= 2 * (CL_THREADS / 32)) {
+                for (int t = warp; t < slen; t += CL_THREADS / 32) {
+                    int64_t e_beg, e_cnt;
+                    first_column(t, lane == 0, e_beg, e_cnt);
+                    warp_walk(a.ient, e_beg, e_beg + e_cnt, lane, first_hit);
+                }
             } else {
-                sh.seed = seed;
-                sh.n -= 1;
-                st.set_p(seed, -1);
-                a.perm[sh.out++] = seed;
-                sh.k = 0;
+                for (int64_t c0 = 0; c0 < slen; c0 += CL_THREADS) {
+                    const int64_t t = c0 + tid;
+                    int64_t e_beg = 0, e_cnt = 0;
+                    if (t < slen) first_column((int)t, true, e_beg, e_cnt);
+                    flat_walk(sh, a.ient, e_beg, e_cnt, first_hit);
+                }
             }
         }
         __syncthreads();
-        if (sh.stop) break;
-        const int pass = sh.pass;
-        const int seed = sh.seed;
-        const int n = sh.n;
-        const int64_t s0 = a.qptr[seed];
-        const int64_t slen = a.qptr[seed + 1] - s0;
+        if (tid == 0) {
+            sh.seed = seed;
+            sh.n = n;
+            st.set_p(seed, -1);
+            a.perm[out0] = seed;
+            sh.out = out0 + 1;
+            sh.k = 0;
+            if (slen > 0) {
+                sh.pcount = (int)slen;
+                sh.nproc = (int)slen;  // walked above
+                sh.wshi = slot_of(max_len(a.t_lo, slen) < NCLS ? max_len(a.t_lo, slen) : NCLS);
+                sh.hg = 0;
+                sh.limit = n;
+                sh.grown = 1;  // the heavy-column step of the first round still has to run
+                sh.m = min_inter(a.t_lo, slen);
+                sh.ub = max_len(a.t_lo, slen);
+                sh.need = (int)(slen - sh.m + 1);
+            }
+        }
+        __syncthreads();
 
         if (slen == 0) {
             // Empty pattern: accepts exactly the empty rows, in decreasing position order.
@@ -391,27 +483,6 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                 __syncthreads();
             }
         } else {
-            for (int t = tid; t < slen; t += CL_THREADS) {  // p = q_seed
-                const int b = a.qcol[s0 + t];
-                atomicOr(&a.pbits[b >> 5], 1u << (b & 31));
-                a.plist[t] = b;
-            }
-            if (tid == 0) {
-                sh.pcount = (int)slen;
-                sh.nproc = 0;
-                sh.wshi = -1;
-                sh.nheavy = 0;
-                sh.hg = 0;
-                sh.ncand = 0;
-                sh.limit = n;
-                sh.grown = 1;
-                sh.cur = 0;
-                sh.m = min_inter(a.t_lo, slen);
-                sh.ub = max_len(a.t_lo, slen);
-                sh.need = (int)(slen - sh.m + 1);
-            }
-            __syncthreads();
-
             for (int round = 0;; ++round) {
                 if (round > a.M + 1) {  // each round settles >= 1 candidate
                     if (tid == 0) { flag_error(a.err, DERR_INTERNAL); sh.stop = 1; }
@@ -484,8 +555,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             const Col c = column(t);
                             __syncwarp();
                             if (lane == 0) record(c);
-                            for (int64_t e = c.e_beg + lane; e < c.e_beg + c.e_cnt; e += 32)
-                                hit(a.ient[e]);
+                            warp_walk(a.ient, c.e_beg, c.e_beg + c.e_cnt, lane, hit);
                         }
                     } else {
                         // many columns (large patterns): CL_THREADS at a time, one per thread,
@@ -746,6 +816,9 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
         if (tid == 0) {
             sh.n = n - k;
             sh.pass += 1;
+            sh.ncand = 0;
+            sh.nheavy = 0;
+            sh.cur = 0;  // the next first walk appends to candidate buffer 0
             if (sh.out > a.M) { flag_error(a.err, DERR_INTERNAL); sh.stop = 1; }
         }
         __syncthreads();
@@ -759,6 +832,25 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
 }
 
 // --- preprocessing kernels -----------------------------------------------------------------------
+
+// For every pattern entry (row r, block column b): the slice of b's inverted list over the size
+// window a pattern of |r| columns admits (fact 2) -- where the first walk of a pass seeded by r
+// starts and ends, with no lookup of the index at pass time.
+__global__ void qslice_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ qcol,
+                              int32_t M, const int64_t* __restrict__ iptr, double t_lo,
+                              longlong2* __restrict__ qslice) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < M;
+         r += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j0 = qptr[r], j1 = qptr[r + 1], len = j1 - j0;
+        if (len == 0) continue;
+        const int64_t m = min_inter(t_lo, len), ub = max_len(t_lo, len);
+        const int slo = slot_of(m), shi = slot_of(ub < NCLS ? ub : NCLS);
+        for (int64_t j = j0; j < j1; ++j) {
+            const int64_t* ib = iptr + (int64_t)qcol[j] * NCLS;
+            qslice[j] = make_longlong2(ib[slo], ib[shi + 1]);
+        }
+    }
+}
 
 __global__ void init_rows_kernel(int32_t* U, int32_t* pos, int32_t* cnt, int32_t M) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M;
@@ -895,6 +987,11 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
                                           ient.get());
     after_launch(h, "inv_fill");
     cursor.release();
+    const double t_lo = (1.0 - (double)tau) - 1.0 / (double)(1 << 22);
+    DevBuf<longlong2> qslice(std::max<int64_t>(npat, 1), s);
+    qslice_kernel<<<grid_1d(h, M, 256), 256, 0, s>>>(qptr.get(), qcol.get(), (int32_t)M,
+                                                      iptr.get(), t_lo, qslice.get());
+    after_launch(h, "cluster_qslice");
 
     // State of the greedy loop.
     int sort_cap = 1;
@@ -938,7 +1035,8 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     a.holes = holes.get();
     a.perm = perm32.get();
     a.tau = tau;
-    a.t_lo = (1.0 - (double)tau) - 1.0 / (double)(1 << 22);
+    a.t_lo = t_lo;
+    a.qslice = qslice.get();
     a.err = h.d_err;
     int smem_optin = 0;
     XS_CHECK_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
