@@ -371,6 +371,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
         sh.ncand = 0;  // the first walk of a pass appends to these before its first barrier
         sh.nheavy = 0;
         sh.cur = 0;
+        sh.nr = 0;
     }
     __syncthreads();
 
@@ -435,341 +436,398 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
             }
         }
         __syncthreads();
-        if (tid == 0) {
-            sh.seed = seed;
-            sh.n = n;
-            st.set_p(seed, -1);
-            a.perm[out0] = seed;
-            sh.out = out0 + 1;
-            sh.k = 0;
-            if (slen > 0) {
-                sh.pcount = (int)slen;
-                sh.nproc = (int)slen;  // walked above
-                sh.wshi = slot_of(max_len(a.t_lo, slen) < NCLS ? max_len(a.t_lo, slen) : NCLS);
-                sh.hg = 0;
-                sh.limit = n;
-                sh.grown = 1;  // the heavy-column step of the first round still has to run
-                sh.m = min_inter(a.t_lo, slen);
-                sh.ub = max_len(a.t_lo, slen);
-                sh.need = (int)(slen - sh.m + 1);
-            }
-        }
-        __syncthreads();
 
-        if (slen == 0) {
-            // Empty pattern: accepts exactly the empty rows, in decreasing position order.
-            for (int hi = n; hi > 0; hi -= CL_THREADS) {
-                const int i = hi - 1 - tid;
-                int f = 0, r = -1;
-                if (i >= 0) {
-                    r = st.u(i);
-                    f = (a.qptr[r + 1] == a.qptr[r]) ? 1 : 0;
+        // Fast path for the common pass: at most CL_THREADS candidates, no heavy column and no
+        // accepted row that adds columns to p. Then every candidate is decided against the seed's
+        // pattern alone and nothing depends on the order of the decisions: evaluate, rank the
+        // accepted rows by position, done -- a handful of barriers instead of the general round
+        // loop. Anything else (growth, heavy columns, many candidates, an empty seed) goes through
+        // the general path, which starts from the same state (the evaluation writes nothing).
+        bool fast_done = false;
+        {
+            const int ncand0 = sh.ncand;
+            const bool fast = slen > 0 && ncand0 <= CL_THREADS && sh.nheavy == 0;
+            int r = -1, len = 0, pr = -1, acc = 0, grow = 0;
+            if (fast && tid < ncand0) {
+                cand_get(sh, a, 0, tid, r, len, pr);
+                const int64_t inter = st.cnt_light(r);
+                acc = jaccard_distance(inter, slen + (int64_t)len - inter) <= a.tau ? 1 : 0;
+                grow = acc && len > inter;
+            }
+            const int any_grow = __syncthreads_or(grow);
+            if (fast && !any_grow) {
+                if (tid < ncand0) {
+                    st.cnt_clear(r);
+                    if (acc) sh.sortbuf[atomicAdd(&sh.nr, 1)] = ((uint64_t)(uint32_t)pr << 32) |
+                                                                 (uint32_t)r;
                 }
-                const int idx = cta_excl_scan(f, sh.s_warp, &sh.total);
-                if (f) {
-                    if (sh.out + idx < a.M && sh.k + idx < a.M) {
-                        a.perm[sh.out + idx] = r;
-                        hole_set(sh, a, sh.k + idx, i);
-                        st.set_p(r, -1);
+                for (int64_t t = tid; t < slen; t += CL_THREADS) {
+                    const int b = a.qcol[s0 + t];
+                    a.pbits[b >> 5] = 0u;
+                }
+                __syncthreads();
+                const int nr = sh.nr;  // <= ncand0 <= CL_THREADS
+                if (tid < nr) {        // decreasing position order, ranked by counting
+                    const uint64_t kv = sh.sortbuf[tid];
+                    int rank = 0;
+                    for (int j = 0; j < nr; ++j) rank += sh.sortbuf[j] > kv;
+                    const int rr = (int)(uint32_t)kv, pp = (int)(kv >> 32);
+                    if (out0 + 1 + rank < a.M) {
+                        a.perm[out0 + 1 + rank] = rr;
+                        hole_set(sh, a, rank, pp);
+                        st.set_p(rr, -1);
                     } else {
                         flag_error(a.err, DERR_INTERNAL);
                     }
                 }
-                __syncthreads();
                 if (tid == 0) {
-                    sh.out += sh.total;
-                    sh.k += sh.total;
+                    sh.seed = seed;
+                    sh.n = n;
+                    st.set_p(seed, -1);
+                    a.perm[out0] = seed;
+                    sh.out = out0 + 1 + nr;
+                    sh.k = nr;  // sh.nr is cleared at the end of the pass
                 }
-                __syncthreads();
+                fast_done = true;
             }
-        } else {
-            for (int round = 0;; ++round) {
-                if (round > a.M + 1) {  // each round settles >= 1 candidate
-                    if (tid == 0) { flag_error(a.err, DERR_INTERNAL); sh.stop = 1; }
-                    __syncthreads();
-                    break;
+        }
+        if (!fast_done) {
+            if (tid == 0) {
+                sh.seed = seed;
+                sh.n = n;
+                st.set_p(seed, -1);
+                a.perm[out0] = seed;
+                sh.out = out0 + 1;
+                sh.k = 0;
+                if (slen > 0) {
+                    sh.pcount = (int)slen;
+                    sh.nproc = (int)slen;  // walked above
+                    sh.wshi = slot_of(max_len(a.t_lo, slen) < NCLS ? max_len(a.t_lo, slen) : NCLS);
+                    sh.hg = 0;
+                    sh.limit = n;
+                    sh.grown = 1;  // the heavy-column step of the first round still has to run
+                    sh.m = min_inter(a.t_lo, slen);
+                    sh.ub = max_len(a.t_lo, slen);
+                    sh.need = (int)(slen - sh.m + 1);
                 }
-                if (sh.grown) {
-                    const int64_t m = sh.m, ub = sh.ub;
-                    const int limit = sh.limit;
-                    const int pc = sh.pcount;
-                    const int slo = slot_of(m), shi = slot_of(ub < NCLS ? ub : NCLS);
-                    // (1) Columns of p with a short ("light") list: one warp walks the size
-                    // window [m, ub] of the list and every eligible row on it gets one hit, so
-                    // |q n p| over light columns is a counter for every row the window admits
-                    // (a row's size class is the same in all of its columns). Each column keeps
-                    // the first class it has not walked; when p grows the window only widens
-                    // upwards, so old columns walk just the newly admitted classes and no
-                    // (column, row) pair is counted twice. Heavy lists are set aside.
-                    // A column is heavy when its window slice is long at the time it joins p
-                    // (hub columns against small patterns); against a large pattern the window
-                    // sits in high size classes and even hub columns are light.
-                    const int t_first = shi != sh.wshi ? 0 : sh.nproc;
-                    const int nproc0 = sh.nproc;
-                    // Column t of p: its slice of the window still to walk ([e_beg, e_beg +
-                    // e_cnt)), or none if it is heavy. A column that joined p since the last walk
-                    // (t >= nproc0) has not been walked in this pass: its slice starts at slo.
-                    struct Col {
-                        int b, kind;  // kind: 0 light, 1 heavy (new), 2 heavy (known)
-                        int64_t e_beg, e_cnt;
-                    };
-                    auto column = [&](int t) {
-                        Col c{a.plist[t], 0, 0, 0};
-                        const int64_t* ib = a.iptr + (int64_t)c.b * NCLS;
-                        int from = slo;
-                        if (t >= nproc0) {
-                            if (ib[shi + 1] - ib[slo] > HEAVY) {
-                                c.kind = 1;
-                                return c;
-                            }
+            }
+            __syncthreads();
+
+            if (slen == 0) {
+                // Empty pattern: accepts exactly the empty rows, in decreasing position order.
+                for (int hi = n; hi > 0; hi -= CL_THREADS) {
+                    const int i = hi - 1 - tid;
+                    int f = 0, r = -1;
+                    if (i >= 0) {
+                        r = st.u(i);
+                        f = (a.qptr[r + 1] == a.qptr[r]) ? 1 : 0;
+                    }
+                    const int idx = cta_excl_scan(f, sh.s_warp, &sh.total);
+                    if (f) {
+                        if (sh.out + idx < a.M && sh.k + idx < a.M) {
+                            a.perm[sh.out + idx] = r;
+                            hole_set(sh, a, sh.k + idx, i);
+                            st.set_p(r, -1);
                         } else {
-                            if (a.hstamp[c.b] == pass) {
-                                c.kind = 2;
-                                return c;
-                            }
-                            if (a.cstamp[c.b] == pass) from = max(a.cslot[c.b], slo);
-                        }
-                        if (from <= shi) {
-                            c.e_beg = ib[from];
-                            c.e_cnt = ib[shi + 1] - c.e_beg;
-                        }
-                        return c;
-                    };
-                    auto record = [&](const Col& c) {
-                        if (c.kind == 1) {
-                            a.hstamp[c.b] = pass;
-                            a.hlist[atomicAdd(&sh.nheavy, 1)] = c.b;
-                        } else if (c.kind == 0) {
-                            a.cstamp[c.b] = pass;
-                            a.cslot[c.b] = shi + 1;
-                        }
-                    };
-                    auto hit = [&](int2 en) {
-                        const int pr = st.p(en.x);
-                        if (pr < 0 || pr >= limit) return;
-                        if (st.cnt_add(en.x) == 0) append_candidate(sh, a, en.x, en.y, pr);
-                    };
-                    if (pc - t_first <= 2 * (CL_THREADS / 32)) {
-                        // few columns: one warp per column, no CTA-wide scan
-                        for (int t = t_first + warp; t < pc; t += CL_THREADS / 32) {
-                            const Col c = column(t);
-                            __syncwarp();
-                            if (lane == 0) record(c);
-                            warp_walk(a.ient, c.e_beg, c.e_beg + c.e_cnt, lane, hit);
-                        }
-                    } else {
-                        // many columns (large patterns): CL_THREADS at a time, one per thread,
-                        // their slices walked as one flattened range by the whole CTA
-                        for (int c0 = t_first; c0 < pc; c0 += CL_THREADS) {
-                            const int t = c0 + tid;
-                            int64_t e_beg = 0, e_cnt = 0;
-                            if (t < pc) {
-                                const Col c = column(t);
-                                record(c);
-                                e_beg = c.e_beg;
-                                e_cnt = c.e_cnt;
-                            }
-                            flat_walk(sh, a.ient, e_beg, e_cnt, hit);
+                            flag_error(a.err, DERR_INTERNAL);
                         }
                     }
                     __syncthreads();
                     if (tid == 0) {
-                        sh.nproc = pc;
-                        sh.wshi = shi;
+                        sh.out += sh.total;
+                        sh.k += sh.total;
                     }
-                    // (2) Heavy columns are needed only when the light ones are fewer than
-                    // |p| - m + 1; then take the cheapest ones over the size window [m, ub].
-                    const int nheavy = sh.nheavy;
-                    const int want = sh.need - (pc - nheavy) - sh.hg;
-                    if (want > 0) {
-                        if (tid == 0) sh.nr = 0;
+                    __syncthreads();
+                }
+            } else {
+                for (int round = 0;; ++round) {
+                    if (round > a.M + 1) {  // each round settles >= 1 candidate
+                        if (tid == 0) { flag_error(a.err, DERR_INTERNAL); sh.stop = 1; }
                         __syncthreads();
-                        for (int t = tid; t < nheavy; t += CL_THREADS) {
-                            const int b = a.hlist[t];
-                            if (a.cstamp[b] != pass) {
-                                const int64_t c = a.iptr[(int64_t)b * NCLS + shi + 1] -
-                                                  a.iptr[(int64_t)b * NCLS + slo];
-                                const uint64_t cost = c > 0xffffffffll ? 0xffffffffull : (uint64_t)c;
-                                a.racc[atomicAdd(&sh.nr, 1)] = (cost << 32) | (uint32_t)b;
+                        break;
+                    }
+                    if (sh.grown) {
+                        const int64_t m = sh.m, ub = sh.ub;
+                        const int limit = sh.limit;
+                        const int pc = sh.pcount;
+                        const int slo = slot_of(m), shi = slot_of(ub < NCLS ? ub : NCLS);
+                        // (1) Columns of p with a short ("light") list: one warp walks the size
+                        // window [m, ub] of the list and every eligible row on it gets one hit, so
+                        // |q n p| over light columns is a counter for every row the window admits
+                        // (a row's size class is the same in all of its columns). Each column keeps
+                        // the first class it has not walked; when p grows the window only widens
+                        // upwards, so old columns walk just the newly admitted classes and no
+                        // (column, row) pair is counted twice. Heavy lists are set aside.
+                        // A column is heavy when its window slice is long at the time it joins p
+                        // (hub columns against small patterns); against a large pattern the window
+                        // sits in high size classes and even hub columns are light.
+                        const int t_first = shi != sh.wshi ? 0 : sh.nproc;
+                        const int nproc0 = sh.nproc;
+                        // Column t of p: its slice of the window still to walk ([e_beg, e_beg +
+                        // e_cnt)), or none if it is heavy. A column that joined p since the last walk
+                        // (t >= nproc0) has not been walked in this pass: its slice starts at slo.
+                        struct Col {
+                            int b, kind;  // kind: 0 light, 1 heavy (new), 2 heavy (known)
+                            int64_t e_beg, e_cnt;
+                        };
+                        auto column = [&](int t) {
+                            Col c{a.plist[t], 0, 0, 0};
+                            const int64_t* ib = a.iptr + (int64_t)c.b * NCLS;
+                            int from = slo;
+                            if (t >= nproc0) {
+                                if (ib[shi + 1] - ib[slo] > HEAVY) {
+                                    c.kind = 1;
+                                    return c;
+                                }
+                            } else {
+                                if (a.hstamp[c.b] == pass) {
+                                    c.kind = 2;
+                                    return c;
+                                }
+                                if (a.cstamp[c.b] == pass) from = max(a.cslot[c.b], slo);
                             }
-                        }
-                        __syncthreads();
-                        const int nu = sh.nr;
-                        int take = nu;
-                        if (want < nu && nu <= SORT_CAP) {
-                            for (int t = tid; t < nu; t += CL_THREADS) sh.sortbuf[t] = a.racc[t];
-                            __syncthreads();
-                            cta_bitonic_sort(sh.sortbuf, nu, pow2_at_least(nu), false);
-                            for (int t = tid; t < want; t += CL_THREADS) a.racc[t] = sh.sortbuf[t];
-                            __syncthreads();
-                            take = want;
-                        }
-                        for (int t = tid; t < take; t += CL_THREADS) {
-                            const int b = (int)(uint32_t)a.racc[t];
-                            a.cstamp[b] = pass;
-                            a.cslot[b] = slo;
-                            a.glist[sh.hg + t] = b;
-                        }
-                        __syncthreads();
-                        if (tid == 0) sh.hg += take;
-                        __syncthreads();
-                    }
-                    const int hg = sh.hg;
-                    for (int c0 = 0; c0 < hg; c0 += CL_THREADS) {
-                        const int ci = c0 + tid;
-                        int64_t e_beg = 0, e_cnt = 0;
-                        if (ci < hg) {
-                            const int b = a.glist[ci];
-                            const int from = max(a.cslot[b], slo);
                             if (from <= shi) {
-                                e_beg = a.iptr[(int64_t)b * NCLS + from];
-                                e_cnt = a.iptr[(int64_t)b * NCLS + shi + 1] - e_beg;
+                                c.e_beg = ib[from];
+                                c.e_cnt = ib[shi + 1] - c.e_beg;
                             }
-                            if (a.cslot[b] < shi + 1) a.cslot[b] = shi + 1;
-                        }
-                        flat_walk(sh, a.ient, e_beg, e_cnt, [&](int2 en) {
-                            if ((int64_t)en.y < m) return;
+                            return c;
+                        };
+                        auto record = [&](const Col& c) {
+                            if (c.kind == 1) {
+                                a.hstamp[c.b] = pass;
+                                a.hlist[atomicAdd(&sh.nheavy, 1)] = c.b;
+                            } else if (c.kind == 0) {
+                                a.cstamp[c.b] = pass;
+                                a.cslot[c.b] = shi + 1;
+                            }
+                        };
+                        auto hit = [&](int2 en) {
                             const int pr = st.p(en.x);
                             if (pr < 0 || pr >= limit) return;
-                            if (st.cnt_heavy(en.x) == 0)
-                                append_candidate(sh, a, en.x, en.y, pr);
-                        });
+                            if (st.cnt_add(en.x) == 0) append_candidate(sh, a, en.x, en.y, pr);
+                        };
+                        if (pc - t_first <= 2 * (CL_THREADS / 32)) {
+                            // few columns: one warp per column, no CTA-wide scan
+                            for (int t = t_first + warp; t < pc; t += CL_THREADS / 32) {
+                                const Col c = column(t);
+                                __syncwarp();
+                                if (lane == 0) record(c);
+                                warp_walk(a.ient, c.e_beg, c.e_beg + c.e_cnt, lane, hit);
+                            }
+                        } else {
+                            // many columns (large patterns): CL_THREADS at a time, one per thread,
+                            // their slices walked as one flattened range by the whole CTA
+                            for (int c0 = t_first; c0 < pc; c0 += CL_THREADS) {
+                                const int t = c0 + tid;
+                                int64_t e_beg = 0, e_cnt = 0;
+                                if (t < pc) {
+                                    const Col c = column(t);
+                                    record(c);
+                                    e_beg = c.e_beg;
+                                    e_cnt = c.e_cnt;
+                                }
+                                flat_walk(sh, a.ient, e_beg, e_cnt, hit);
+                            }
+                        }
+                        __syncthreads();
+                        if (tid == 0) {
+                            sh.nproc = pc;
+                            sh.wshi = shi;
+                        }
+                        // (2) Heavy columns are needed only when the light ones are fewer than
+                        // |p| - m + 1; then take the cheapest ones over the size window [m, ub].
+                        const int nheavy = sh.nheavy;
+                        const int want = sh.need - (pc - nheavy) - sh.hg;
+                        if (want > 0) {
+                            if (tid == 0) sh.nr = 0;
+                            __syncthreads();
+                            for (int t = tid; t < nheavy; t += CL_THREADS) {
+                                const int b = a.hlist[t];
+                                if (a.cstamp[b] != pass) {
+                                    const int64_t c = a.iptr[(int64_t)b * NCLS + shi + 1] -
+                                                      a.iptr[(int64_t)b * NCLS + slo];
+                                    const uint64_t cost = c > 0xffffffffll ? 0xffffffffull : (uint64_t)c;
+                                    a.racc[atomicAdd(&sh.nr, 1)] = (cost << 32) | (uint32_t)b;
+                                }
+                            }
+                            __syncthreads();
+                            const int nu = sh.nr;
+                            int take = nu;
+                            if (want < nu && nu <= SORT_CAP) {
+                                for (int t = tid; t < nu; t += CL_THREADS) sh.sortbuf[t] = a.racc[t];
+                                __syncthreads();
+                                cta_bitonic_sort(sh.sortbuf, nu, pow2_at_least(nu), false);
+                                for (int t = tid; t < want; t += CL_THREADS) a.racc[t] = sh.sortbuf[t];
+                                __syncthreads();
+                                take = want;
+                            }
+                            for (int t = tid; t < take; t += CL_THREADS) {
+                                const int b = (int)(uint32_t)a.racc[t];
+                                a.cstamp[b] = pass;
+                                a.cslot[b] = slo;
+                                a.glist[sh.hg + t] = b;
+                            }
+                            __syncthreads();
+                            if (tid == 0) sh.hg += take;
+                            __syncthreads();
+                        }
+                        const int hg = sh.hg;
+                        for (int c0 = 0; c0 < hg; c0 += CL_THREADS) {
+                            const int ci = c0 + tid;
+                            int64_t e_beg = 0, e_cnt = 0;
+                            if (ci < hg) {
+                                const int b = a.glist[ci];
+                                const int from = max(a.cslot[b], slo);
+                                if (from <= shi) {
+                                    e_beg = a.iptr[(int64_t)b * NCLS + from];
+                                    e_cnt = a.iptr[(int64_t)b * NCLS + shi + 1] - e_beg;
+                                }
+                                if (a.cslot[b] < shi + 1) a.cslot[b] = shi + 1;
+                            }
+                            flat_walk(sh, a.ient, e_beg, e_cnt, [&](int2 en) {
+                                if ((int64_t)en.y < m) return;
+                                const int pr = st.p(en.x);
+                                if (pr < 0 || pr >= limit) return;
+                                if (st.cnt_heavy(en.x) == 0)
+                                    append_candidate(sh, a, en.x, en.y, pr);
+                            });
+                        }
+                        if (tid == 0) {
+                            sh.grown = 0;
+                            sh.smax = -1;
+                            sh.nr = 0;
+                            sh.nkeep = 0;
+                        }
+                        __syncthreads();
                     }
+                    const int ncand = sh.ncand;
+                    if (ncand == 0) break;
+                    const int buf = sh.cur;
+
+                    // Evaluate every pending candidate against the current p.
+                    const int pcount = sh.pcount;
+                    const int nheavy = sh.nheavy;
+                    for (int c = tid; c < ncand; c += CL_THREADS) {
+                        int r, len, pr;
+                        cand_get(sh, a, buf, c, r, len, pr);
+                        int64_t inter = st.cnt_light(r);
+                        // Light hits are exact; each heavy column adds at most one. The distance is
+                        // non-increasing in the intersection (fixed |p| + |q|), so a candidate that
+                        // fails even with every heavy column counted is rejected without reading its
+                        // pattern.
+                        bool hopeless = false;
+                        if (nheavy > 0) {
+                            const int64_t imax = min(inter + (int64_t)nheavy, (int64_t)len);
+                            hopeless = jaccard_distance(imax, pcount + (int64_t)len - imax) > a.tau;
+                        }
+                        if (nheavy > 0 && !hopeless) {
+                            const int64_t q0 = a.qptr[r], q1 = a.qptr[r + 1];
+                            if ((int64_t)nheavy * 4 >= len) {  // scan q against all of p
+                                inter = 0;
+                                for (int64_t j = q0; j < q1; ++j) {
+                                    const int b = a.qcol[j];
+                                    inter += (a.pbits[b >> 5] >> (b & 31)) & 1u;
+                                }
+                            } else {  // light hits are counted; look the heavy columns up in q
+                                for (int h = 0; h < nheavy; ++h)
+                                    inter += pattern_has(a.qcol, q0, q1, a.hlist[h]) ? 1 : 0;
+                            }
+                        }
+                        const int64_t uni = pcount + (int64_t)len - inter;
+                        const bool acc = !hopeless && jaccard_distance(inter, uni) <= a.tau;
+                        const bool grow = acc && len > inter;
+                        flag_set(sh, a, c, acc ? (grow ? 2 : 1) : 0);
+                        if (grow) atomicMax(&sh.smax, pr);
+                    }
+                    __syncthreads();
+                    const int smax = sh.smax;
+
+                    // Settle every candidate at or above smax (its counter is cleared: it can never
+                    // be gathered again in this pass); keep the rest, in any order, in the other
+                    // buffer. Settled acceptances are collected with their positions.
+                    for (int c = tid; c < ncand; c += CL_THREADS) {
+                        int r, len, pr;
+                        cand_get(sh, a, buf, c, r, len, pr);
+                        if (pr < smax) {
+                            cand_set(sh, a, buf ^ 1, atomicAdd(&sh.nkeep, 1), r, len, pr);
+                        } else {
+                            st.cnt_clear(r);
+                            if (flag_get(sh, a, c)) {
+                                const int slot = atomicAdd(&sh.nr, 1);
+                                const uint64_t kv = ((uint64_t)(uint32_t)pr << 32) | (uint32_t)r;
+                                if (slot < SORT_CAP) sh.sortbuf[slot] = kv; else a.racc[slot] = kv;
+                            }
+                        }
+                    }
+                    __syncthreads();
+                    const int nr = sh.nr;
+                    // Append the settled acceptances in decreasing position order.
+                    if (nr <= CL_THREADS) {  // rank by counting
+                        if (tid < nr) {
+                            const uint64_t kv = sh.sortbuf[tid];
+                            int rank = 0;
+                            for (int j = 0; j < nr; ++j) rank += sh.sortbuf[j] > kv;
+                            const int r = (int)(uint32_t)kv, pr = (int)(kv >> 32);
+                            if (sh.out + rank < a.M && sh.k + rank < a.M) {
+                                a.perm[sh.out + rank] = r;
+                                hole_set(sh, a, sh.k + rank, pr);
+                                st.set_p(r, -1);
+                            } else {
+                                flag_error(a.err, DERR_INTERNAL);
+                            }
+                        }
+                    } else {
+                        uint64_t* keys = a.gsort;
+                        for (int t = tid; t < nr; t += CL_THREADS)
+                            keys[t] = t < SORT_CAP ? sh.sortbuf[t] : a.racc[t];
+                        __syncthreads();
+                        cta_bitonic_sort(keys, nr, pow2_at_least(nr), true);
+                        for (int t = tid; t < nr; t += CL_THREADS) {
+                            const uint64_t kv = keys[t];
+                            const int r = (int)(uint32_t)kv, pr = (int)(kv >> 32);
+                            if (sh.out + t < a.M && sh.k + t < a.M) {
+                                a.perm[sh.out + t] = r;
+                                hole_set(sh, a, sh.k + t, pr);
+                                st.set_p(r, -1);
+                            } else {
+                                flag_error(a.err, DERR_INTERNAL);
+                            }
+                        }
+                    }
+                    __syncthreads();
                     if (tid == 0) {
-                        sh.grown = 0;
+                        sh.out += nr;
+                        sh.k += nr;
+                        sh.ncand = sh.nkeep;
+                        sh.cur = buf ^ 1;
                         sh.smax = -1;
                         sh.nr = 0;
                         sh.nkeep = 0;
                     }
+                    if (smax < 0) {  // nothing grew p: every candidate is settled
+                        __syncthreads();
+                        break;
+                    }
+                    // The candidate at smax was accepted and adds columns: grow p.
+                    const int grow_row = st.u(smax);
+                    const int64_t g0 = a.qptr[grow_row], g1 = a.qptr[grow_row + 1];
+                    for (int64_t j = g0 + tid; j < g1; j += CL_THREADS) {
+                        const int b = a.qcol[j];
+                        const uint32_t bit = 1u << (b & 31);
+                        if (!(atomicOr(&a.pbits[b >> 5], bit) & bit)) a.plist[atomicAdd(&sh.pcount, 1)] = b;
+                    }
+                    __syncthreads();
+                    if (tid == 0) {
+                        sh.limit = smax;
+                        sh.grown = 1;
+                        sh.m = min_inter(a.t_lo, sh.pcount);
+                        sh.ub = max_len(a.t_lo, sh.pcount);
+                        sh.need = (int)(sh.pcount - sh.m + 1);
+                    }
                     __syncthreads();
                 }
-                const int ncand = sh.ncand;
-                if (ncand == 0) break;
-                const int buf = sh.cur;
-
-                // Evaluate every pending candidate against the current p.
-                const int pcount = sh.pcount;
-                const int nheavy = sh.nheavy;
-                for (int c = tid; c < ncand; c += CL_THREADS) {
-                    int r, len, pr;
-                    cand_get(sh, a, buf, c, r, len, pr);
-                    int64_t inter = st.cnt_light(r);
-                    // Light hits are exact; each heavy column adds at most one. The distance is
-                    // non-increasing in the intersection (fixed |p| + |q|), so a candidate that
-                    // fails even with every heavy column counted is rejected without reading its
-                    // pattern.
-                    bool hopeless = false;
-                    if (nheavy > 0) {
-                        const int64_t imax = min(inter + (int64_t)nheavy, (int64_t)len);
-                        hopeless = jaccard_distance(imax, pcount + (int64_t)len - imax) > a.tau;
-                    }
-                    if (nheavy > 0 && !hopeless) {
-                        const int64_t q0 = a.qptr[r], q1 = a.qptr[r + 1];
-                        if ((int64_t)nheavy * 4 >= len) {  // scan q against all of p
-                            inter = 0;
-                            for (int64_t j = q0; j < q1; ++j) {
-                                const int b = a.qcol[j];
-                                inter += (a.pbits[b >> 5] >> (b & 31)) & 1u;
-                            }
-                        } else {  // light hits are counted; look the heavy columns up in q
-                            for (int h = 0; h < nheavy; ++h)
-                                inter += pattern_has(a.qcol, q0, q1, a.hlist[h]) ? 1 : 0;
-                        }
-                    }
-                    const int64_t uni = pcount + (int64_t)len - inter;
-                    const bool acc = !hopeless && jaccard_distance(inter, uni) <= a.tau;
-                    const bool grow = acc && len > inter;
-                    flag_set(sh, a, c, acc ? (grow ? 2 : 1) : 0);
-                    if (grow) atomicMax(&sh.smax, pr);
-                }
-                __syncthreads();
-                const int smax = sh.smax;
-
-                // Settle every candidate at or above smax (its counter is cleared: it can never
-                // be gathered again in this pass); keep the rest, in any order, in the other
-                // buffer. Settled acceptances are collected with their positions.
-                for (int c = tid; c < ncand; c += CL_THREADS) {
-                    int r, len, pr;
-                    cand_get(sh, a, buf, c, r, len, pr);
-                    if (pr < smax) {
-                        cand_set(sh, a, buf ^ 1, atomicAdd(&sh.nkeep, 1), r, len, pr);
-                    } else {
-                        st.cnt_clear(r);
-                        if (flag_get(sh, a, c)) {
-                            const int slot = atomicAdd(&sh.nr, 1);
-                            const uint64_t kv = ((uint64_t)(uint32_t)pr << 32) | (uint32_t)r;
-                            if (slot < SORT_CAP) sh.sortbuf[slot] = kv; else a.racc[slot] = kv;
-                        }
-                    }
-                }
-                __syncthreads();
-                const int nr = sh.nr;
-                // Append the settled acceptances in decreasing position order.
-                if (nr <= CL_THREADS) {  // rank by counting
-                    if (tid < nr) {
-                        const uint64_t kv = sh.sortbuf[tid];
-                        int rank = 0;
-                        for (int j = 0; j < nr; ++j) rank += sh.sortbuf[j] > kv;
-                        const int r = (int)(uint32_t)kv, pr = (int)(kv >> 32);
-                        if (sh.out + rank < a.M && sh.k + rank < a.M) {
-                            a.perm[sh.out + rank] = r;
-                            hole_set(sh, a, sh.k + rank, pr);
-                            st.set_p(r, -1);
-                        } else {
-                            flag_error(a.err, DERR_INTERNAL);
-                        }
-                    }
-                } else {
-                    uint64_t* keys = a.gsort;
-                    for (int t = tid; t < nr; t += CL_THREADS)
-                        keys[t] = t < SORT_CAP ? sh.sortbuf[t] : a.racc[t];
-                    __syncthreads();
-                    cta_bitonic_sort(keys, nr, pow2_at_least(nr), true);
-                    for (int t = tid; t < nr; t += CL_THREADS) {
-                        const uint64_t kv = keys[t];
-                        const int r = (int)(uint32_t)kv, pr = (int)(kv >> 32);
-                        if (sh.out + t < a.M && sh.k + t < a.M) {
-                            a.perm[sh.out + t] = r;
-                            hole_set(sh, a, sh.k + t, pr);
-                            st.set_p(r, -1);
-                        } else {
-                            flag_error(a.err, DERR_INTERNAL);
-                        }
-                    }
-                }
-                __syncthreads();
-                if (tid == 0) {
-                    sh.out += nr;
-                    sh.k += nr;
-                    sh.ncand = sh.nkeep;
-                    sh.cur = buf ^ 1;
-                    sh.smax = -1;
-                    sh.nr = 0;
-                    sh.nkeep = 0;
-                }
-                if (smax < 0) {  // nothing grew p: every candidate is settled
-                    __syncthreads();
-                    break;
-                }
-                // The candidate at smax was accepted and adds columns: grow p.
-                const int grow_row = st.u(smax);
-                const int64_t g0 = a.qptr[grow_row], g1 = a.qptr[grow_row + 1];
-                for (int64_t j = g0 + tid; j < g1; j += CL_THREADS) {
-                    const int b = a.qcol[j];
-                    const uint32_t bit = 1u << (b & 31);
-                    if (!(atomicOr(&a.pbits[b >> 5], bit) & bit)) a.plist[atomicAdd(&sh.pcount, 1)] = b;
-                }
-                __syncthreads();
-                if (tid == 0) {
-                    sh.limit = smax;
-                    sh.grown = 1;
-                    sh.m = min_inter(a.t_lo, sh.pcount);
-                    sh.ub = max_len(a.t_lo, sh.pcount);
-                    sh.need = (int)(sh.pcount - sh.m + 1);
-                }
-                __syncthreads();
+                for (int t = tid; t < sh.pcount; t += CL_THREADS) a.pbits[a.plist[t] >> 5] = 0u;
             }
-            for (int t = tid; t < sh.pcount; t += CL_THREADS) a.pbits[a.plist[t] >> 5] = 0u;
         }
 
         // Replay the pass's removals (U[h] = U.back(); pop, h decreasing): for a hole h_t below
@@ -812,13 +870,14 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
             st.set_u(h, r);
             st.set_p(r, h);
         }
-        __syncthreads();
+        // No barrier before this: the replay reads none of these fields.
         if (tid == 0) {
             sh.n = n - k;
             sh.pass += 1;
             sh.ncand = 0;
             sh.nheavy = 0;
             sh.cur = 0;  // the next first walk appends to candidate buffer 0
+            sh.nr = 0;
             if (sh.out > a.M) { flag_error(a.err, DERR_INTERNAL); sh.stop = 1; }
         }
         __syncthreads();
