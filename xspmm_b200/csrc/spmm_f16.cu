@@ -65,7 +65,7 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 }
 
 template <typename IT, int WARPS, bool ALIGNED>
-__global__ void __launch_bounds__(WARPS * 32)
+__global__ void __launch_bounds__(WARPS * 32, 24 / WARPS)
 bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_ind,
                          const __half* __restrict__ vals, const __half* __restrict__ B,
                          float* __restrict__ C, const IT* __restrict__ row_map, int64_t M,
