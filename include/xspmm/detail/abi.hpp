@@ -25,6 +25,8 @@ struct Abi;
         static constexpr auto count = xspmm_csr_to_bcsr_count_##IS;                                \
         static constexpr auto fill = xspmm_csr_to_bcsr_fill_##VS##_##IS;                           \
         static constexpr auto unpermute = xspmm_unpermute_dense_##VS##_##IS;                       \
+        static constexpr auto plan_csr = xspmm_plan_csr_##VS##f32_##IS;                            \
+        static constexpr auto plan_bcsr = xspmm_plan_bcsr_##VS##f32_##IS;                          \
     };
 XSPMM_ABI_ROW(__half, int32_t, f16, i32)
 XSPMM_ABI_ROW(__half, int64_t, f16, i64)

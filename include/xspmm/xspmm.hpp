@@ -23,6 +23,7 @@
 #include "matrix/bcsr.hpp"
 #include "matrix/conversion.hpp"
 #include "matrix/csr.hpp"
+#include "plan.hpp"
 
 namespace xspmm {
 

@@ -58,14 +58,24 @@ int main(int argc, char** argv) {
     auto A_bcsr = xspmm::csr_to_bcsr(exec, A_opt, 16, 16);
     xspmm::spmm(A_bcsr, d_B, d_Ctmp, N);
     xspmm::unpermute_dense_matrix(exec, d_Ctmp, d_C2, d_perm, M, N);
+
+    // the same product from a plan (stages done once, then the Tier-1 kernel only)
+    float* d_C3 = nullptr;
+    exec->allocate(reinterpret_cast<void**>(&d_C3), (size_t)M * N * sizeof(float));
+    {
+        xspmm::SpMMPlan<__half, int32_t> plan(exec, A, 16, true);
+        plan.execute(d_B, d_C3, N);
+        if (plan.info().rows != M) return 4;
+    }
     exec->synchronize();
 
     std::vector<int32_t> perm(M);
-    std::vector<float> C1((size_t)M * N), C2((size_t)M * N);
+    std::vector<float> C1((size_t)M * N), C2((size_t)M * N), C3((size_t)M * N);
     exec->copy_to_host(perm.data(), d_perm, perm.size() * sizeof(int32_t));
     exec->copy_to_host(C1.data(), d_C1, C1.size() * sizeof(float));
     exec->copy_to_host(C2.data(), d_C2, C2.size() * sizeof(float));
-    for (void* p : {(void*)d_B, (void*)d_C1, (void*)d_C2, (void*)d_Ctmp, (void*)d_perm})
+    exec->copy_to_host(C3.data(), d_C3, C3.size() * sizeof(float));
+    for (void* p : {(void*)d_B, (void*)d_C1, (void*)d_C2, (void*)d_Ctmp, (void*)d_perm, (void*)d_C3})
         exec->free(p);
 
     bool threw = false;  // the reference's error behaviour: bad dimensions -> invalid_argument
@@ -84,6 +94,7 @@ int main(int argc, char** argv) {
     std::fwrite(C1.data(), sizeof(float), C1.size(), o);
     std::fwrite(C2.data(), sizeof(float), C2.size(), o);
     std::fwrite(tm, sizeof(double), 6, o);
+    std::fwrite(C3.data(), sizeof(float), C3.size(), o);
     std::fclose(o);
     std::printf("ok M=%d N=%d nnz=%d total_ms=%.3f\n", M, N, nnz, t.total_pipeline_ms);
     return 0;

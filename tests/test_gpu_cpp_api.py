@@ -56,3 +56,5 @@ def test_cpp_api_pipeline(tmp_path):
     assert errors(ref, C1, 1e-3)["max_rel_guarded"] <= 1e-3
     assert np.array_equal(C1.view(np.uint32), C2.view(np.uint32))
     assert tm[5] > 0 and tm[0] > 0
+    C3 = np.frombuffer(raw, dtype=np.float32, count=M * N, offset=off + 8 * M * N + 48).reshape(M, N)
+    assert np.array_equal(C1.view(np.uint32), C3.view(np.uint32))  # SpMMPlan: same product
