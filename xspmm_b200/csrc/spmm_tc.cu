@@ -64,7 +64,7 @@ static_assert(TC_STAGES % TC_PRODUCERS == 0, "each producer owns fixed stage slo
 constexpr int TMEM_COLS = 256;
 constexpr long long WAIT_LIMIT = 1ll << 22;        // polls of an mbarrier before giving up
 constexpr size_t TC_SMEM = (size_t)TC_STAGES * STAGE_BYTES + 1024 + 256;
-static_assert(2 * TC_STAGES * 8 + 8 + 4 <= 256, "barrier area");
+static_assert(2 * TC_STAGES * 8 + 3 * 8 <= 256, "barrier area");
 
 // ---- PTX wrappers ---------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -186,51 +186,6 @@ constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 16) | ((uint32_t)(TC_BN >> 3) <
                               ((uint32_t)(128 >> 4) << 24);
 
 // ---- the kernel -----------------------------------------------------------------------------------
-// Split-K reduction of one CTA's rows: C[map(g*128 + r0 + rr), n0 + 4*ce ..] = sum over the
-// S partials (rank order) of element (r0 + rr, ce), for the `total` = nr x nce items. Items are
-// taken B at a time per thread, with all their S loads issued before any is used.
-template <int SMAX, int B, typename IT>
-__device__ __forceinline__ void tc_reduce_rows(const float4* __restrict__ tile_ws,
-                                               float* __restrict__ C, const IT* __restrict__ row_map,
-                                               int g, int n0, int r0, int nr, int total, int64_t M,
-                                               int64_t N, unsigned* err, int S = SMAX) {
-#pragma unroll 1
-    for (int it0 = threadIdx.x; it0 < total; it0 += B * TC_THREADS) {
-        float4 acc[B];
-#pragma unroll
-        for (int u = 0; u < B; ++u) {
-            const int it = it0 + u * TC_THREADS;
-            acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (it >= total) continue;
-            const int rr = it % nr, ce = it / nr;
-            float4 v[SMAX];
-#pragma unroll
-            for (int k = 0; k < SMAX; ++k)
-                if (k < S) v[k] = __ldcg(tile_ws + (size_t)k * 8192 + ce * 128 + r0 + rr);
-            acc[u] = v[0];
-#pragma unroll
-            for (int k = 1; k < SMAX; ++k)
-                if (k < S) {
-                    acc[u].x += v[k].x; acc[u].y += v[k].y; acc[u].z += v[k].z; acc[u].w += v[k].w;
-                }
-        }
-#pragma unroll
-        for (int u = 0; u < B; ++u) {
-            const int it = it0 + u * TC_THREADS;
-            if (it >= total) continue;
-            const int rr = it % nr, ce = it / nr;
-            const int64_t grow = (int64_t)g * 128 + r0 + rr;
-            if (grow >= M) continue;
-            const int64_t orow = row_map ? (int64_t)row_map[grow] : grow;
-            if (orow < 0 || orow >= M) {
-                flag_error(err, DERR_PERM_OUT_OF_RANGE);
-                continue;
-            }
-            *reinterpret_cast<float4*>(C + orow * N + n0 + ce * 4) = acc[u];
-        }
-    }
-}
-
 template <typename IT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUtensorMap tmB,
@@ -244,6 +199,7 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * STAGE_BYTES);
     uint64_t* empty = full + TC_STAGES;
     uint64_t* accum = empty + TC_STAGES;
+    uint64_t* redbar = accum + 2;  // split-K bulk copies of the partials
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -263,6 +219,7 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
+        mbar_init(redbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
     }
@@ -415,19 +372,25 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
             }
         }
     } else {
-        // Split tile: the `splits` CTAs of the cluster each hold a partial 128 x 256 sum. Each
-        // writes its partial to the workspace straight from TMEM, in the order [32-column chunk]
-        // [float4 e][row][4], so one warp store covers 32 consecutive rows' float4 e: 512
-        // contiguous bytes. After a cluster barrier (which publishes those stores to the
-        // cluster), CTA k adds rows [k*128/S, (k+1)*128/S) over the S partials in rank order (a
-        // fixed order: the result does not depend on timing) and stores them to C through the
-        // row map. The partials stay in L2.
+        // Split tile: the `splits` CTAs of the cluster (S = 2, 4 or 8) each hold a partial
+        // 128 x 256 sum; rows [k*nr, (k+1)*nr) belong to CTA k (nr = 128/S). Each CTA writes its
+        // partial to the workspace straight from TMEM, grouped by owner: owner k's rows form one
+        // block of 64 float4 columns x nr rows, element (lr, ce) at ce*nr + (lr ^ (ce & 15)) --
+        // a warp store (32 consecutive rows, one float4 column) stays within 512 bytes, and the
+        // owner's copy in shared memory reads conflict-free along ce. After a cluster barrier
+        // (which publishes the stores) each owner pulls its S blocks with bulk copies, in two
+        // halves of 32 float4 columns, adds them in rank order (a fixed order: the result does
+        // not depend on timing) and stores its rows of C, one warp per 512-byte row segment,
+        // through the row map. The partials stay in L2.
         const int S = splits;
+        const int nr = 128 / S;
         const int tile = blockIdx.x / S;
-        float4* mine = ws + ((size_t)tile * S + split) * 8192;
+        float4* tile_ws = ws + (size_t)tile * S * 8192;
         if (warp >= 1) {
             const int q = warp & 3;
             const int row = q * 32 + lane;
+            const int own = row / nr, lr = row - own * nr;
+            float4* blk = tile_ws + (size_t)split * 8192 + (size_t)own * 64 * nr;
 #pragma unroll 1
             for (int ch = 0; ch < TC_BN / 32 && n0 + ch * 32 < N; ++ch) {
                 uint32_t v[32];
@@ -438,22 +401,54 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
                     for (int e = 0; e < 32; ++e) v[e] = 0u;
                 }
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    mine[(ch * 8 + e) * 128 + row] =
+                for (int e = 0; e < 8; ++e) {
+                    const int ce = ch * 8 + e;
+                    blk[ce * nr + (lr ^ (ce & 15))] =
                         make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
                                     __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                }
             }
         }
+        // the stores above are read by other CTAs' bulk copies (async proxy)
+        asm volatile("fence.proxy.async.global;" ::: "memory");
         cluster_sync_all();
-        {
-            // all 5 warps; up to 16 loads of 16 B in flight per thread (an L2 round trip each)
-            const int r0 = split * 128 / S, r1 = (split + 1) * 128 / S, nr = r1 - r0;
-            const int nce = (int)min((int64_t)(TC_BN / 4), (N - n0 + 3) / 4);  // float4 columns
-            const int total = nr * nce;
-            const float4* tile_ws = ws + (size_t)tile * S * 8192;
-            if (S == 2) tc_reduce_rows<2, 8>(tile_ws, C, row_map, g, n0, r0, nr, total, M, N, err);
-            else if (S <= 4) tc_reduce_rows<4, 4>(tile_ws, C, row_map, g, n0, r0, nr, total, M, N, err, S);
-            else tc_reduce_rows<8, 2>(tile_ws, C, row_map, g, n0, r0, nr, total, M, N, err, S);
+        const int r0 = split * nr;
+        const int nce = (int)min((int64_t)(TC_BN / 4), (N - n0 + 3) / 4);  // float4 columns of C
+        float4* buf = reinterpret_cast<float4*>(smem);                    // [S][32][nr], 64 KB
+        const uint32_t half_bytes = 32u * (uint32_t)nr * 16u;
+#pragma unroll 1
+        for (int hf = 0; hf < 2 && hf * 32 < nce; ++hf) {
+            if (hf > 0) __syncthreads();  // every read of the previous half is done
+            if (threadIdx.x == 32) {
+                // the generic reads of this buffer come before the copy's writes
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_expect_tx(redbar, (uint32_t)S * half_bytes);
+                for (int pp = 0; pp < S; ++pp)
+                    bulk_load(buf + (size_t)pp * 32 * nr,
+                              tile_ws + (size_t)pp * 8192 + (size_t)split * 64 * nr +
+                                  (size_t)hf * 32 * nr,
+                              half_bytes, redbar);
+            }
+            const bool ok = mbar_wait(redbar, (uint32_t)hf & 1u, err);
+#pragma unroll 1
+            for (int it = threadIdx.x; it < 32 * nr; it += TC_THREADS) {
+                const int lr = it >> 5, cl = it & 31;  // a warp: one row, 32 float4 columns
+                const int ce = hf * 32 + cl;
+                const int64_t grow = (int64_t)g * 128 + r0 + lr;
+                if (!ok || ce >= nce || grow >= M) continue;
+                const int off = cl * nr + (lr ^ (ce & 15));
+                float4 acc = buf[off];
+                for (int pp = 1; pp < S; ++pp) {
+                    const float4 v = buf[(size_t)pp * 32 * nr + off];
+                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                }
+                const int64_t orow = row_map ? (int64_t)row_map[grow] : grow;
+                if (orow < 0 || orow >= M) {
+                    flag_error(err, DERR_PERM_OUT_OF_RANGE);
+                    continue;
+                }
+                *reinterpret_cast<float4*>(C + orow * N + n0 + (int64_t)ce * 4) = acc;
+            }
         }
     }
     tc_fence_before();
@@ -764,10 +759,10 @@ void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M
     // Split-K factor: the CTAs of a tile form one cluster, and clusters are placed whole inside
     // a GPC, so the number resident at once depends on the cluster size. Pick the split that
     // minimises (waves) x (union entries per CTA + a fixed cost of ~30 entries for the prologue
-    // and the epilogue), at most 8 and never slices shorter than 32 union entries.
+    // and the epilogue): 1, 2, 4 or 8, never slices shorter than 32 union entries.
     int splits = 1;
     double best = 0.0;
-    for (int sp = 1; sp <= 8; ++sp) {
+    for (int sp = 1; sp <= 8; sp *= 2) {  // a power of two: owners get 128/sp rows
         if (sp > 1 && avg_union / sp < 32) break;
         const int64_t resident = tc_resident_ctas(h.device, sp);
         if (resident <= 0) continue;
