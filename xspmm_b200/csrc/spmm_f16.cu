@@ -65,7 +65,7 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 }
 
 template <typename IT, int WARPS, bool ALIGNED>
-__global__ void __launch_bounds__(WARPS * 32, 24 / WARPS)
+__global__ void __launch_bounds__(WARPS * 32, WARPS == 1 ? 24 : 1)
 bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_ind,
                          const __half* __restrict__ vals, const __half* __restrict__ B,
                          float* __restrict__ C, const IT* __restrict__ row_map, int64_t M,
@@ -327,9 +327,10 @@ void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const
                        const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map,
                        const MmaWork* work) {
     if (nbr == 0 || N == 0 || M == 0) return;
-    const int64_t nwork = work ? work->nitems : nbr;
-    const MmaItem* items = work ? work->items.get() : nullptr;
-    DevBuf<float> wsb(work && work->nslots > 0 ? (size_t)(work->nslots * 16 * N) : 0, h.stream);
+    const bool listed = work && work->nitems > 0;
+    const int64_t nwork = listed ? work->nitems : nbr;
+    const MmaItem* items = listed ? work->items.get() : nullptr;
+    DevBuf<float> wsb(listed && work->nslots > 0 ? (size_t)(work->nslots * 16 * N) : 0, h.stream);
     float* ws = wsb.get();
     XS_REQUIRE(ceil_div(N, 64) <= 65535, XSPMM_STATUS_UNSUPPORTED, "N above 4,194,240 columns");
     const bool aligned = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
@@ -345,7 +346,7 @@ void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const
         else if (warps == 2) launch<IT, 2, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
         else launch<IT, 4, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
     }
-    if (work && work->nlong > 0) {
+    if (listed && work->nlong > 0) {
         const int64_t total = work->nlong * 16 * N;
         const unsigned grid = (unsigned)std::max<int64_t>(
             1, std::min(ceil_div(total, 256), (int64_t)sm_count(h.device) * 16));
@@ -438,6 +439,10 @@ void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT*
             items.push_back(MmaItem{j0 + o, r, (int32_t)std::min(chunk, len - o), slot++, 0});
     }
     first_slot.push_back(slot);
+    if (long_rows.empty() && !by_first_col) {  // the natural order, nothing to cut: no list
+        out.nitems = 0;
+        return;
+    }
     XS_REQUIRE(items.size() < (size_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "too many work items");
     out.nitems = (int64_t)items.size();
     out.nlong = (int64_t)long_rows.size();
