@@ -600,6 +600,11 @@ def run_sharded(args):
             shard = BlockRowShard(Ab, int(bounds[rank]), int(bounds[rank + 1]))
             B = B_full.clone() if rank == 0 else torch.zeros(P.B.shape, dtype=torch.float16,
                                                               device=dev)
+            if g > 1:  # the group's communicator is set up by its first collective: not timed
+                warm = torch.zeros(1, device=dev)
+                dist.all_reduce(warm, group=group)
+                dist.barrier(group=group)
+                torch.cuda.synchronize()
             b0, b1 = ev(), ev()
             b0.record(stream)
             if g > 1:
