@@ -35,10 +35,18 @@
 // counter read -- no dependent load of the candidate's pattern. Long lists ("heavy", the hub
 // columns of power-law matrices) are walked only when the light columns of p are fewer than
 // |p| - m + 1, and then only over the size window of (2); a candidate's hits in heavy columns are
-// looked up in its pattern. The greedy loop is inherently sequential across clusters and runs in
-// one persistent CTA of 256 threads; all per-pass work (gather, evaluate, compaction, sorting,
-// replay) is parallel inside it. Every loop is bounded by the data sizes; an internal consistency
-// failure sets an error flag and stops instead of spinning.
+// looked up in its pattern (after a bound check that rejects most candidates without it).
+//
+// The greedy loop is inherently sequential across clusters and runs in one persistent CTA of 256
+// threads; all per-pass work (gather, evaluate, compaction, sorting, replay) is parallel inside
+// it, and a pass is a chain of latency, so the code keeps that chain short: every thread reads the
+// seed itself, the first walk starts from the seed's pattern entries and their window slices
+// (precomputed per pattern entry) with no barrier before it, hit counters are 16-bit shared-memory
+// atomics when the row state fits in shared memory, and a pass with at most 256 candidates, no
+// heavy column and no accepted row that grows p -- the common case -- is decided in one
+// evaluation, ranked by counting and replayed in place (a handful of barriers); every other pass
+// takes the general round loop of (3). Every loop is bounded by the data sizes; an internal
+// consistency failure sets an error flag and stops instead of spinning.
 
 #include "ops.cuh"
 
@@ -390,6 +398,8 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
             break;
         }
         const int n = n_old - 1;
+        // read by the fast path until the previous pass's last barrier; first used after B2
+        if (tid == 0) sh.nr = 0;
         const int64_t s0 = a.qptr[seed];
         const int64_t slen = a.qptr[seed + 1] - s0;
         if (slen > 0) {
@@ -407,16 +417,9 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                 e_beg = sl.x;
                 e_cnt = sl.y - sl.x;
                 const bool heavy = e_cnt > HEAVY;
-                if (writer) {
-                    atomicOr(&a.pbits[b >> 5], 1u << (b & 31));
-                    a.plist[t] = b;
-                    if (heavy) {
-                        a.hstamp[b] = pass;
-                        a.hlist[atomicAdd(&sh.nheavy, 1)] = b;
-                    } else {
-                        a.cstamp[b] = pass;
-                        a.cslot[b] = shi0 + 1;
-                    }
+                if (writer && heavy) {  // p's bitmap and column list wait for the general path
+                    a.hstamp[b] = pass;
+                    a.hlist[atomicAdd(&sh.nheavy, 1)] = b;
                 }
                 if (heavy) e_cnt = 0;
             };
@@ -461,10 +464,6 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     if (acc) sh.sortbuf[atomicAdd(&sh.nr, 1)] = ((uint64_t)(uint32_t)pr << 32) |
                                                                  (uint32_t)r;
                 }
-                for (int64_t t = tid; t < slen; t += CL_THREADS) {
-                    const int b = a.qcol[s0 + t];
-                    a.pbits[b >> 5] = 0u;
-                }
                 __syncthreads();
                 const int nr = sh.nr;  // <= ncand0 <= CL_THREADS
                 if (tid < nr) {        // decreasing position order, ranked by counting
@@ -474,10 +473,34 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     const int rr = (int)(uint32_t)kv, pp = (int)(kv >> 32);
                     if (out0 + 1 + rank < a.M) {
                         a.perm[out0 + 1 + rank] = rr;
-                        hole_set(sh, a, rank, pp);
                         st.set_p(rr, -1);
                     } else {
                         flag_error(a.err, DERR_INTERNAL);
+                    }
+                    // The removals, replayed here (fact 4): hole h_rank < n-nr receives
+                    // U[chase(n-1-rank)]; chase steps to n-1-rank(x) while x is a hole. The reads
+                    // (positions >= n-nr) and the writes (holes < n-nr) never meet.
+                    if (pp < n - nr) {
+                        int x = n - 1 - rank, steps = 0;
+                        for (;;) {
+                            int hr = -1;  // rank of x among the holes, or -1
+                            for (int j = 0; j < nr; ++j)
+                                if ((int)(sh.sortbuf[j] >> 32) == x) {
+                                    hr = 0;
+                                    for (int i = 0; i < nr; ++i) hr += sh.sortbuf[i] > sh.sortbuf[j];
+                                    break;
+                                }
+                            if (hr < 0 || steps > nr) break;
+                            x = n - 1 - hr;
+                            ++steps;
+                        }
+                        if (steps > nr || x >= n) {
+                            flag_error(a.err, DERR_INTERNAL);
+                        } else {
+                            const int mv = st.u(x);
+                            st.set_u(pp, mv);
+                            st.set_p(mv, pp);
+                        }
                     }
                 }
                 if (tid == 0) {
@@ -492,6 +515,19 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
             }
         }
         if (!fast_done) {
+            if (slen > 0) {
+                const int64_t ub0 = max_len(a.t_lo, slen);
+                const int shi0 = slot_of(ub0 < NCLS ? ub0 : NCLS);
+                for (int64_t t = tid; t < slen; t += CL_THREADS) {  // p = q_seed
+                    const int b = a.qcol[s0 + t];
+                    atomicOr(&a.pbits[b >> 5], 1u << (b & 31));
+                    a.plist[t] = b;
+                    if (a.hstamp[b] != pass) {  // light: walked up to shi0 by the first walk
+                        a.cstamp[b] = pass;
+                        a.cslot[b] = shi0 + 1;
+                    }
+                }
+            }
             if (tid == 0) {
                 sh.seed = seed;
                 sh.n = n;
@@ -828,56 +864,56 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                 }
                 for (int t = tid; t < sh.pcount; t += CL_THREADS) a.pbits[a.plist[t] >> 5] = 0u;
             }
-        }
 
-        // Replay the pass's removals (U[h] = U.back(); pop, h decreasing): for a hole h_t below
-        // n-k the element that lands there is U[chase(n-1-t)], chase(x) = x unless x is itself a
-        // hole h_j, then chase(n-1-j). Only holes >= n-k can be chased into; they are a prefix of
-        // the decreasing holes list, searched by bisection.
-        __syncthreads();
-        const int k = sh.k;
-        int ktop;
-        {
-            int lo = 0, hi = k;  // first index with holes[idx] < n-k
-            while (lo < hi) {
-                const int mid = (lo + hi) >> 1;
-                if (hole_get(sh, a, mid) >= n - k) lo = mid + 1; else hi = mid;
-            }
-            ktop = lo;
-        }
-        for (int t = ktop + tid; t < k; t += CL_THREADS) {
-            const int h = hole_get(sh, a, t);
-            int x = n - 1 - t;
-            int steps = 0;
-            for (;;) {
-                int lo = 0, hi = ktop;  // find x in holes[0, ktop) (decreasing)
+            // Replay the pass's removals (U[h] = U.back(); pop, h decreasing): for a hole h_t below
+            // n-k the element that lands there is U[chase(n-1-t)], chase(x) = x unless x is itself a
+            // hole h_j, then chase(n-1-j). Only holes >= n-k can be chased into; they are a prefix of
+            // the decreasing holes list, searched by bisection.
+            __syncthreads();
+            const int k = sh.k;
+            int ktop;
+            {
+                int lo = 0, hi = k;  // first index with holes[idx] < n-k
                 while (lo < hi) {
                     const int mid = (lo + hi) >> 1;
-                    if (hole_get(sh, a, mid) > x) lo = mid + 1; else hi = mid;
+                    if (hole_get(sh, a, mid) >= n - k) lo = mid + 1; else hi = mid;
                 }
-                if (lo < ktop && hole_get(sh, a, lo) == x && steps <= k) {
-                    x = n - 1 - lo;
-                    ++steps;
-                } else {
-                    break;
+                ktop = lo;
+            }
+            for (int t = ktop + tid; t < k; t += CL_THREADS) {
+                const int h = hole_get(sh, a, t);
+                int x = n - 1 - t;
+                int steps = 0;
+                for (;;) {
+                    int lo = 0, hi = ktop;  // find x in holes[0, ktop) (decreasing)
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (hole_get(sh, a, mid) > x) lo = mid + 1; else hi = mid;
+                    }
+                    if (lo < ktop && hole_get(sh, a, lo) == x && steps <= k) {
+                        x = n - 1 - lo;
+                        ++steps;
+                    } else {
+                        break;
+                    }
                 }
+                if (steps > k || x >= n) {
+                    flag_error(a.err, DERR_INTERNAL);
+                    continue;
+                }
+                const int r = st.u(x);
+                st.set_u(h, r);
+                st.set_p(r, h);
             }
-            if (steps > k || x >= n) {
-                flag_error(a.err, DERR_INTERNAL);
-                continue;
-            }
-            const int r = st.u(x);
-            st.set_u(h, r);
-            st.set_p(r, h);
         }
-        // No barrier before this: the replay reads none of these fields.
+        // No barrier before this: the replay reads none of these fields, and sh.k was written by
+        // thread 0 itself (fast path) or read after a barrier (general path).
         if (tid == 0) {
-            sh.n = n - k;
+            sh.n = n - sh.k;
             sh.pass += 1;
             sh.ncand = 0;
             sh.nheavy = 0;
             sh.cur = 0;  // the next first walk appends to candidate buffer 0
-            sh.nr = 0;
             if (sh.out > a.M) { flag_error(a.err, DERR_INTERNAL); sh.stop = 1; }
         }
         __syncthreads();
