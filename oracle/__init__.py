@@ -85,6 +85,11 @@ def ref_lib():
             f.argtypes = [ctypes.c_void_p, ip, ip, _f32p]
             f = getattr(L, "ref_bcsr_free_" + suf)
             f.argtypes = [ctypes.c_void_p]
+        L.ref_read_mtx.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32),
+                                   ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int64)]
+        L.ref_read_mtx.restype = ctypes.c_void_p
+        L.ref_mtx_copy.argtypes = [ctypes.c_void_p, _i32p, _i32p, _f32p]
+        L.ref_mtx_free.argtypes = [ctypes.c_void_p]
         _ref = L
     return _ref
 
@@ -237,3 +242,19 @@ def ref_csr_to_bcsr(rp, ci, vals, M, K, rb=16, cb=16, index_dtype=np.int64):
     getattr(L, "ref_bcsr_copy_" + suf)(h, brp, bci, bv)
     getattr(L, "ref_bcsr_free_" + suf)(h)
     return brp, bci[:nb], bv[:nb]
+
+
+def ref_read_mtx(path):
+    """The reference's matrix_utils::io::read_mtx<float> (utils/matrix_io.hpp:27-98) on `path`:
+    (rows, cols, row_ptr int32, col_ind int32, values fp32). Raises RuntimeError if it threw."""
+    L = ref_lib()
+    r, c, n = ctypes.c_int32(0), ctypes.c_int32(0), ctypes.c_int64(0)
+    h = L.ref_read_mtx(os.fsencode(path), ctypes.byref(r), ctypes.byref(c), ctypes.byref(n))
+    if not h:
+        raise RuntimeError("reference read_mtx raised")
+    rp = np.zeros(r.value + 1, dtype=np.int32)
+    ci = np.zeros(max(n.value, 1), dtype=np.int32)
+    v = np.zeros(max(n.value, 1), dtype=np.float32)
+    L.ref_mtx_copy(h, rp, ci, v)
+    L.ref_mtx_free(h)
+    return r.value, c.value, rp, ci[:n.value], v[:n.value]

@@ -135,3 +135,39 @@ void ref_bcsr_free_i32(void* h) { delete static_cast<BcsrBox<int32_t>*>(h); }
 void ref_bcsr_free_i64(void* h) { delete static_cast<BcsrBox<int64_t>*>(h); }
 
 }  // extern "C"
+
+// ---- Matrix Market reader (utils/matrix_io.hpp, header-only, read where it lies) -------------
+#include "matrix_io.hpp"
+
+namespace {
+struct MtxBox {
+    matrix_utils::io::HostCSRMatrix<float> m;
+};
+}  // namespace
+
+extern "C" {
+
+// Reads `path` with matrix_utils::io::read_mtx<float>; returns an opaque box (null if the reader
+// threw) and the sizes; ref_mtx_copy copies the CSR out, ref_mtx_free releases the box.
+void* ref_read_mtx(const char* path, int32_t* rows, int32_t* cols, int64_t* nnz) {
+    try {
+        auto* box = new MtxBox{matrix_utils::io::read_mtx<float>(path)};
+        *rows = box->m.num_rows;
+        *cols = box->m.num_cols;
+        *nnz = static_cast<int64_t>(box->m.values.size());
+        return box;
+    } catch (const std::exception&) {
+        return nullptr;
+    }
+}
+void ref_mtx_copy(void* h, int32_t* rp, int32_t* ci, float* vals) {
+    auto& m = static_cast<MtxBox*>(h)->m;
+    std::memcpy(rp, m.row_ptr.data(), sizeof(int32_t) * m.row_ptr.size());
+    if (!m.values.empty()) {
+        std::memcpy(ci, m.col_ind.data(), sizeof(int32_t) * m.col_ind.size());
+        std::memcpy(vals, m.values.data(), sizeof(float) * m.values.size());
+    }
+}
+void ref_mtx_free(void* h) { delete static_cast<MtxBox*>(h); }
+
+}  // extern "C"
