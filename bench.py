@@ -676,6 +676,117 @@ def run_sharded(args):
         dist.destroy_process_group()
 
 
+VENDOR_HEADER = ("Pattern,M,K,N,Density(%),NNZ,xSpMM_Total,xSpMM_Clust,xSpMM_Perm,xSpMM_Conv,"
+                 "xSpMM_Math,xSpMM_Unperm,Vendor_CSR,Vendor_BSR,Dense_BLAS,dtype,xSpMM_Plan,"
+                 "nnzb_before,nnzb_after")
+
+
+def vendor_patterns(size, densities):
+    """The pattern list of the reference's examples/02_spmm_benchmark.cpp:251-280 (generators of
+    xspmm_b200.generators, values U[0.1, 1))."""
+    from xspmm_b200 import generators as gen
+    yield "Banded_bw16", gen.banded(size, 16)
+    yield "Arrowhead_w16", gen.arrowhead(size, 16)
+    yield "Checkers_b16", gen.checkers(size, size, 16)
+    yield "PowerLaw_a2.5", gen.power_law(size, size, 2.5)
+    for d in densities:
+        tag = f"{d * 100:g}%"
+        yield "UpperTri_" + tag, gen.triangular(size, True, d)
+        yield "Hessenberg_" + tag, gen.hessenberg(size, True, d)
+        yield "BlockDiag_" + tag, gen.block_diagonal(size, 16, d)
+        if size <= 4096:  # sampled per upper-triangle entry on the host
+            yield "NearSymm_" + tag, gen.near_symmetric(size, d, 0.1)
+
+
+def run_vendor_compare(args):
+    """xSpMM against the vendor libraries on the reference's benchmark patterns (the columns of
+    examples/02_spmm_benchmark.cpp:81, plus dtype, the plan-reusing product and block counts).
+    Times in ms: xSpMM stage times from SpMMTimings of one Tier-2 call after warm-up (as the
+    reference prints them); vendor and plan times averaged over 10 calls after 3 warm-ups with
+    CUDA events (the reference's BenchTimer). Vendor CSR/BSR = cuSPARSE SpMM through
+    torch.sparse (BSR only for fp32, the type cuSPARSE's block kernel takes), dense = cuBLAS
+    through torch.matmul (TF32 off, as cublasSgemm). N = M = K, B = ones, as the reference."""
+    import torch
+
+    import xspmm_b200 as xs
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = "cuda:0"
+    ex = xs.CudaExecutor(0)
+    sizes = [int(s) for s in args.vendor_sizes.split(",")]
+    dens = [float(d) for d in args.vendor_densities.split(",")]
+    dtypes = {"fp32": (np.float32, torch.float32), "fp16": (np.float16, torch.float16)}
+    print(VENDOR_HEADER, flush=True)
+
+    def avg_ms(fn, iters=10, warm=3):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    for size in sizes:
+        for name, (rp, ci, v) in vendor_patterns(size, dens):
+            for dname in args.vendor_dtypes.split(","):
+                npt, tdt = dtypes[dname]
+                M = K = N = size
+                nnz = int(rp[-1])
+                rp32, ci32 = rp.astype(np.int32), ci.astype(np.int32)
+                vals = v.astype(npt)
+                A = xs.CSRMatrix.from_host(ex, M, K, rp32, ci32, vals, index_dtype=torch.int32)
+                B = torch.ones((K, N), dtype=tdt, device=dev)
+                C = torch.zeros((M, N), dtype=torch.float32, device=dev)
+                for _ in range(2):
+                    xs.spmm(ex, A, B, C, N, 16, True)
+                t = xs.SpMMTimings()
+                xs.spmm(ex, A, B, C, N, 16, True, t)
+                torch.cuda.synchronize()
+                plan = xs.SpMMPlan(ex, A, 16, True)
+                plan_ms = avg_ms(lambda: plan.execute(B, C, N))
+                after = plan.info()["nnz_blocks"]
+                plan.close()
+                before = xs.csr_to_bcsr(ex, A, 16, 16).num_blocks
+                Acsr = torch.sparse_csr_tensor(torch.as_tensor(rp32, device=dev),
+                                               torch.as_tensor(ci32, device=dev),
+                                               torch.as_tensor(vals, device=dev), size=(M, K))
+                row = {"csr": None, "bsr": None, "dense": None}
+                try:
+                    row["csr"] = avg_ms(lambda: torch.sparse.mm(Acsr, B))
+                except Exception:
+                    pass
+                if dname == "fp32":
+                    try:
+                        Absr = Acsr.to_sparse_bsr((16, 16)) if M % 16 == 0 else None
+                        if Absr is not None:
+                            row["bsr"] = avg_ms(lambda: torch.sparse.mm(Absr, B))
+                        del Absr
+                    except Exception:
+                        pass
+                try:
+                    Ad = Acsr.to_dense()
+                    row["dense"] = avg_ms(lambda: torch.matmul(Ad, B))
+                    del Ad
+                except Exception:
+                    pass
+                del Acsr
+
+                def f(x):
+                    return "" if x is None else f"{x:.3f}"
+                print(",".join([name, str(M), str(K), str(N), f"{100.0 * nnz / (M * K):.4f}",
+                                str(nnz), f(t.total_pipeline_ms), f(t.clustering_ms),
+                                f(t.permutation_ms), f(t.conversion_ms), f(t.spmm_ms),
+                                f(t.unpermutation_ms), f(row["csr"]), f(row["bsr"]),
+                                f(row["dense"]), dname, f(plan_ms), str(before), str(after)]),
+                      flush=True)
+                del A, B, C
+                torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -693,7 +804,17 @@ def main():
                     help="one full-size matrix split by block rows over the ranks (Tier-1)")
     ap.add_argument("--scaling-sweep", action="store_true",
                     help="with --sharded: also time the first 1, 2, 4, ... ranks of the launch")
+    ap.add_argument("--vendor-compare", action="store_true",
+                    help="CSV: xSpMM vs cuSPARSE CSR/BSR and cuBLAS on the reference's patterns")
+    ap.add_argument("--vendor-sizes", default="1024,4096",
+                    help="the reference sweeps 1024,2048,4096,8192")
+    ap.add_argument("--vendor-densities", default="0.1,0.01,0.001",
+                    help="the reference sweeps 0.7,0.5,0.2,0.1,0.01,0.005,0.001")
+    ap.add_argument("--vendor-dtypes", default="fp32,fp16")
     args = ap.parse_args()
+    if args.vendor_compare:
+        run_vendor_compare(args)
+        return
     if args.tier1_compare:
         run_tier1_compare(args)
         return

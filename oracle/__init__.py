@@ -90,6 +90,12 @@ def ref_lib():
         L.ref_read_mtx.restype = ctypes.c_void_p
         L.ref_mtx_copy.argtypes = [ctypes.c_void_p, _i32p, _i32p, _f32p]
         L.ref_mtx_free.argtypes = [ctypes.c_void_p]
+        L.ref_gen.argtypes = [ctypes.c_int, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                              ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                              ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int64)]
+        L.ref_gen.restype = ctypes.c_void_p
+        L.ref_gen_copy.argtypes = [ctypes.c_void_p, _i32p, _i32p, _f32p]
+        L.ref_gen_free.argtypes = [ctypes.c_void_p]
         _ref = L
     return _ref
 
@@ -258,3 +264,24 @@ def ref_read_mtx(path):
     L.ref_mtx_copy(h, rp, ci, v)
     L.ref_mtx_free(h)
     return r.value, c.value, rp, ci[:n.value], v[:n.value]
+
+
+REF_GEN_KINDS = {"banded": 0, "triangular": 1, "hessenberg": 2, "arrowhead": 3, "checkers": 4,
+                 "block_diagonal": 5, "near_symmetric": 6, "power_law": 7}
+
+
+def ref_generate(kind, a, b=0, c=0, f1=0.0, f2=0.0, seed=42):
+    """The reference's own generator `kind` (utils/matrix_gen.hpp:68-323, float values, int32
+    indices); parameters as in ref_gen of ref_driver.cpp. Returns (rows, row_ptr, col_ind,
+    values)."""
+    L = ref_lib()
+    rows, n = ctypes.c_int32(0), ctypes.c_int64(0)
+    h = L.ref_gen(REF_GEN_KINDS[kind], a, b, c, f1, f2, seed, ctypes.byref(rows), ctypes.byref(n))
+    if not h:
+        raise RuntimeError("reference generator raised")
+    rp = np.zeros(rows.value + 1, dtype=np.int32)
+    ci = np.zeros(max(n.value, 1), dtype=np.int32)
+    v = np.zeros(max(n.value, 1), dtype=np.float32)
+    L.ref_gen_copy(h, rp, ci, v)
+    L.ref_gen_free(h)
+    return rows.value, rp, ci[:n.value], v[:n.value]

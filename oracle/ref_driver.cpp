@@ -171,3 +171,55 @@ void ref_mtx_copy(void* h, int32_t* rp, int32_t* ci, float* vals) {
 void ref_mtx_free(void* h) { delete static_cast<MtxBox*>(h); }
 
 }  // extern "C"
+
+// ---- generators (utils/matrix_gen.hpp, header-only, read where it lies) ----------------------
+#include "matrix_gen.hpp"
+
+namespace {
+struct GenBox {
+    std::vector<int32_t> rp, ci;
+    std::vector<float> v;
+};
+}  // namespace
+
+extern "C" {
+
+// kind: 0 banded(a=size, b=bandwidth), 1 triangular(a, upper=b, density=f1),
+// 2 hessenberg(a, upper=b, density=f1), 3 arrowhead(a, width=b), 4 checkers(rows=a, cols=b,
+// block=c), 5 block_diagonal(a, block=b, density=f1), 6 near_symmetric(a, density=f1,
+// drop=f2), 7 power_law(rows=a, cols=b, alpha=f1). Returns an opaque box (null on error).
+void* ref_gen(int kind, int32_t a, int32_t b, int32_t c, float f1, float f2, int seed,
+              int32_t* rows_out, int64_t* nnz_out) {
+    namespace g = matrix_utils::generation;
+    try {
+        auto* box = new GenBox;
+        int32_t rows = a;
+        switch (kind) {
+            case 0: g::generate_banded<float, int32_t>(a, b, box->rp, box->ci, box->v, seed); break;
+            case 1: g::generate_triangular<float, int32_t>(a, b != 0, f1, box->rp, box->ci, box->v, seed); break;
+            case 2: g::generate_hessenberg<float, int32_t>(a, b != 0, f1, box->rp, box->ci, box->v, seed); break;
+            case 3: g::generate_arrowhead<float, int32_t>(a, b, box->rp, box->ci, box->v, seed); break;
+            case 4: g::generate_checkers<float, int32_t>(a, b, c, box->rp, box->ci, box->v, seed); break;
+            case 5: g::generate_block_diagonal<float, int32_t>(a, b, f1, box->rp, box->ci, box->v, seed); break;
+            case 6: g::generate_near_symmetric<float, int32_t>(a, f1, f2, box->rp, box->ci, box->v, seed); break;
+            case 7: g::generate_power_law<float, int32_t>(a, b, f1, box->rp, box->ci, box->v, seed); break;
+            default: delete box; return nullptr;
+        }
+        *rows_out = rows;
+        *nnz_out = static_cast<int64_t>(box->v.size());
+        return box;
+    } catch (const std::exception&) {
+        return nullptr;
+    }
+}
+void ref_gen_copy(void* h, int32_t* rp, int32_t* ci, float* v) {
+    auto* box = static_cast<GenBox*>(h);
+    std::memcpy(rp, box->rp.data(), sizeof(int32_t) * box->rp.size());
+    if (!box->v.empty()) {
+        std::memcpy(ci, box->ci.data(), sizeof(int32_t) * box->ci.size());
+        std::memcpy(v, box->v.data(), sizeof(float) * box->v.size());
+    }
+}
+void ref_gen_free(void* h) { delete static_cast<GenBox*>(h); }
+
+}  // extern "C"

@@ -33,9 +33,17 @@ def _np(t):
 # ------------------------------------------------------------------------------------------------
 # structure: clustering, permutation, conversion, unpermute -- bit-exact
 # ------------------------------------------------------------------------------------------------
+@pytest.fixture(params=["auto", "index"])
+def cluster_kernel(request, monkeypatch):
+    """Clustering through the automatic choice (the shared-memory bitset sweep for inputs this
+    small) and forced through the inverted-index kernel that large inputs take."""
+    monkeypatch.setenv("XSPMM_CLUSTER_KERNEL", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("idx", IDX, ids=["i32", "i64"])
 @pytest.mark.parametrize("path", CASES, ids=[os.path.basename(p)[:-4] for p in CASES])
-def test_golden_structure(executor, path, idx):
+def test_golden_structure(executor, path, idx, cluster_kernel):
     g = load_golden(path)
     M, K, tau, w = int(g["M"]), int(g["K"]), float(g["tau"]), int(g["w"])
     A = _csr(executor, M, K, g["row_ptr"], g["col_ind"], g["vals"], idx, np.float32)
@@ -68,7 +76,7 @@ def _random(seed, M=None, K=None):
 
 
 @pytest.mark.parametrize("seed", range(12))
-def test_random_structure_vs_oracle(executor, seed):
+def test_random_structure_vs_oracle(executor, seed, cluster_kernel):
     M, K, rp, ci, v = _random(seed)
     idx = IDX[seed % 2]
     tau = [0.5, 0.3, 0.8, 0.5][seed % 4]

@@ -50,6 +50,9 @@
 
 #include "ops.cuh"
 
+#include <cstdlib>
+#include <cstring>
+
 namespace xspmm_b200 {
 namespace {
 
@@ -1043,6 +1046,14 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
         after_launch(h, "reversed_perm");
         return;
     }
+    // Row patterns that fit one SM's shared memory as bitsets: the sweep of cluster_bits.cu.
+    // XSPMM_CLUSTER_KERNEL = index | bits forces one of the two (bits fails if they do not fit).
+    const char* ck = std::getenv("XSPMM_CLUSTER_KERNEL");
+    const bool want_index = ck && std::strcmp(ck, "index") == 0;
+    const bool want_bits = ck && std::strcmp(ck, "bits") == 0;
+    if (!want_index && cluster_jaccard_bits<IT>(h, M, K, row_ptr, col_ind, tau, w, perm)) return;
+    XS_REQUIRE(!want_bits, XSPMM_STATUS_UNSUPPORTED,
+               "bitset clustering: the row patterns do not fit in shared memory");
     const int64_t nbc = ceil_div(K, w);
     XS_REQUIRE(nbc < (int64_t(1) << 31) / NCLS, XSPMM_STATUS_UNSUPPORTED,
                "clustering supports at most 2^26 block columns");

@@ -1,0 +1,246 @@
+// cluster_bits.cu -- exact greedy 1-D Jaccard clustering for matrices whose row patterns fit in
+// shared memory as bitsets.
+//
+// Same result, bit for bit, as the reference's compute_1d_jaccard_clustering
+// (src/cpu/clustering_sylos_labini.cpp:51-120) and as the inverted-index kernel of cluster.cu.
+// The reference holds each row's block-column set q_r as a dense bitset (:13-33) and tests every
+// remaining row against the cluster pattern p (:86-107). When M x ceil(nbc/32) words fit in one
+// SM's shared memory, that is also the fastest layout on the GPU: one CTA keeps all bitsets, the
+// pattern sizes |q_r| and the position array U on chip, and a round evaluates every unscanned
+// position at once -- |p n q| is a few AND + popc, |p u q| = |p| + |q| - |p n q| -- with one warp
+// per 32 consecutive positions, so acceptance and growth come out as ballot words. The inverted
+// index pays off when p meets few rows; on patterns where every pass meets a large share of the
+// matrix (random structure of a few thousand rows) its walk costs more than this sweep.
+//
+// Pass structure (facts (3) and (4) of cluster.cu): positions below the scan pointer are fixed
+// during a pass, so a round evaluates positions [0, top] against the current p; g = the highest
+// accepted position whose row adds block columns to p. Accepted positions in (g, top] and g are
+// final in this round: one thread replays them in decreasing order exactly as the reference does
+// (perm gets U[j]; U[j] = U.back(); pop), p |= q_{U[g]}, and the next round scans [0, g - 1].
+// With no growth the pass ends and the next seed is U.back(). Two CTA barriers per round.
+#include "ops.cuh"
+
+namespace xspmm_b200 {
+namespace {
+
+constexpr int CB_THREADS = 512;
+constexpr int CB_WARPS = CB_THREADS / 32;
+
+__device__ __forceinline__ bool cb_accept(int inter, int uni, float tau, float t_lo) {
+    // 1 - (float)|p n q| / (float)|p u q| <= tau, |p u q| == 0 -> distance 0 (:35-46). A row
+    // the test accepts has |p n q| >= t_lo |p u q| with t_lo = 1 - tau - 2^-22 (the margin is
+    // above the float rounding of the test, and of the product here for |p u q| < 2^24), so rows
+    // below that are rejected without the division.
+    if (uni == 0) return 0.0f <= tau;
+    if ((float)inter < t_lo * (float)uni) return false;
+    return __fsub_rn(1.0f, __fdiv_rn((float)inter, (float)uni)) <= tau;
+}
+
+struct CbShared {
+    int n;      // rows still unclustered (positions [0, n) of U)
+    int top;    // highest position the next round evaluates (-1: none)
+    int out;    // next perm slot
+    int g;      // highest accepted position whose row grows p (-1: none)
+    int prow;   // row whose pattern joins p (pmode 1) or becomes p (pmode 2)
+    int pmode;  // 0: p unchanged, 1: p |= q_prow, 2: p = q_prow (new seed)
+    int psz;    // |p|
+};
+
+// smem: bits[M * ns] | qsz[M] (uint16) | U[M] | acc[ceil(M/32)] | p[nw]. A row's bitset takes
+// ns = nw | 1 words: with an odd stride the rows that a warp reads at once fall on different
+// banks.
+template <typename IT>
+__global__ void __launch_bounds__(CB_THREADS, 1)
+cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_ind, int M,
+                    int64_t K, int64_t w, int nw, float tau, float t_lo, IT* __restrict__ perm,
+                    unsigned* __restrict__ err) {
+    extern __shared__ __align__(16) uint8_t cb_smem[];
+    __shared__ CbShared st;
+    const int nmw = (M + 31) >> 5;
+    const int ns = nw | 1;
+    uint32_t* bits = reinterpret_cast<uint32_t*>(cb_smem);
+    uint16_t* qsz = reinterpret_cast<uint16_t*>(bits + (size_t)M * ns);
+    int32_t* U = reinterpret_cast<int32_t*>(
+        cb_smem + (((size_t)M * ns * 4 + (size_t)M * 2 + 15) & ~size_t(15)));
+    uint32_t* acc = reinterpret_cast<uint32_t*>(U + M);
+    uint32_t* p = acc + nmw;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    // ---- row bitsets from the CSR (block column = col / w) ----
+    for (int64_t i = tid; i < (int64_t)M * ns; i += CB_THREADS) bits[i] = 0u;
+    for (int i = tid; i < M; i += CB_THREADS) U[i] = i;  // U = [0, 1, ..., M-1] (:78-82)
+    if (tid == 0) {
+        st.n = M;
+        st.top = -1;  // the first iteration only takes the first seed
+        st.out = 0;
+        st.g = -1;
+        st.prow = -1;
+        st.pmode = 0;
+        st.psz = 0;
+    }
+    __syncthreads();
+    for (int r = warp; r < M; r += CB_WARPS) {
+        const int64_t b = (int64_t)row_ptr[r], e = (int64_t)row_ptr[r + 1];
+        if (e < b) {
+            if (lane == 0) flag_error(err, DERR_ROW_PTR);
+            continue;
+        }
+        for (int64_t j = b + lane; j < e; j += 32) {
+            const int64_t c = (int64_t)col_ind[j];
+            if (c < 0 || c >= K) {
+                flag_error(err, DERR_COL_OUT_OF_RANGE);
+                continue;
+            }
+            const int64_t bc = c / w;
+            atomicOr(&bits[(size_t)r * ns + (bc >> 5)], 1u << (bc & 31));
+        }
+    }
+    __syncthreads();
+    for (int r = tid; r < M; r += CB_THREADS) {
+        int sz = 0;
+        for (int k = 0; k < nw; ++k) sz += __popc(bits[(size_t)r * ns + k]);
+        qsz[r] = (uint16_t)sz;
+    }
+    __syncthreads();
+
+    // ---- greedy passes: one iteration per round ----
+    // Each iteration either ends a pass (at most M passes) or accepts the row that grows p (at
+    // most M such rows), so the loop ends after at most 2M + 1 rounds.
+    for (;;) {
+        const int top = st.top, n = st.n, psz = st.psz;
+        if (top < 0 && n <= 0) break;
+        if (top >= 0) {
+            // warp w evaluates positions [32c, 32c + 32) for c = w, w + WARPS, ...
+            int gmax = -1;
+            for (int c = warp; c <= (top >> 5); c += CB_WARPS) {
+                const int j = (c << 5) + lane;
+                bool a = false, gr = false;
+                if (j <= top) {
+                    const int r = U[j];
+                    const uint32_t* q = bits + (size_t)r * ns;
+                    int inter = 0;
+                    for (int k = 0; k < nw; ++k) inter += __popc(p[k] & q[k]);
+                    const int qs = qsz[r];
+                    a = cb_accept(inter, psz + qs - inter, tau, t_lo);
+                    gr = a && inter < qs;
+                }
+                const uint32_t av = __ballot_sync(0xffffffffu, a);
+                const uint32_t gv = __ballot_sync(0xffffffffu, gr);
+                if (lane == 0) acc[c] = av;
+                if (gv) gmax = max(gmax, (c << 5) + 31 - __clz(gv));
+            }
+            if (lane == 0 && gmax >= 0) atomicMax(&st.g, gmax);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            const int g = st.g;
+            int nn = n, out = st.out, grow_row = -1;
+            if (top >= 0) {
+                // the round's acceptances in decreasing position, (g, top] then g, replayed as
+                // the reference removes them: perm += U[j]; U[j] = U.back(); pop. The warp finds
+                // the nonzero acceptance words 32 at a time; lane 0 replays their bits.
+                const int lo = g < 0 ? 0 : g;
+                const int chi = top >> 5, clo = lo >> 5;
+                for (int base = chi; base >= clo; base -= 32) {
+                    const int c = base - lane;
+                    uint32_t v = 0u;
+                    if (c >= clo) {
+                        v = acc[c];
+                        const int hi_bit = top - (c << 5);  // bits above it are past top
+                        if (hi_bit < 31) v &= (1u << (hi_bit + 1)) - 1u;
+                        const int lo_bit = lo - (c << 5);   // bits below it wait for next round
+                        if (lo_bit > 0) v &= ~((1u << lo_bit) - 1u);
+                    }
+                    uint32_t live = __ballot_sync(0xffffffffu, v != 0u);
+                    while (live) {  // lowest lane = highest word first
+                        const int l = __ffs(live) - 1;
+                        live &= live - 1u;
+                        uint32_t vv = __shfl_sync(0xffffffffu, v, l);
+                        if (lane == 0) {
+                            const int cc = base - l;
+                            while (vv) {
+                                const int b = 31 - __clz(vv);
+                                vv &= ~(1u << b);
+                                const int j = (cc << 5) + b;
+                                const int row = U[j];
+                                if (j == g) grow_row = row;
+                                perm[out++] = (IT)row;
+                                U[j] = U[nn - 1];
+                                --nn;
+                            }
+                        }
+                    }
+                }
+            }
+            if (lane == 0) {
+                st.g = -1;
+                if (grow_row >= 0) {  // p grows; rows below g are evaluated again
+                    st.top = g - 1;
+                    st.prow = grow_row;
+                    st.pmode = 1;
+                } else if (nn > 0) {  // pass over: next seed = U.back()
+                    const int seed = U[nn - 1];
+                    perm[out++] = (IT)seed;
+                    --nn;
+                    st.top = nn - 1;
+                    st.prow = seed;
+                    st.pmode = 2;
+                } else {
+                    st.top = -1;
+                    st.pmode = 0;
+                }
+                st.n = nn;
+                st.out = out;
+            }
+            __syncwarp();
+            const int mode = st.pmode, row = st.prow;
+            if (mode != 0) {
+                int sz = 0;
+                for (int k = lane; k < nw; k += 32) {
+                    const uint32_t q = bits[(size_t)row * ns + k];
+                    const uint32_t v = mode == 2 ? q : (p[k] | q);
+                    p[k] = v;
+                    sz += __popc(v);
+                }
+                for (int o = 16; o; o >>= 1) sz += __shfl_xor_sync(0xffffffffu, sz, o);
+                if (lane == 0) st.psz = sz;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+// Shared memory the bitset kernel needs for M rows of nbc block columns (0 if it cannot run).
+size_t cluster_bits_smem(int64_t M, int64_t nbc) {
+    if (M <= 0 || M >= (int64_t(1) << 24) || nbc <= 0 || nbc >= 65536) return 0;
+    const int64_t nw = (nbc + 31) / 32, ns = nw | 1;
+    const int64_t nmw = (M + 31) / 32;
+    const size_t head = (((size_t)M * ns * 4 + (size_t)M * 2 + 15) & ~size_t(15));
+    return head + (size_t)M * 4 + (size_t)nmw * 4 + (size_t)nw * 4;
+}
+
+template <typename IT>
+bool cluster_jaccard_bits(Handle& h, int64_t M, int64_t K, const IT* row_ptr, const IT* col_ind,
+                          float tau, int64_t w, IT* perm) {
+    const int64_t nbc = ceil_div(K, w);
+    const size_t smem = cluster_bits_smem(M, nbc);
+    int optin = 0;
+    XS_CHECK_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, h.device));
+    if (smem == 0 || smem + sizeof(CbShared) + 1024 > (size_t)optin) return false;
+    auto kern = cluster_bits_kernel<IT>;
+    XS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const float t_lo = (float)((1.0 - (double)tau) - 1.0 / (double)(1 << 22));
+    kern<<<1, CB_THREADS, smem, h.stream>>>(row_ptr, col_ind, (int)M, K, w, (int)((nbc + 31) / 32),
+                                           tau, t_lo, perm, h.d_err);
+    after_launch(h, "cluster_bits");
+    return true;
+}
+
+template bool cluster_jaccard_bits<int32_t>(Handle&, int64_t, int64_t, const int32_t*,
+                                            const int32_t*, float, int64_t, int32_t*);
+template bool cluster_jaccard_bits<int64_t>(Handle&, int64_t, int64_t, const int64_t*,
+                                            const int64_t*, float, int64_t, int64_t*);
+
+}  // namespace xspmm_b200

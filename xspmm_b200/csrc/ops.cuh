@@ -72,6 +72,13 @@ void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT
 enum class Tier1Kernel { Auto, Mma, Tc };
 Tier1Kernel tier1_kernel_choice(const Handle& h);
 
+// The same clustering with every row's block-column bitset in one CTA's shared memory; returns
+// false (and does nothing) when they do not fit.
+template <typename IT>
+bool cluster_jaccard_bits(Handle& h, int64_t M, int64_t K, const IT* row_ptr, const IT* col_ind,
+                          float tau, int64_t w, IT* perm);
+size_t cluster_bits_smem(int64_t M, int64_t nbc);
+
 // Exact greedy Jaccard clustering (writes perm[M]).
 template <typename IT>
 void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
