@@ -33,10 +33,11 @@ def _np(t):
 # ------------------------------------------------------------------------------------------------
 # structure: clustering, permutation, conversion, unpermute -- bit-exact
 # ------------------------------------------------------------------------------------------------
-@pytest.fixture(params=["auto", "index"])
+@pytest.fixture(params=["auto", "sweep", "index"])
 def cluster_kernel(request, monkeypatch):
     """Clustering through the automatic choice (the shared-memory bitset sweep for inputs this
-    small) and forced through the inverted-index kernel that large inputs take."""
+    small), forced through the cluster-wide sweep, and through the inverted-index kernel that the
+    largest inputs take."""
     monkeypatch.setenv("XSPMM_CLUSTER_KERNEL", request.param)
     return request.param
 
@@ -105,12 +106,17 @@ def test_random_structure_vs_oracle(executor, seed, cluster_kernel):
     ("cfg4", dict(n=1 << 16, N=8)),
     ("cfg5", dict(scale=14, N=8)),
 ])
-def test_config_clustering_vs_oracle(executor, name, kw):
+def test_config_clustering_vs_oracle(executor, name, kw, cluster_kernel):
     P = synth.CONFIGS[name](**kw)
     A = _csr(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values, torch.int32,
              P.values.dtype)
     perm = torch.zeros(P.M, dtype=torch.int32, device=executor.device)
-    xs.compute_1d_jaccard_clustering(executor, A, 0.5, 16, perm)
+    try:
+        xs.compute_1d_jaccard_clustering(executor, A, 0.5, 16, perm)
+    except xs.XSpMMError as e:
+        if cluster_kernel != "auto" and e.status == 2:  # UNSUPPORTED: does not fit that path
+            pytest.skip(str(e))
+        raise
     assert np.array_equal(_np(perm), oracle.cluster_fast(P.row_ptr, P.col_ind, P.M, P.K))
 
 

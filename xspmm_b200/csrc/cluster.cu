@@ -64,6 +64,9 @@ constexpr int HOLE_CAP = 1024;      // holes of a pass kept in shared memory (th
 constexpr int SMEM_ROWS = 20480;    // U and pos live in shared memory up to this many rows
 constexpr int64_t HEAVY = 2048;     // inverted lists longer than this are walked by size window
 constexpr int LIGHT_MASK = (1 << 30) - 1;
+// Expected inverted-list entries per pass above which the cluster sweep (cluster_bits.cu) is
+// faster, from measurements on B200 (index kernel ~2 ns per entry, sweep ~10 us per pass).
+constexpr int64_t SWEEP_VISITS = 8192;
 constexpr int HEAVY_MARK = 1 << 30;
 
 struct ClusterArgs {
@@ -1046,12 +1049,18 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
         after_launch(h, "reversed_perm");
         return;
     }
-    // Row patterns that fit one SM's shared memory as bitsets: the sweep of cluster_bits.cu.
-    // XSPMM_CLUSTER_KERNEL = index | bits forces one of the two (bits fails if they do not fit).
+    // Three exact implementations (cluster_bits.cu, this file): row bitsets in one SM's shared
+    // memory (whenever they fit); row patterns spread over a cluster's shared memory (when they
+    // fit and the inverted lists are long, see SWEEP_VISITS); the inverted index otherwise.
+    // XSPMM_CLUSTER_KERNEL = bits | sweep | index forces one (bits and sweep fail if the matrix
+    // does not fit them).
     const char* ck = std::getenv("XSPMM_CLUSTER_KERNEL");
     const bool want_index = ck && std::strcmp(ck, "index") == 0;
     const bool want_bits = ck && std::strcmp(ck, "bits") == 0;
-    if (!want_index && cluster_jaccard_bits<IT>(h, M, K, row_ptr, col_ind, tau, w, perm)) return;
+    const bool want_sweep = ck && std::strcmp(ck, "sweep") == 0;
+    if (!want_index && !want_sweep &&
+        cluster_jaccard_bits<IT>(h, M, K, row_ptr, col_ind, tau, w, perm))
+        return;
     XS_REQUIRE(!want_bits, XSPMM_STATUS_UNSUPPORTED,
                "bitset clustering: the row patterns do not fit in shared memory");
     const int64_t nbc = ceil_div(K, w);
@@ -1075,6 +1084,15 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     }
     qptr_it.release();
     qcol_it.release();
+    // An inverted-index pass visits ~sum_c len_c^2 / M list entries for a random seed (~2 ns
+    // each on a B200), at least npat^2 / (nbc M) (equal when the columns are evenly used, as in
+    // random structure); the cluster sweep's pass costs ~10 us whatever the structure.
+    const double visits_lb = (double)npat * (double)npat / ((double)nbc * (double)M);
+    if (want_sweep || (!want_index && visits_lb > (double)SWEEP_VISITS)) {
+        if (cluster_jaccard_sweep<IT>(h, M, nbc, qptr.get(), qcol.get(), tau, perm)) return;
+        XS_REQUIRE(!want_sweep, XSPMM_STATUS_UNSUPPORTED,
+                   "cluster sweep: the row patterns do not fit a cluster's shared memory");
+    }
 
     // Inverted index by (block column, size class).
     const int64_t nb = std::max<int64_t>(nbc, 1);

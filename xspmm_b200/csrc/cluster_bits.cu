@@ -20,6 +20,8 @@
 // With no growth the pass ends and the next seed is U.back(). Two CTA barriers per round.
 #include "ops.cuh"
 
+#include <vector>
+
 namespace xspmm_b200 {
 namespace {
 
@@ -210,6 +212,260 @@ cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_i
     }
 }
 
+// ---- the same sweep over a thread-block cluster ----------------------------------------------
+// For matrices whose bitsets exceed one SM but whose row patterns (sorted distinct block
+// columns, 2 bytes each) fit the distributed shared memory of a cluster of up to 8 CTAs (the
+// hidden-block config: 16384 rows, ~84K pattern entries). CTA k owns rows [kR, (k+1)R): their
+// pattern lists, |q| and positions pos[r] live in its shared memory, and it evaluates its own rows
+// whose position is in [0, top] against a copy of p held as a bitmap (|p n q| = bits of p at the
+// row's columns). Acceptances are marked in CTA 0's acceptance bitmap and the highest growing
+// position in CTA 0's state, through distributed shared memory. After a cluster barrier CTA 0
+// (which holds U) replays the round exactly as above, writes the new positions of the rows it
+// moves into their owners' shared memory, updates p from the owner's pattern, and a second
+// cluster barrier publishes it. No global memory is read after the set-up.
+constexpr int CS_THREADS = 512;
+constexpr int CS_WARPS = CS_THREADS / 32;
+
+__device__ __forceinline__ uint32_t cs_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t cs_mapa(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(cs_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ uint32_t cs_ld32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t cs_ld16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared::cluster.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cs_st32(uint32_t a, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void cs_red_or(uint32_t a, uint32_t v) {
+    asm volatile("red.shared::cluster.or.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void cs_red_max(uint32_t a, int v) {
+    asm volatile("red.shared::cluster.max.s32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void cs_cluster_sync() {
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+__device__ __forceinline__ uint32_t cs_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+struct CsShared {
+    int n, top, out, g, psz, prow, pmode, pad;
+};
+
+// Shared-memory layout (identical in every CTA, so mapa finds a peer's copy at the same offset):
+// pos[R] int32 | loff[R + 1] uint32 | acc[nmw] uint32 | pl[nw] uint32 | qsz[R] uint16 |
+// lq[emax] uint16 | (16-byte aligned) U[M] int32 (used by CTA 0 only)
+struct CsLayout {
+    size_t pos, loff, acc, pl, qsz, lq, U, total;
+};
+__host__ __device__ inline CsLayout cs_layout(int64_t M, int64_t R, int64_t nw, int64_t emax) {
+    CsLayout L;
+    const int64_t nmw = (M + 31) / 32;
+    L.pos = 0;
+    L.loff = L.pos + 4 * (size_t)R;
+    L.acc = L.loff + 4 * (size_t)(R + 1);
+    L.pl = L.acc + 4 * (size_t)nmw;
+    L.qsz = L.pl + 4 * (size_t)nw;
+    L.lq = L.qsz + 2 * (size_t)R;
+    L.U = (L.lq + 2 * (size_t)emax + 15) & ~size_t(15);
+    L.total = L.U + 4 * (size_t)M;
+    return L;
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(CS_THREADS, 1)
+cluster_sweep_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ qcol, int M,
+                     int R, int nw, int emax, float tau, float t_lo, IT* __restrict__ perm,
+                     unsigned* __restrict__ err) {
+    extern __shared__ __align__(16) uint8_t cs_smem[];
+    __shared__ CsShared st;
+    const CsLayout L = cs_layout(M, R, nw, emax);
+    int32_t* pos = reinterpret_cast<int32_t*>(cs_smem + L.pos);
+    uint32_t* loff = reinterpret_cast<uint32_t*>(cs_smem + L.loff);
+    uint32_t* acc = reinterpret_cast<uint32_t*>(cs_smem + L.acc);
+    uint32_t* pl = reinterpret_cast<uint32_t*>(cs_smem + L.pl);
+    uint16_t* qsz = reinterpret_cast<uint16_t*>(cs_smem + L.qsz);
+    uint16_t* lq = reinterpret_cast<uint16_t*>(cs_smem + L.lq);
+    int32_t* U = reinterpret_cast<int32_t*>(cs_smem + L.U);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t rank = cs_rank();
+    const int nmw = (M + 31) >> 5;
+    const int r0 = (int)min((int64_t)rank * R, (int64_t)M), r1 = (int)min((int64_t)r0 + R, (int64_t)M);
+    const int nr = r1 - r0;
+
+    // ---- set-up: this CTA's rows ----
+    const int64_t base = qptr[r0];
+    const int64_t ne = qptr[r1] - base;
+    if (ne > emax) {  // the host sized emax from the same offsets
+        if (tid == 0) flag_error(err, DERR_INTERNAL);
+    }
+    for (int i = tid; i < nr; i += CS_THREADS) {
+        const int64_t a = qptr[r0 + i], b = qptr[r0 + i + 1];
+        loff[i] = (uint32_t)(a - base);
+        qsz[i] = (uint16_t)(b - a);
+        pos[i] = r0 + i;  // U starts as [0, 1, ..., M-1]
+    }
+    if (tid == 0) loff[nr] = (uint32_t)ne;
+    for (int64_t e = tid; e < min(ne, (int64_t)emax); e += CS_THREADS) lq[e] = (uint16_t)qcol[base + e];
+    for (int i = tid; i < nmw; i += CS_THREADS) acc[i] = 0u;
+    if (rank == 0) {
+        for (int j = tid; j < M; j += CS_THREADS) U[j] = j;
+        if (tid == 0) {
+            st.n = M;
+            st.top = -1;  // the first iteration only takes the first seed
+            st.out = 0;
+            st.g = -1;
+            st.psz = 0;
+            st.prow = -1;
+            st.pmode = 0;
+        }
+        for (int k = tid; k < nw; k += CS_THREADS) pl[k] = 0u;
+    }
+    __syncthreads();
+    cs_cluster_sync();
+
+    const uint32_t st_g_remote = cs_mapa(&st.g, 0);
+    // Each iteration either ends a pass (at most M) or accepts the row that grows p (at most M):
+    // at most 2M + 1 iterations, the same number in every CTA (all read CTA 0's state).
+    for (;;) {
+        if (rank != 0) {
+            if (tid == 0) {
+                st.n = (int)cs_ld32(cs_mapa(&st.n, 0));
+                st.top = (int)cs_ld32(cs_mapa(&st.top, 0));
+                st.psz = (int)cs_ld32(cs_mapa(&st.psz, 0));
+            }
+            for (int k = tid; k < nw; k += CS_THREADS) pl[k] = cs_ld32(cs_mapa(&pl[k], 0));
+        }
+        __syncthreads();
+        const int top = st.top, n = st.n, psz = st.psz;
+        if (top < 0 && n <= 0) break;
+        if (top >= 0) {
+            for (int i = tid; i < nr; i += CS_THREADS) {
+                const int j = pos[i];
+                if (j < 0 || j > top) continue;
+                int inter = 0;
+                for (uint32_t e = loff[i], e1 = loff[i + 1]; e < e1; ++e) {
+                    const uint32_t c = lq[e];
+                    inter += (pl[c >> 5] >> (c & 31)) & 1u;
+                }
+                const int qs = qsz[i];
+                if (cb_accept(inter, psz + qs - inter, tau, t_lo)) {
+                    cs_red_or(cs_mapa(&acc[j >> 5], 0), 1u << (j & 31));
+                    if (inter < qs) cs_red_max(st_g_remote, j);
+                }
+            }
+        }
+        cs_cluster_sync();  // acceptances are in CTA 0
+        if (rank == 0) {
+            const int g = st.g;
+            const int lo = g < 0 ? 0 : g;
+            if (warp == 0) {
+                int nn = n, out = st.out, grow_row = -1;
+                if (top >= 0) {
+                    const int chi = top >> 5, clo = lo >> 5;
+                    for (int bw = chi; bw >= clo; bw -= 32) {
+                        const int c = bw - lane;
+                        uint32_t v = 0u;
+                        if (c >= clo) {
+                            v = acc[c];
+                            acc[c] = 0u;  // consumed (bits below lo are re-marked next round)
+                            const int hi_bit = top - (c << 5);
+                            if (hi_bit < 31) v &= (1u << (hi_bit + 1)) - 1u;
+                            const int lo_bit = lo - (c << 5);
+                            if (lo_bit > 0) v &= ~((1u << lo_bit) - 1u);
+                        }
+                        uint32_t live = __ballot_sync(0xffffffffu, v != 0u);
+                        while (live) {
+                            const int l = __ffs(live) - 1;
+                            live &= live - 1u;
+                            uint32_t vv = __shfl_sync(0xffffffffu, v, l);
+                            if (lane == 0) {
+                                const int cc = bw - l;
+                                while (vv) {
+                                    const int b = 31 - __clz(vv);
+                                    vv &= ~(1u << b);
+                                    const int j = (cc << 5) + b;
+                                    const int row = U[j];
+                                    if (j == g) grow_row = row;
+                                    perm[out++] = (IT)row;
+                                    const int moved = U[nn - 1];
+                                    U[j] = moved;
+                                    --nn;
+                                    cs_st32(cs_mapa(&pos[row % R], row / R), (uint32_t)-1);
+                                    if (moved != row)
+                                        cs_st32(cs_mapa(&pos[moved % R], moved / R), (uint32_t)j);
+                                }
+                            }
+                        }
+                    }
+                }
+                if (lane == 0) {
+                    st.g = -1;
+                    if (grow_row >= 0) {
+                        st.top = g - 1;
+                        st.prow = grow_row;
+                        st.pmode = 1;
+                    } else if (nn > 0) {
+                        const int seed = U[nn - 1];
+                        perm[out++] = (IT)seed;
+                        --nn;
+                        cs_st32(cs_mapa(&pos[seed % R], seed / R), (uint32_t)-1);
+                        st.top = nn - 1;
+                        st.prow = seed;
+                        st.pmode = 2;
+                    } else {
+                        st.top = -1;
+                        st.pmode = 0;
+                    }
+                    st.n = nn;
+                    st.out = out;
+                }
+                __syncwarp();
+                const int mode = st.pmode, prow = st.prow;
+                if (mode != 0) {
+                    if (mode == 2)
+                        for (int k = lane; k < nw; k += 32) pl[k] = 0u;
+                    __syncwarp();
+                    const uint32_t owner = (uint32_t)(prow / R);
+                    const int li = prow % R;
+                    const uint32_t e0 = cs_ld32(cs_mapa(&loff[li], owner));
+                    const uint32_t e1 = cs_ld32(cs_mapa(&loff[li + 1], owner));
+                    for (uint32_t e = e0 + lane; e < e1; e += 32) {
+                        const uint32_t c = cs_ld16(cs_mapa(&lq[e], owner));
+                        atomicOr(&pl[c >> 5], 1u << (c & 31));
+                    }
+                    __syncwarp();
+                    int sz = 0;
+                    for (int k = lane; k < nw; k += 32) sz += __popc(pl[k]);
+                    for (int o = 16; o; o >>= 1) sz += __shfl_xor_sync(0xffffffffu, sz, o);
+                    if (lane == 0) st.psz = sz;
+                }
+            } else if (top >= 0) {
+                // acceptance words below lo>>5 were marked for rows that are evaluated again
+                for (int c = tid - 32; c < (lo >> 5); c += CS_THREADS - 32) acc[c] = 0u;
+            }
+        }
+        cs_cluster_sync();  // CTA 0's state, p and the moved rows' positions are published
+    }
+    cs_cluster_sync();  // no CTA leaves while a peer may still read its shared memory
+}
+
 }  // namespace
 
 // Shared memory the bitset kernel needs for M rows of nbc block columns (0 if it cannot run).
@@ -238,6 +494,62 @@ bool cluster_jaccard_bits(Handle& h, int64_t M, int64_t K, const IT* row_ptr, co
     return true;
 }
 
+// Cluster size and shared memory of the cluster sweep for M rows with the given pattern offsets
+// (qptr on the device); 0 CTAs if it does not fit 8 CTAs.
+template <typename IT>
+bool cluster_jaccard_sweep(Handle& h, int64_t M, int64_t nbc, const int64_t* qptr,
+                           const int32_t* qcol, float tau, IT* perm) {
+    if (M <= 0 || M >= (int64_t(1) << 24) || nbc <= 0 || nbc >= 65536) return false;
+    int optin = 0;
+    XS_CHECK_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, h.device));
+    const int64_t nw = (nbc + 31) / 32;
+    for (int C = 4; C <= 8; C *= 2) {
+        const int64_t R = ceil_div(M, C);  // the last CTAs may own no row
+        std::vector<int64_t> off(C + 1);
+        for (int k = 0; k <= C; ++k) {
+            const int64_t r = std::min<int64_t>((int64_t)k * R, M);
+            XS_CHECK_CUDA(cudaMemcpyAsync(&off[k], qptr + r, sizeof(int64_t),
+                                          cudaMemcpyDeviceToHost, h.stream));
+        }
+        XS_CHECK_CUDA(cudaStreamSynchronize(h.stream));
+        int64_t emax = 1;
+        for (int k = 0; k < C; ++k) emax = std::max<int64_t>(emax, off[k + 1] - off[k]);
+        if (emax >= (int64_t(1) << 31)) return false;
+        const CsLayout L = cs_layout(M, R, nw, emax);
+        if (L.total + sizeof(CsShared) + 1024 > (size_t)optin) continue;
+        auto kern = cluster_sweep_kernel<IT>;
+        XS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)L.total));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)C);
+        cfg.blockDim = dim3(CS_THREADS);
+        cfg.dynamicSmemBytes = L.total;
+        cfg.stream = h.stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)C;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int nclusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg) != cudaSuccess || nclusters < 1) {
+            cudaGetLastError();
+            continue;
+        }
+        const float t_lo = (float)((1.0 - (double)tau) - 1.0 / (double)(1 << 22));
+        XS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, qptr, qcol, (int)M, (int)R, (int)nw,
+                                         (int)emax, tau, t_lo, perm, h.d_err));
+        after_launch(h, "cluster_sweep");
+        return true;
+    }
+    return false;
+}
+
+template bool cluster_jaccard_sweep<int32_t>(Handle&, int64_t, int64_t, const int64_t*,
+                                             const int32_t*, float, int32_t*);
+template bool cluster_jaccard_sweep<int64_t>(Handle&, int64_t, int64_t, const int64_t*,
+                                             const int32_t*, float, int64_t*);
 template bool cluster_jaccard_bits<int32_t>(Handle&, int64_t, int64_t, const int32_t*,
                                             const int32_t*, float, int64_t, int32_t*);
 template bool cluster_jaccard_bits<int64_t>(Handle&, int64_t, int64_t, const int64_t*,

@@ -78,6 +78,11 @@ template <typename IT>
 bool cluster_jaccard_bits(Handle& h, int64_t M, int64_t K, const IT* row_ptr, const IT* col_ind,
                           float tau, int64_t w, IT* perm);
 size_t cluster_bits_smem(int64_t M, int64_t nbc);
+// The same clustering with the row patterns (qptr/qcol: sorted distinct block columns per row)
+// spread over the shared memory of a thread-block cluster of 4 or 8 CTAs; false if they do not fit.
+template <typename IT>
+bool cluster_jaccard_sweep(Handle& h, int64_t M, int64_t nbc, const int64_t* qptr,
+                           const int32_t* qcol, float tau, IT* perm);
 
 // Exact greedy Jaccard clustering (writes perm[M]).
 template <typename IT>
