@@ -184,6 +184,31 @@ def test_tier1_dense_blocks_long_rows(executor):
                      torch.int32, seed=N, long_rows=True)
 
 
+@pytest.mark.parametrize("N", [16, 100, 1024])
+def test_tier1_f32_dense_blocks_long_rows(executor, N):
+    """fp32 blocks, every block present, block rows of 128 blocks: exercises the fp32 kernel
+    with one warp per (block row, column tile) and, for small N, with warps sharing a block row."""
+    P = synth.cfg3_pruned_llm(seed=12, M=192, K=2048, N=8)
+    _tier1_check(executor, P.M, P.K, N, P.row_ptr, P.col_ind, P.values.astype(np.float32),
+                 np.float32, torch.int64, seed=N)
+
+
+def test_tier1_f32_row_map_scatter(executor):
+    M, K, N = 300, 200, 70
+    rp, ci, v = synth.random_csr(M, K, 0.05, seed=10)
+    rng = np.random.default_rng(10)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    perm = rng.permutation(M).astype(np.int32)
+    A = _csr(executor, M, K, rp, ci, v, torch.int32, np.float32)
+    Ab = xs.csr_to_bcsr(executor, A, 16, 16)
+    C = torch.zeros((M, N), dtype=torch.float32, device=executor.device)
+    xs.api._tier1(Ab, torch.as_tensor(B).to(executor.device), C, N,
+                  out_row_map=torch.as_tensor(perm).to(executor.device))
+    brp, bci, bv = oracle.csr_to_bcsr(rp, ci, np.asarray(v, np.float32), M, K)
+    ref = oracle.unpermute_dense(oracle.bcsr_spmm_f64(M, K, N, brp, bci, bv, B), perm)
+    assert errors(ref, _np(C), 1e-5)["max_rel_guarded"] <= 1e-5
+
+
 def test_tier1_row_map_scatter(executor):
     M, K, N = 300, 200, 48
     rp, ci, v = synth.random_csr(M, K, 0.05, seed=9)
