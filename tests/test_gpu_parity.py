@@ -299,3 +299,61 @@ def test_errors(executor):
     # the handle stays usable after reported errors
     xs.spmm(executor, A, B, C, 8)
     executor.synchronize()
+
+
+# ------------------------------------------------------------------------------------------------
+# conversion of block rows with more than 4096 entries (one CTA per block row)
+# ------------------------------------------------------------------------------------------------
+def _long_rows_csr(seed):
+    """A 700 x 5000 matrix whose first rows are dense (block rows of 16 x 5000 entries), with
+    unsorted columns and duplicated (row, col) pairs in some of them, plus ordinary sparse rows."""
+    rng = np.random.default_rng(seed)
+    M, K = 700, 5000
+    rows, cols = [], []
+    for r in range(M):
+        if r < 40 or r % 97 == 0:
+            c = np.arange(K)
+            if r % 3 == 0:
+                c = rng.permutation(c)                        # unsorted
+            if r % 5 == 0:
+                c = np.concatenate([c, rng.integers(0, K, 300)])  # duplicates, later ones win
+        else:
+            c = np.sort(rng.choice(K, 12, replace=False))
+        rows.append(np.full(len(c), r))
+        cols.append(c)
+    rows, cols = np.concatenate(rows), np.concatenate(cols)
+    rp = np.zeros(M + 1, np.int64)
+    np.cumsum(np.bincount(rows, minlength=M), out=rp[1:])
+    v = rng.standard_normal(len(cols)).astype(np.float16)
+    return M, K, rp, cols.astype(np.int64), v
+
+
+@pytest.mark.parametrize("idx", IDX, ids=["i32", "i64"])
+@pytest.mark.parametrize("rb,cb", [(16, 16), (1, 16), (32, 8)])
+def test_conversion_long_block_rows(executor, idx, rb, cb):
+    M, K, rp, ci, v = _long_rows_csr(31)
+    A = _csr(executor, M, K, rp, ci, v, idx)
+    Bm = xs.csr_to_bcsr(executor, A, rb, cb)
+    brp, bci, bv = oracle.csr_to_bcsr(rp, ci, v, M, K, rb, cb)
+    assert np.array_equal(_np(Bm.row_ptr), brp)
+    assert np.array_equal(_np(Bm.col_ind), bci)
+    assert np.array_equal(_np(Bm.values).reshape(-1).view(np.uint16), bv.reshape(-1).view(np.uint16))
+
+
+def test_conversion_long_rows_checkers_and_clustering(executor, cluster_kernel):
+    from xspmm_b200 import generators as gen
+    rp, ci, v = gen.checkers(600, 9000, 16, dtype=np.float16)   # rows of 4500 entries
+    rp, ci, v, _ = gen.shuffle_rows(rp, ci, v, seed=2)
+    A = _csr(executor, 600, 9000, rp, ci, v, torch.int32)
+    Bm = xs.csr_to_bcsr(executor, A, 16, 16)
+    brp, bci, bv = oracle.csr_to_bcsr(rp, ci, v, 600, 9000)
+    assert np.array_equal(_np(Bm.row_ptr), brp) and np.array_equal(_np(Bm.col_ind), bci)
+    assert np.array_equal(_np(Bm.values).reshape(-1).view(np.uint16), bv.reshape(-1).view(np.uint16))
+    perm = torch.zeros(600, dtype=torch.int32, device=executor.device)
+    try:
+        xs.compute_1d_jaccard_clustering(executor, A, 0.5, 1, perm)  # w = 1: 9000 block columns
+    except xs.XSpMMError as e:
+        if cluster_kernel != "auto" and e.status == 2:
+            pytest.skip(str(e))
+        raise
+    assert np.array_equal(_np(perm), oracle.cluster_fast(rp, ci, 600, 9000, 0.5, 1))

@@ -25,6 +25,7 @@ namespace xspmm_b200 {
 namespace {
 
 constexpr int CV_WARPS = 8;
+constexpr int64_t CV_LONG = 4096;  // entries above which a block row gets a CTA of its own
 
 // Validates row_ptr over [r0, r1]; returns false (and flags) when it is malformed.
 template <typename IT>
@@ -46,7 +47,8 @@ template <typename IT>
 __global__ void __launch_bounds__(CV_WARPS * 32)
 bcsr_count_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, int64_t M, int64_t K,
                   int64_t nnz, int64_t nbr, int64_t rb, BlockDiv bd, IT* __restrict__ counts,
-                  unsigned* err) {
+                  int64_t* __restrict__ long_list, unsigned* __restrict__ long_n,
+                  unsigned long_cap, unsigned* err) {
     __shared__ uint32_t win_all[CV_WARPS][WIN_WORDS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint32_t* win = win_all[warp];
@@ -58,6 +60,14 @@ bcsr_count_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, int64_t 
             continue;
         }
         const int64_t e0 = rp[r0], e1 = rp[r1];
+        if (long_list && e1 - e0 > CV_LONG) {  // a CTA of its own counts it (below)
+            if (lane == 0) {
+                const unsigned k = atomicAdd(long_n, 1u);
+                if (k < long_cap) long_list[k] = br;
+                else flag_error(err, DERR_INTERNAL);
+            }
+            continue;
+        }
         int64_t lo, hi;
         block_col_range(ci, e0, e1, K, bd, lo, hi, err);
         int64_t count = 0;
@@ -77,7 +87,9 @@ template <typename VT, typename IT>
 __global__ void __launch_bounds__(CV_WARPS * 32)
 bcsr_fill_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const VT* __restrict__ v,
                  int64_t M, int64_t K, int64_t nbr, int64_t rb, int64_t cb, BlockDiv bd,
-                 const IT* __restrict__ brp, IT* __restrict__ bci, VT* __restrict__ bvals) {
+                 const IT* __restrict__ brp, IT* __restrict__ bci, VT* __restrict__ bvals,
+                 int64_t* __restrict__ long_list, unsigned* __restrict__ long_n,
+                 unsigned long_cap) {
     __shared__ uint32_t win_all[CV_WARPS][WIN_WORDS];
     __shared__ uint32_t pre_all[CV_WARPS][WIN_WORDS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -90,6 +102,13 @@ bcsr_fill_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const VT*
         if (nb <= 0) continue;
         const int64_t r0 = br * rb, r1 = min(M, r0 + rb);
         const int64_t e0 = rp[r0], e1 = rp[r1];
+        if (long_list && e1 - e0 > CV_LONG) {  // filled by bcsr_fill_long_kernel (below)
+            if (lane == 0) {
+                const unsigned k = atomicAdd(long_n, 1u);
+                if (k < long_cap) long_list[k] = br;
+            }
+            continue;
+        }
         if (bvals) {  // zero the block row's blocks
             VT* z = bvals + base * bsz;
             const int64_t n = nb * bsz;
@@ -169,10 +188,196 @@ bcsr_fill_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const VT*
     }
 }
 
+// ---- block rows with more than CV_LONG entries: one CTA each ---------------------------------
+// A warp walking tens of thousands of entries (a dense row, the hub rows of a power-law graph,
+// the 16 x 688-block rows of the pruned-LLM config) would serialize the launch; these rows are
+// listed by the count kernel and done by a whole CTA: the window is marked by all threads, its
+// prefix popcount is a CTA scan, and the value scatter gives each warp its own rows.
+constexpr int CL_T = CV_WARPS * 32;
+
+__device__ __forceinline__ int64_t cta_reduce_min(int64_t v, int64_t* red) {
+    v = warp_min64(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int64_t r = red[0];
+    for (int w = 1; w < CV_WARPS; ++w) r = min(r, red[w]);
+    __syncthreads();
+    return r;
+}
+__device__ __forceinline__ int64_t cta_reduce_max(int64_t v, int64_t* red) {
+    v = warp_max64(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int64_t r = red[0];
+    for (int w = 1; w < CV_WARPS; ++w) r = max(r, red[w]);
+    __syncthreads();
+    return r;
+}
+
+// Column-block range of [e0, e1) over the CTA (hi < 0 if empty).
+template <typename IT>
+__device__ void cta_col_range(const IT* ci, int64_t e0, int64_t e1, int64_t K, BlockDiv bd,
+                              int64_t* red, int64_t& lo, int64_t& hi) {
+    int64_t l = INT64_MAX, h = -1;
+    for (int64_t e = e0 + threadIdx.x; e < e1; e += CL_T) {
+        const int64_t c = (int64_t)ci[e];
+        if (c < 0 || c >= K) continue;
+        const int64_t b = bd(c);
+        l = min(l, b);
+        h = max(h, b);
+    }
+    lo = cta_reduce_min(l, red);
+    hi = cta_reduce_max(h, red);
+}
+
+// Marks [wb, wb + WIN_BITS) over the CTA; returns this thread's word population (thread t owns
+// word t) with the exclusive prefix in *pre_out and the window total in *tot_out.
+template <typename IT>
+__device__ void cta_mark(uint32_t* win, const IT* ci, int64_t e0, int64_t e1, int64_t K,
+                         BlockDiv bd, int64_t wb, uint32_t* s_warp, uint32_t* pre_out,
+                         uint32_t* tot_out) {
+    static_assert(CL_T == WIN_WORDS, "one window word per thread");
+    win[threadIdx.x] = 0u;
+    __syncthreads();
+    for (int64_t e = e0 + threadIdx.x; e < e1; e += CL_T) {
+        const int64_t c = (int64_t)ci[e];
+        if (c < 0 || c >= K) continue;
+        const int64_t d = bd(c) - wb;
+        if (d >= 0 && d < WIN_BITS) atomicOr(&win[d >> 5], 1u << (d & 31));
+    }
+    __syncthreads();
+    const uint32_t pc = __popc(win[threadIdx.x]);
+    const uint32_t inc = warp_inclusive_sum(pc);
+    if ((threadIdx.x & 31) == 31) s_warp[threadIdx.x >> 5] = inc;
+    __syncthreads();
+    uint32_t off = 0, tot = 0;
+    for (int w = 0; w < CV_WARPS; ++w) {
+        if (w < (int)(threadIdx.x >> 5)) off += s_warp[w];
+        tot += s_warp[w];
+    }
+    *pre_out = off + inc - pc;
+    *tot_out = tot;
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(CL_T)
+bcsr_count_long_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, int64_t M, int64_t K,
+                       int64_t rb, BlockDiv bd, const int64_t* __restrict__ long_list,
+                       const unsigned* __restrict__ long_n, IT* __restrict__ counts) {
+    __shared__ uint32_t win[WIN_WORDS];
+    __shared__ uint32_t s_warp[CV_WARPS];
+    __shared__ int64_t red[CV_WARPS];
+    const unsigned n = *long_n;
+    for (unsigned i = blockIdx.x; i < n; i += gridDim.x) {
+        const int64_t br = long_list[i];
+        const int64_t r0 = br * rb, r1 = min(M, r0 + rb);
+        const int64_t e0 = rp[r0], e1 = rp[r1];
+        int64_t lo, hi;
+        cta_col_range(ci, e0, e1, K, bd, red, lo, hi);
+        int64_t count = 0;
+        for (int64_t wb = lo; wb <= hi; wb += WIN_BITS) {
+            uint32_t pre, tot;
+            cta_mark(win, ci, e0, e1, K, bd, wb, s_warp, &pre, &tot);
+            count += tot;
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) counts[br] = (IT)count;
+    }
+}
+
+template <typename VT, typename IT>
+__global__ void __launch_bounds__(CL_T)
+bcsr_fill_long_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci,
+                      const VT* __restrict__ v, int64_t M, int64_t K, int64_t rb, int64_t cb,
+                      BlockDiv bd, const IT* __restrict__ brp, IT* __restrict__ bci,
+                      VT* __restrict__ bvals, const int64_t* __restrict__ long_list,
+                      const unsigned* __restrict__ long_n) {
+    __shared__ uint32_t win[WIN_WORDS];
+    __shared__ uint32_t pre_s[WIN_WORDS];
+    __shared__ uint32_t s_warp[CV_WARPS];
+    __shared__ int64_t red[CV_WARPS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t bsz = rb * cb;
+    const unsigned n = *long_n;
+    for (unsigned i = blockIdx.x; i < n; i += gridDim.x) {
+        const int64_t br = long_list[i];
+        const int64_t base = brp[br], nb = (int64_t)brp[br + 1] - base;
+        const int64_t r0 = br * rb, r1 = min(M, r0 + rb);
+        const int64_t e0 = rp[r0], e1 = rp[r1];
+        if (bvals && nb > 0) {  // zero the block row's blocks
+            VT* z = bvals + base * bsz;
+            const int64_t cnt = nb * bsz;
+            const int64_t bytes = cnt * (int64_t)sizeof(VT);
+            if (reinterpret_cast<uintptr_t>(z) % 16 == 0 && bytes % 16 == 0) {
+                uint4* z4 = reinterpret_cast<uint4*>(z);
+                for (int64_t t = threadIdx.x; t < bytes / 16; t += CL_T) z4[t] = make_uint4(0, 0, 0, 0);
+            } else {
+                for (int64_t t = threadIdx.x; t < cnt; t += CL_T) z[t] = VT(0.0f);
+            }
+        }
+        __syncthreads();
+        int64_t lo, hi;
+        cta_col_range(ci, e0, e1, K, bd, red, lo, hi);
+        int64_t rank_base = 0;
+        for (int64_t wb = lo; wb <= hi; wb += WIN_BITS) {
+            uint32_t pre, tot;
+            cta_mark(win, ci, e0, e1, K, bd, wb, s_warp, &pre, &tot);
+            pre_s[threadIdx.x] = pre;
+            {
+                uint32_t x = win[threadIdx.x];
+                int64_t o = base + rank_base + pre;
+                while (x) {
+                    const int b = __ffs(x) - 1;
+                    bci[o++] = (IT)(wb + (int64_t)threadIdx.x * 32 + b);
+                    x &= x - 1;
+                }
+            }
+            __syncthreads();
+            if (bvals) {
+                // warp w scatters rows r0 + w, r0 + w + WARPS, ...: distinct rows never share a
+                // destination; a row whose columns are not strictly increasing is written by one
+                // lane in CSR order, so its last duplicate wins
+                for (int64_t r = r0 + warp; r < r1; r += CV_WARPS) {
+                    const int64_t s0 = rp[r], t0 = rp[r + 1];
+                    bool unsorted = false;
+                    for (int64_t e = s0 + lane; e + 1 < t0; e += 32)
+                        if (ci[e] >= ci[e + 1]) unsorted = true;
+                    unsorted = __any_sync(0xffffffffu, unsorted);
+                    const int64_t roff = (r - r0) * cb;
+                    auto put = [&](int64_t e) {
+                        const int64_t c = (int64_t)ci[e];
+                        if (c < 0 || c >= K) return;
+                        const int64_t b = bd(c);
+                        const int64_t d = b - wb;
+                        if (d < 0 || d >= WIN_BITS) return;
+                        const uint32_t word = win[d >> 5];
+                        const int64_t rank =
+                            rank_base + pre_s[d >> 5] + __popc(word & ((1u << (d & 31)) - 1u));
+                        bvals[(base + rank) * bsz + roff + (c - b * cb)] = v[e];
+                    };
+                    if (!unsorted) {
+                        for (int64_t e = s0 + lane; e < t0; e += 32) put(e);
+                    } else if (lane == 0) {
+                        for (int64_t e = s0; e < t0; ++e) put(e);
+                    }
+                }
+            }
+            rank_base += tot;
+            __syncthreads();
+        }
+    }
+}
+
 unsigned cv_grid(Handle& h, int64_t nbr) {
     const int64_t want = ceil_div(nbr, CV_WARPS);
     const int64_t cap = (int64_t)sm_count(h.device) * 32;
     return (unsigned)std::max<int64_t>(1, std::min(want, cap));
+}
+
+// CTAs for the long block rows: at most one per listed row, at most 4 per SM (a grid-stride loop
+// over the device-side list, whose length the host does not read)
+unsigned cl_grid(Handle& h, int64_t cap) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(cap, (int64_t)sm_count(h.device) * 4));
 }
 
 }  // namespace
@@ -185,23 +390,49 @@ int64_t csr_to_bcsr_count(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT
         XS_CHECK_CUDA(cudaMemsetAsync(brp, 0, sizeof(IT), h.stream));
         return 0;
     }
+    // block rows above CV_LONG entries are listed by the warp kernel and counted by CTAs
+    const bool may_be_long = nnz > CV_LONG;
+    const int64_t cap = std::max<int64_t>(1, std::min<int64_t>(nbr, nnz / CV_LONG + 1));
+    DevBuf<int64_t> long_list(may_be_long ? cap : 0, h.stream);
+    DevBuf<unsigned> long_n(may_be_long ? 1 : 0, h.stream);
+    if (may_be_long) XS_CHECK_CUDA(cudaMemsetAsync(long_n.get(), 0, sizeof(unsigned), h.stream));
     bcsr_count_kernel<IT><<<cv_grid(h, nbr), CV_WARPS * 32, 0, h.stream>>>(
-        row_ptr, col_ind, M, K, nnz, nbr, rb, make_div(cb), brp, h.d_err);
+        row_ptr, col_ind, M, K, nnz, nbr, rb, make_div(cb), brp, long_list.get(), long_n.get(),
+        (unsigned)cap, h.d_err);
     after_launch(h, "bcsr_count");
+    if (may_be_long) {
+        bcsr_count_long_kernel<IT><<<cl_grid(h, cap), CL_T, 0, h.stream>>>(
+            row_ptr, col_ind, M, K, rb, make_div(cb), long_list.get(), long_n.get(), brp);
+        after_launch(h, "bcsr_count_long");
+    }
     exclusive_scan<IT>(h, brp, brp, nbr);
     throw_on_device_errors(h, "csr_to_bcsr");
     return (int64_t)read_scalar<IT>(h, brp + nbr);
 }
 
 template <typename VT, typename IT>
-void csr_to_bcsr_fill(Handle& h, int64_t M, int64_t K, int64_t, const IT* row_ptr,
+void csr_to_bcsr_fill(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
                       const IT* col_ind, const VT* values, int64_t rb, int64_t cb, const IT* brp,
                       IT* bci, VT* bvals) {
     const int64_t nbr = ceil_div(M, rb);
     if (nbr == 0) return;
+    // block rows above CV_LONG entries (the same ones the count listed; row_ptr was validated
+    // there) are listed by the warp kernel and filled by CTAs
+    const bool may_be_long = nnz > CV_LONG;
+    const int64_t cap = std::max<int64_t>(1, std::min<int64_t>(nbr, nnz / CV_LONG + 1));
+    DevBuf<int64_t> long_list(may_be_long ? cap : 0, h.stream);
+    DevBuf<unsigned> long_n(may_be_long ? 1 : 0, h.stream);
+    if (may_be_long) XS_CHECK_CUDA(cudaMemsetAsync(long_n.get(), 0, sizeof(unsigned), h.stream));
     bcsr_fill_kernel<VT, IT><<<cv_grid(h, nbr), CV_WARPS * 32, 0, h.stream>>>(
-        row_ptr, col_ind, values, M, K, nbr, rb, cb, make_div(cb), brp, bci, bvals);
+        row_ptr, col_ind, values, M, K, nbr, rb, cb, make_div(cb), brp, bci, bvals,
+        long_list.get(), long_n.get(), (unsigned)cap);
     after_launch(h, "bcsr_fill");
+    if (may_be_long) {
+        bcsr_fill_long_kernel<VT, IT><<<cl_grid(h, cap), CL_T, 0, h.stream>>>(
+            row_ptr, col_ind, values, M, K, rb, cb, make_div(cb), brp, bci, bvals,
+            long_list.get(), long_n.get());
+        after_launch(h, "bcsr_fill_long");
+    }
 }
 
 template int64_t csr_to_bcsr_count<int32_t>(Handle&, int64_t, int64_t, int64_t, const int32_t*,
