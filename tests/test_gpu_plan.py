@@ -198,3 +198,80 @@ def test_plan_power_law_rows(executor):
         plan.execute(torch.as_tensor(P.B).to(executor.device), C, P.N)
         ref, emu = _oracle_tier2(P, P.B, False)
         _close(ref, emu, C.cpu().numpy())
+
+
+def _mixed_problem(seed, M=4000, K=6000):
+    """Rows 0..399 in 16x16 blocks filled to 50 % (20 block columns per block row), rows 400..
+    ultra-sparse (2 nonzeros), with a hub row of 2000 nonzeros every 151 rows; fp16 values. The
+    block grid stays below the density at which a plan takes the tcgen05 kernel, so the mma.sync
+    and gather kernels share it."""
+    rng = np.random.default_rng(seed)
+    nbc = (K + 15) // 16
+    rows, cols = [], []
+    bcs = None
+    for r in range(M):
+        if r < 400:
+            if r % 16 == 0:
+                bcs = rng.choice(nbc - 1, 20, replace=False)
+            c = np.sort(np.concatenate([bc * 16 + rng.choice(16, 8, replace=False) for bc in bcs]))
+        elif r % 151 == 0:
+            c = np.sort(rng.choice(K, 2000, replace=False))
+        else:
+            c = np.sort(rng.choice(K, 2, replace=False))
+        rows.append(np.full(len(c), r))
+        cols.append(c)
+    rows, cols = np.concatenate(rows), np.concatenate(cols)
+    rp = np.zeros(M + 1, np.int64)
+    np.cumsum(np.bincount(rows, minlength=M), out=rp[1:])
+    v = rng.standard_normal(len(cols)).astype(np.float16)
+    return synth.Problem("mixed", M, K, 8, rp, cols.astype(np.int64), v, None)
+
+
+@pytest.mark.parametrize("N,clustering", [(64, False), (130, True), (256, False), (37, True)])
+def test_plan_sparse_block_rows(executor, N, clustering):
+    """Block rows of nearly empty blocks run on the gather kernels (spmm_sparse.cu), the rest on
+    the mma.sync block kernel; C must match the oracle and be the same bits on every run."""
+    P = _mixed_problem(40 + N)
+    B = np.random.default_rng(N).standard_normal((P.K, N)).astype(np.float16)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int32 if N % 2 else torch.int64)
+    with xs.SpMMPlan(executor, A, 16, clustering) as plan:
+        Bd = torch.as_tensor(B).to(executor.device)
+        C1 = torch.full((P.M, N), float("nan"), device=executor.device)
+        C2 = torch.full((P.M, N), float("nan"), device=executor.device)
+        plan.execute(Bd, C1, N)
+        plan.execute(Bd, C2, N)
+        assert torch.equal(C1, C2)
+        ref, emu = _oracle_tier2(P, B, clustering)
+        got = C1.cpu().numpy()
+        _close(ref[:400], emu[:400], got[:400])  # dense rows: the block kernel
+        if not clustering:
+            # 2-nonzero and hub rows: the gather kernels, fp64 accumulation rounded once
+            e = errors(ref[400:], got[400:], 1e-5)
+            assert e["max_rel_guarded"] <= 1e-5, e
+        else:
+            _close(ref[400:], emu[400:], got[400:])
+        assert plan.info()["device_bytes"] > 0
+
+
+def test_plan_all_sparse_and_forced_block_kernel_agree(executor):
+    """An R-MAT matrix whose block rows all take the gather path, against the same plan forced
+    onto the block kernel: both within the tolerance of the oracle."""
+    P = synth.cfg5_rmat(seed=5, scale=12, N=128)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int32)
+    ref, emu = _oracle_tier2(P, P.B, False)
+    Bd = torch.as_tensor(P.B).to(executor.device)
+    outs = []
+    for kind in ("auto", "mma"):
+        executor.set_tier1_kernel(kind)
+        try:
+            with xs.SpMMPlan(executor, A, 16, False) as plan:
+                C = torch.full((P.M, P.N), float("nan"), device=executor.device)
+                plan.execute(Bd, C, P.N)
+                outs.append(C.cpu().numpy())
+        finally:
+            executor.set_tier1_kernel("auto")
+        _close(ref, emu, outs[-1])
+    # fp64 accumulation on the gather path is at least as close to the fp64 oracle
+    assert errors(ref, outs[0], 1e-3)["max_abs"] <= errors(ref, outs[1], 1e-3)["max_abs"] * 1.01 + 1e-7

@@ -6,6 +6,7 @@
 #include "common.cuh"
 
 #include <new>
+#include <vector>
 
 namespace xspmm_b200 {
 
@@ -54,10 +55,13 @@ struct MmaWork {
     DevBuf<MmaItem> items;
     DevBuf<int32_t> long_rows, first_slot;
     int64_t nitems = 0, nlong = 0, nslots = 0;
+    bool empty = false;  // every block row was left to another kernel: nothing to launch
 };
+// keep (optional, host): block rows to include (1) or leave to another kernel (0).
 template <typename IT>
 void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,
-                    const IT* ci, bool by_first_col, MmaWork& out);
+                    const IT* ci, bool by_first_col, MmaWork& out,
+                    const std::vector<uint8_t>* keep = nullptr);
 template <typename IT>
 void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
                        const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map,
@@ -66,6 +70,31 @@ void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const
 template <typename IT>
 void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT* ci,
                      DevBuf<int32_t>& order);
+
+// Block rows whose blocks are nearly empty, taken off the block kernels by a plan: their
+// nonzeros extracted per row in column order (spmm_sparse.cu) and multiplied by gathering one B
+// row per nonzero. dense_br (host) marks the block rows that stay on the block kernels.
+constexpr int64_t SP_DENSE_NNZ = 12;  // nonzeros per block (of 256) above which a block row stays
+struct SparseChunk {
+    int64_t e0, e1;  // nonzeros [e0, e1) of row `row`, partial sum into workspace slot `slot`
+    int32_t row, slot;
+};
+struct SparseRows {
+    std::vector<uint8_t> dense_br;
+    DevBuf<int64_t> rptr;  // [M+1]: row r's nonzeros are [rptr[r], rptr[r+1]) (empty if dense)
+    DevBuf<int32_t> col;
+    DevBuf<__half> val;
+    DevBuf<int32_t> brs, short_rows, long_rows;
+    DevBuf<SparseChunk> chunks;    // long rows cut into chunks
+    DevBuf<int32_t> long_first;    // [nlong+1] first chunk of each long row
+    int64_t nbrs = 0, nnz = 0, nshort = 0, nlong = 0, nchunks = 0;
+};
+template <typename IT>
+void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT* ci,
+                       const __half* v, SparseRows& out);
+template <typename IT>
+void sparse_rows_execute(Handle& h, const SparseRows& sp, const __half* B, float* C, int64_t M,
+                         int64_t K, int64_t N, const IT* map);
 
 // Which Tier-1 fp16 kernel runs: the handle's setting (xspmm_set_tier1_kernel) if not auto, else
 // the environment XSPMM_TIER1_KERNEL = mma | tc | auto (default auto).

@@ -120,13 +120,26 @@ void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
         // A single product of a small matrix does not repay building the list (one host
         // round trip); a large one does (long rows would serialize on one CTA).
         const bool want_work = !one_shot || nnzb >= (int64_t(1) << 18);
+        // Block rows of nearly empty blocks go to the gather kernels (spmm_sparse.cu); the
+        // split is decided once per plan from the block values.
+        if (want_work && nbr > 0 && !sparse_built && tier1_kernel_choice(h) == Tier1Kernel::Auto &&
+            reinterpret_cast<uintptr_t>(v) % 16 == 0) {
+            sparse_rows_build<IT>(h, nbr, M, rp, ci, v, sparse);
+            sparse_built = true;
+            work_built = false;  // the work list must leave those rows out
+        }
+        const bool split = sparse_built && sparse.nbrs > 0;
         if (want_work && nbr > 0 && (!work_built || (big_b && !work_sorted))) {
             work = MmaWork();
-            mma_work_build<IT>(h, nbr, nbc, nnzb, rp, ci, big_b, work);
+            mma_work_build<IT>(h, nbr, nbc, nnzb, rp, ci, big_b, work,
+                               split ? &sparse.dense_br : nullptr);
             work_built = true;
             work_sorted = big_b;
         }
-        bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map, work_built ? &work : nullptr);
+        if (!(split && work.empty))
+            bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map,
+                                  work_built ? &work : nullptr);
+        if (split) sparse_rows_execute<IT>(h, sparse, B, C, M, K, N, map);
     } else {
         bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
     }

@@ -41,6 +41,8 @@ struct Plan final : PlanBase {
     bool tc_built = false;
     MmaWork work;  // work list of the mma.sync kernel (order, split long rows)
     bool work_built = false;
+    SparseRows sparse;  // block rows of nearly empty blocks, on the gather kernels
+    bool sparse_built = false;
     bool work_sorted = false;
     bool one_shot = false;  // built for a single product (the Tier-2 call)
 
@@ -53,6 +55,11 @@ struct Plan final : PlanBase {
                (int64_t)work.items.n * (int64_t)sizeof(MmaItem) +
                (int64_t)(work.long_rows.n + work.first_slot.n) * (int64_t)sizeof(int32_t) +
                (int64_t)bv.n * (int64_t)sizeof(VT) +
+               (int64_t)(sparse.rptr.n * sizeof(int64_t) + sparse.col.n * sizeof(int32_t) +
+                         sparse.val.n * sizeof(__half) +
+                         (sparse.brs.n + sparse.short_rows.n + sparse.long_rows.n +
+                          sparse.long_first.n) * sizeof(int32_t) +
+                         sparse.chunks.n * sizeof(SparseChunk)) +
                (int64_t)(tc.gptr.n * sizeof(int64_t) + tc.gcol.n * sizeof(int32_t) +
                          tc.apk.n * sizeof(__half));
     }
@@ -62,6 +69,9 @@ struct Plan final : PlanBase {
         work.long_rows.s = s;
         work.first_slot.s = s;
         bv.s = s;
+        sparse.rptr.s = sparse.col.s = sparse.val.s = s;
+        sparse.brs.s = sparse.short_rows.s = sparse.long_rows.s = sparse.long_first.s = s;
+        sparse.chunks.s = s;
         tc.gptr.s = s;
         tc.gcol.s = s;
         tc.apk.s = s;

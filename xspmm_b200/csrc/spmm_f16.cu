@@ -404,7 +404,8 @@ void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT
 }
 template <typename IT>
 void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,
-                    const IT* ci, bool by_first_col, MmaWork& out) {
+                    const IT* ci, bool by_first_col, MmaWork& out,
+                    const std::vector<uint8_t>* keep) {
     cudaStream_t s = h.stream;
     std::vector<int32_t> order(nbr);
     if (by_first_col) {
@@ -426,8 +427,13 @@ void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT*
     std::vector<int32_t> long_rows, first_slot;
     items.reserve(nbr);
     int32_t slot = 0;
+    bool dropped = false;  // block rows left to another kernel (keep[r] == 0)
     for (int64_t t = 0; t < nbr; ++t) {
         const int32_t r = order[t];
+        if (keep && !(*keep)[r]) {
+            dropped = true;
+            continue;
+        }
         const int64_t j0 = (int64_t)hrp[r], len = (int64_t)hrp[r + 1] - j0;
         if (len <= chunk) {
             items.push_back(MmaItem{j0, r, (int32_t)len, -1, 0});
@@ -439,10 +445,11 @@ void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT*
             items.push_back(MmaItem{j0 + o, r, (int32_t)std::min(chunk, len - o), slot++, 0});
     }
     first_slot.push_back(slot);
-    if (long_rows.empty() && !by_first_col) {  // the natural order, nothing to cut: no list
+    if (long_rows.empty() && !by_first_col && !dropped) {  // every row, natural order: no list
         out.nitems = 0;
         return;
     }
+    out.empty = items.empty();
     XS_REQUIRE(items.size() < (size_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "too many work items");
     out.nitems = (int64_t)items.size();
     out.nlong = (int64_t)long_rows.size();
@@ -463,9 +470,9 @@ void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT*
 template void block_row_order<int32_t>(Handle&, int64_t, int64_t, const int32_t*, const int32_t*,
                                        DevBuf<int32_t>&);
 template void mma_work_build<int32_t>(Handle&, int64_t, int64_t, int64_t, const int32_t*,
-                                      const int32_t*, bool, MmaWork&);
+                                      const int32_t*, bool, MmaWork&, const std::vector<uint8_t>*);
 template void mma_work_build<int64_t>(Handle&, int64_t, int64_t, int64_t, const int64_t*,
-                                      const int64_t*, bool, MmaWork&);
+                                      const int64_t*, bool, MmaWork&, const std::vector<uint8_t>*);
 template void block_row_order<int64_t>(Handle&, int64_t, int64_t, const int64_t*, const int64_t*,
                                        DevBuf<int32_t>&);
 
