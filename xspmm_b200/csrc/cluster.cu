@@ -472,7 +472,51 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                 }
                 __syncthreads();
                 const int nr = sh.nr;  // <= ncand0 <= CL_THREADS
-                if (tid < nr) {        // decreasing position order, ranked by counting
+                if (nr <= 32) {
+                    // The common case, in warp 0 alone: lane j holds acceptance j; its rank (by
+                    // decreasing position) comes from 32 shuffles, and the holes at positions
+                    // >= n-nr -- the only ones the chase of fact 4 can meet -- are looked up in a
+                    // table of their ranks instead of rescanning the acceptances.
+                    if (warp == 0) {
+                        const uint64_t kv = lane < nr ? sh.sortbuf[lane] : 0ull;
+                        int rank = 0;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const uint64_t kj = __shfl_sync(0xffffffffu, kv, j);
+                            rank += (j < nr && kj > kv) ? 1 : 0;
+                        }
+                        const int rr = (int)(uint32_t)kv, pp = (int)(kv >> 32);
+                        const int hbase = n - nr;  // holes at or above it are table entries
+                        if (lane < nr) sh.holes[lane] = -1;
+                        __syncwarp();
+                        if (lane < nr && pp >= hbase) sh.holes[pp - hbase] = rank;
+                        __syncwarp();
+                        if (lane < nr) {
+                            if (out0 + 1 + rank < a.M) {
+                                a.perm[out0 + 1 + rank] = rr;
+                                st.set_p(rr, -1);
+                            } else {
+                                flag_error(a.err, DERR_INTERNAL);
+                            }
+                            if (pp < hbase) {  // hole h_rank receives U[chase(n-1-rank)]
+                                int x = n - 1 - rank, steps = 0;
+                                while (x >= hbase && steps <= nr) {
+                                    const int hr = sh.holes[x - hbase];
+                                    if (hr < 0) break;
+                                    x = n - 1 - hr;
+                                    ++steps;
+                                }
+                                if (steps > nr || x >= n) {
+                                    flag_error(a.err, DERR_INTERNAL);
+                                } else {
+                                    const int mv = st.u(x);
+                                    st.set_u(pp, mv);
+                                    st.set_p(mv, pp);
+                                }
+                            }
+                        }
+                    }
+                } else if (tid < nr) {  // decreasing position order, ranked by counting
                     const uint64_t kv = sh.sortbuf[tid];
                     int rank = 0;
                     for (int j = 0; j < nr; ++j) rank += sh.sortbuf[j] > kv;
