@@ -61,6 +61,9 @@ constexpr int NCLS = 32;            // size classes per block column in the inve
 constexpr int SORT_CAP = 1024;      // settled acceptances kept in shared memory (uint64 keys)
 constexpr int CAND_CAP = 1024;      // candidates kept in shared memory (the rest in global)
 constexpr int HOLE_CAP = 1024;      // holes of a pass kept in shared memory (the rest in global)
+constexpr int FAST_PER = 4;         // candidates per thread the fast path evaluates
+static_assert(FAST_PER * CL_THREADS <= CAND_CAP && FAST_PER * CL_THREADS <= SORT_CAP,
+              "fast-path candidates stay in shared memory");
 constexpr int SMEM_ROWS = 20480;    // U and pos live in shared memory up to this many rows
 constexpr int64_t HEAVY = 2048;     // inverted lists longer than this are walked by size window
 constexpr int LIGHT_MASK = (1 << 30) - 1;
@@ -446,7 +449,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
         }
         __syncthreads();
 
-        // Fast path for the common pass: at most CL_THREADS candidates, no heavy column and no
+        // Fast path for the common pass: at most FAST_PER*CL_THREADS candidates, no heavy column and no
         // accepted row that adds columns to p. Then every candidate is decided against the seed's
         // pattern alone and nothing depends on the order of the decisions: evaluate, rank the
         // accepted rows by position, done -- a handful of barriers instead of the general round
@@ -455,23 +458,37 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
         bool fast_done = false;
         {
             const int ncand0 = sh.ncand;
-            const bool fast = slen > 0 && ncand0 <= CL_THREADS && sh.nheavy == 0;
-            int r = -1, len = 0, pr = -1, acc = 0, grow = 0;
-            if (fast && tid < ncand0) {
-                cand_get(sh, a, 0, tid, r, len, pr);
-                const int64_t inter = st.cnt_light(r);
-                acc = jaccard_distance(inter, slen + (int64_t)len - inter) <= a.tau ? 1 : 0;
-                grow = acc && len > inter;
+            // up to FAST_PER candidates per thread (the candidate buffer holds CAND_CAP)
+            const bool fast = slen > 0 && ncand0 <= FAST_PER * CL_THREADS && sh.nheavy == 0;
+            int rq[FAST_PER], prq[FAST_PER], accq[FAST_PER];
+            int grow = 0;
+#pragma unroll
+            for (int q = 0; q < FAST_PER; ++q) {
+                rq[q] = -1;
+                prq[q] = -1;
+                accq[q] = 0;
+                const int c = tid + q * CL_THREADS;
+                if (fast && c < ncand0) {
+                    int len = 0;
+                    cand_get(sh, a, 0, c, rq[q], len, prq[q]);
+                    const int64_t inter = st.cnt_light(rq[q]);
+                    accq[q] =
+                        jaccard_distance(inter, slen + (int64_t)len - inter) <= a.tau ? 1 : 0;
+                    grow |= accq[q] && len > inter;
+                }
             }
             const int any_grow = __syncthreads_or(grow);
             if (fast && !any_grow) {
-                if (tid < ncand0) {
-                    st.cnt_clear(r);
-                    if (acc) sh.sortbuf[atomicAdd(&sh.nr, 1)] = ((uint64_t)(uint32_t)pr << 32) |
-                                                                 (uint32_t)r;
+#pragma unroll
+                for (int q = 0; q < FAST_PER; ++q) {
+                    if (rq[q] < 0) continue;
+                    st.cnt_clear(rq[q]);
+                    if (accq[q])
+                        sh.sortbuf[atomicAdd(&sh.nr, 1)] =
+                            ((uint64_t)(uint32_t)prq[q] << 32) | (uint32_t)rq[q];
                 }
                 __syncthreads();
-                const int nr = sh.nr;  // <= ncand0 <= CL_THREADS
+                const int nr = sh.nr;  // <= ncand0 <= SORT_CAP
                 if (nr <= 32) {
                     // The common case, in warp 0 alone: lane j holds acceptance j; its rank (by
                     // decreasing position) comes from 32 shuffles, and the holes at positions
@@ -516,8 +533,9 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             }
                         }
                     }
-                } else if (tid < nr) {  // decreasing position order, ranked by counting
-                    const uint64_t kv = sh.sortbuf[tid];
+                } else {  // decreasing position order, ranked by counting
+                  for (int kq = tid; kq < nr; kq += CL_THREADS) {
+                    const uint64_t kv = sh.sortbuf[kq];
                     int rank = 0;
                     for (int j = 0; j < nr; ++j) rank += sh.sortbuf[j] > kv;
                     const int rr = (int)(uint32_t)kv, pp = (int)(kv >> 32);
@@ -552,6 +570,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             st.set_p(mv, pp);
                         }
                     }
+                  }
                 }
                 if (tid == 0) {
                     sh.seed = seed;
