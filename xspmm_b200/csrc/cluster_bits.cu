@@ -46,9 +46,11 @@ struct CbShared {
     int prow;   // row whose pattern joins p (pmode 1) or becomes p (pmode 2)
     int pmode;  // 0: p unchanged, 1: p |= q_prow, 2: p = q_prow (new seed)
     int psz;    // |p|
+    int kacc;   // acceptances marked this round (an upper bound of the round's final ones)
 };
 
-// smem: bits[M * ns] | qsz[M] (uint16) | U[M] | acc[ceil(M/32)] | p[nw]. A row's bitset takes
+// smem: bits[M * ns] | qsz[M] (uint16) | U[M] | acc[ceil(M/32)] | wpre[ceil(M/32)] | p[nw]. A
+// row's bitset takes
 // ns = nw | 1 words: with an odd stride the rows that a warp reads at once fall on different
 // banks.
 template <typename IT>
@@ -65,7 +67,8 @@ cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_i
     int32_t* U = reinterpret_cast<int32_t*>(
         cb_smem + (((size_t)M * ns * 4 + (size_t)M * 2 + 15) & ~size_t(15)));
     uint32_t* acc = reinterpret_cast<uint32_t*>(U + M);
-    uint32_t* p = acc + nmw;
+    int* wpre = reinterpret_cast<int*>(acc + nmw);  // acceptances above each word, this round
+    uint32_t* p = reinterpret_cast<uint32_t*>(wpre + nmw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     // ---- row bitsets from the CSR (block column = col / w) ----
@@ -79,6 +82,7 @@ cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_i
         st.prow = -1;
         st.pmode = 0;
         st.psz = 0;
+        st.kacc = 0;
     }
     __syncthreads();
     for (int r = warp; r < M; r += CB_WARPS) {
@@ -113,7 +117,7 @@ cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_i
         if (top < 0 && n <= 0) break;
         if (top >= 0) {
             // warp w evaluates positions [32c, 32c + 32) for c = w, w + WARPS, ...
-            int gmax = -1;
+            int gmax = -1, kw = 0;
             for (int c = warp; c <= (top >> 5); c += CB_WARPS) {
                 const int j = (c << 5) + lane;
                 bool a = false, gr = false;
@@ -129,18 +133,20 @@ cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_i
                 const uint32_t av = __ballot_sync(0xffffffffu, a);
                 const uint32_t gv = __ballot_sync(0xffffffffu, gr);
                 if (lane == 0) acc[c] = av;
+                kw += __popc(av);
                 if (gv) gmax = max(gmax, (c << 5) + 31 - __clz(gv));
             }
             if (lane == 0 && gmax >= 0) atomicMax(&st.g, gmax);
+            if (lane == 0 && kw) atomicAdd(&st.kacc, kw);
         }
         __syncthreads();
         if (warp == 0) {
             const int g = st.g;
-            int nn = n, out = st.out, grow_row = -1;
-            if (top >= 0) {
-                // the round's acceptances in decreasing position, (g, top] then g, replayed as
-                // the reference removes them: perm += U[j]; U[j] = U.back(); pop. The warp finds
-                // the nonzero acceptance words 32 at a time; lane 0 replays their bits.
+            int nn = n, out = st.out;
+            const int kacc = st.kacc;
+            if (top >= 0 && kacc > 0 && kacc <= 8) {
+                // few acceptances: lane 0 replays them as the reference removes them
+                // (perm += U[j]; U[j] = U.back(); pop), in decreasing position
                 const int lo = g < 0 ? 0 : g;
                 const int chi = top >> 5, clo = lo >> 5;
                 for (int base = chi; base >= clo; base -= 32) {
@@ -148,9 +154,9 @@ cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_i
                     uint32_t v = 0u;
                     if (c >= clo) {
                         v = acc[c];
-                        const int hi_bit = top - (c << 5);  // bits above it are past top
+                        const int hi_bit = top - (c << 5);
                         if (hi_bit < 31) v &= (1u << (hi_bit + 1)) - 1u;
-                        const int lo_bit = lo - (c << 5);   // bits below it wait for next round
+                        const int lo_bit = lo - (c << 5);
                         if (lo_bit > 0) v &= ~((1u << lo_bit) - 1u);
                     }
                     uint32_t live = __ballot_sync(0xffffffffu, v != 0u);
@@ -165,7 +171,7 @@ cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_i
                                 vv &= ~(1u << b);
                                 const int j = (cc << 5) + b;
                                 const int row = U[j];
-                                if (j == g) grow_row = row;
+                                if (j == g) st.prow = row;
                                 perm[out++] = (IT)row;
                                 U[j] = U[nn - 1];
                                 --nn;
@@ -173,9 +179,81 @@ cluster_bits_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_i
                         }
                     }
                 }
+                nn = __shfl_sync(0xffffffffu, nn, 0);
+                out = __shfl_sync(0xffffffffu, out, 0);
+                __syncwarp();
+            } else if (top >= 0 && kacc > 8) {
+                // The round's acceptances, (g, top] then g, in decreasing position, replayed as
+                // the reference removes them (perm += U[j]; U[j] = U.back(); pop), in parallel:
+                // the t-th acceptance goes to perm[out + t], and a hole h_t below n - k receives
+                // U[chase(n - 1 - t)] (fact 4 of cluster.cu), chase stepping from x to
+                // n - 1 - rank(x) while x is a hole of this round. rank() comes from per-word
+                // prefix counts of the acceptance bitmap; the reads (positions >= n - k) and the
+                // writes (holes < n - k) never meet.
+                const int lo = g < 0 ? 0 : g;
+                const int chi = top >> 5, clo = lo >> 5;
+                auto masked = [&](int c) {
+                    uint32_t v = acc[c];
+                    const int hi_bit = top - (c << 5);  // bits above it are past top
+                    if (hi_bit < 31) v &= (1u << (hi_bit + 1)) - 1u;
+                    const int lo_bit = lo - (c << 5);   // bits below it wait for next round
+                    if (lo_bit > 0) v &= ~((1u << lo_bit) - 1u);
+                    return v;
+                };
+                int run = 0;  // acceptances in the words above the current chunk
+                for (int base = chi; base >= clo; base -= 32) {
+                    const int c = base - lane;
+                    const int pc = c >= clo ? __popc(masked(c)) : 0;
+                    int incl = pc;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                        if (lane >= o) incl += t;
+                    }
+                    if (c >= clo) wpre[c] = run + incl - pc;
+                    run += __shfl_sync(0xffffffffu, incl, 31);
+                }
+                const int k = run;
+                __syncwarp();
+                auto rank_of = [&](int x) {  // acceptances above position x (x accepted)
+                    const int c = x >> 5;
+                    return wpre[c] + __popc(masked(c) & ~((2u << (x & 31)) - 1u));
+                };
+                auto is_hole = [&](int x) {
+                    return x >= lo && x <= top && ((masked(x >> 5) >> (x & 31)) & 1u);
+                };
+                for (int base = chi; base >= clo; base -= 32) {
+                    const int c = base - lane;
+                    if (c < clo) continue;
+                    uint32_t v = masked(c);
+                    int t = wpre[c];
+                    while (v) {
+                        const int b = 31 - __clz(v);
+                        v &= ~(1u << b);
+                        const int j = (c << 5) + b;
+                        const int row = U[j];
+                        if (j == g) st.prow = row;  // joins p below
+                        perm[out + t] = (IT)row;
+                        if (j < n - k) {
+                            int x = n - 1 - t, steps = 0;
+                            while (is_hole(x) && steps <= k) {
+                                x = n - 1 - rank_of(x);
+                                ++steps;
+                            }
+                            if (steps > k) flag_error(err, DERR_INTERNAL);
+                            else U[j] = U[x];
+                        }
+                        ++t;
+                    }
+                }
+                nn = n - k;
+                out += k;
+                __syncwarp();
             }
+            const int grow_row = (top >= 0 && g >= 0) ? st.prow : -1;
             if (lane == 0) {
                 st.g = -1;
+                st.kacc = 0;
                 if (grow_row >= 0) {  // p grows; rows below g are evaluated again
                     st.top = g - 1;
                     st.prow = grow_row;
@@ -474,7 +552,7 @@ size_t cluster_bits_smem(int64_t M, int64_t nbc) {
     const int64_t nw = (nbc + 31) / 32, ns = nw | 1;
     const int64_t nmw = (M + 31) / 32;
     const size_t head = (((size_t)M * ns * 4 + (size_t)M * 2 + 15) & ~size_t(15));
-    return head + (size_t)M * 4 + (size_t)nmw * 4 + (size_t)nw * 4;
+    return head + (size_t)M * 4 + (size_t)nmw * 8 + (size_t)nw * 4;
 }
 
 template <typename IT>
