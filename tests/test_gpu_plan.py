@@ -275,3 +275,55 @@ def test_plan_all_sparse_and_forced_block_kernel_agree(executor):
         _close(ref, emu, outs[-1])
     # fp64 accumulation on the gather path is at least as close to the fp64 oracle
     assert errors(ref, outs[0], 1e-3)["max_abs"] <= errors(ref, outs[1], 1e-3)["max_abs"] * 1.01 + 1e-7
+
+
+def _as_f32(P, seed):
+    v = np.random.default_rng(seed).uniform(-1.0, 1.0, len(P.values)).astype(np.float32)
+    return synth.Problem(P.name, P.M, P.K, P.N, P.row_ptr, P.col_ind, v, None)
+
+
+@pytest.mark.parametrize("N,clustering", [(64, False), (130, True), (33, False)])
+def test_plan_sparse_block_rows_fp32(executor, N, clustering):
+    """fp32 plans split the same way at a higher fill: the 50 %-filled block rows (128 nonzeros
+    per block) stay on the SIMT block kernel, the rest go to the gather kernels. Both accumulate
+    in fp64, so every row meets the fp32 tolerance (1e-5, guarded) against the fp64 oracle, and
+    repeated products are the same bits."""
+    P = _as_f32(_mixed_problem(60 + N), N)
+    B = np.random.default_rng(N).uniform(-1.0, 1.0, (P.K, N)).astype(np.float32)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int64 if N % 2 else torch.int32)
+    with xs.SpMMPlan(executor, A, 16, clustering) as plan:
+        Bd = torch.as_tensor(B).to(executor.device)
+        C1 = torch.full((P.M, N), float("nan"), device=executor.device)
+        C2 = torch.full((P.M, N), float("nan"), device=executor.device)
+        plan.execute(Bd, C1, N)
+        plan.execute(Bd, C2, N)
+        assert torch.equal(C1, C2)
+        ref, _ = _oracle_tier2(P, B, clustering)
+        e = errors(ref, C1.cpu().numpy(), 1e-5)
+        assert e["max_rel_guarded"] <= 1e-5, e
+
+
+def test_plan_fp32_split_matches_block_kernel(executor):
+    """cfg1-shaped fp32 matrix (4096^2, 1 % uniform: ~2.6 nonzeros per block, every block row
+    takes the gather path) through a plan and through the one-shot pipeline, against the plan
+    forced onto the block kernel: all within 1e-5 (guarded) of the fp64 oracle."""
+    P = synth.cfg1_plumbing(seed=3)
+    A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,
+                               index_dtype=torch.int32)
+    ref, _ = _oracle_tier2(P, P.B, False)
+    Bd = torch.as_tensor(P.B).to(executor.device)
+    for kind in ("auto", "mma"):
+        executor.set_tier1_kernel(kind)
+        try:
+            with xs.SpMMPlan(executor, A, 16, False) as plan:
+                C = torch.full((P.M, P.N), float("nan"), device=executor.device)
+                plan.execute(Bd, C, P.N)
+            e = errors(ref, C.cpu().numpy(), 1e-5)
+            assert e["max_rel_guarded"] <= 1e-5, (kind, e)
+        finally:
+            executor.set_tier1_kernel("auto")
+    C = torch.full((P.M, P.N), float("nan"), device=executor.device)
+    xs.spmm(executor, A, Bd, C, P.N, 16, False)
+    e = errors(ref, C.cpu().numpy(), 1e-5)
+    assert e["max_rel_guarded"] <= 1e-5, e

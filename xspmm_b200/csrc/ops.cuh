@@ -74,7 +74,11 @@ void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT
 // Block rows whose blocks are nearly empty, taken off the block kernels by a plan: their
 // nonzeros extracted per row in column order (spmm_sparse.cu) and multiplied by gathering one B
 // row per nonzero. dense_br (host) marks the block rows that stay on the block kernels.
-constexpr int64_t SP_DENSE_NNZ = 12;  // nonzeros per block (of 256) above which a block row stays
+// Nonzeros per block (of 256) above which a block row stays on the block kernels: the fp16
+// tensor-core kernels cost little per block; the fp32 SIMT kernel pays 16 fp64 FMAs per nonzero
+// column of a block, which a gather beats until blocks are about a quarter full.
+constexpr int64_t SP_DENSE_NNZ_F16 = 12;
+constexpr int64_t SP_DENSE_NNZ_F32 = 64;
 struct SparseChunk {
     int64_t e0, e1;  // nonzeros [e0, e1) of row `row`, partial sum into workspace slot `slot`
     int32_t row, slot;
@@ -83,18 +87,24 @@ struct SparseRows {
     std::vector<uint8_t> dense_br;
     DevBuf<int64_t> rptr;  // [M+1]: row r's nonzeros are [rptr[r], rptr[r+1]) (empty if dense)
     DevBuf<int32_t> col;
-    DevBuf<__half> val;
+    DevBuf<uint8_t> val;   // nnz values of the matrix's value type
     DevBuf<int32_t> brs, short_rows, long_rows;
     DevBuf<SparseChunk> chunks;    // long rows cut into chunks
     DevBuf<int32_t> long_first;    // [nlong+1] first chunk of each long row
-    int64_t nbrs = 0, nnz = 0, nshort = 0, nlong = 0, nchunks = 0;
+    DevBuf<int32_t> dense_list;    // [ndense] block rows left on the block kernels, ascending
+    int64_t nbrs = 0, nnz = 0, nshort = 0, nlong = 0, nchunks = 0, ndense = 0;
 };
-template <typename IT>
+template <typename VT, typename IT>
 void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT* ci,
-                       const __half* v, SparseRows& out);
-template <typename IT>
-void sparse_rows_execute(Handle& h, const SparseRows& sp, const __half* B, float* C, int64_t M,
+                       const VT* v, int64_t dense_nnz, SparseRows& out);
+template <typename VT, typename IT>
+void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C, int64_t M,
                          int64_t K, int64_t N, const IT* map);
+// The fp32 block kernel over the listed block rows only (spmm_f32.cu).
+template <typename IT>
+void bcsr_spmm_f32_rows(Handle& h, const int32_t* br_list, int64_t nlist, const IT* rp,
+                        const IT* ci, const float* v, const float* B, float* C, int64_t M,
+                        int64_t K, int64_t N, const IT* map);
 
 // Which Tier-1 fp16 kernel runs: the handle's setting (xspmm_set_tier1_kernel) if not auto, else
 // the environment XSPMM_TIER1_KERNEL = mma | tc | auto (default auto).

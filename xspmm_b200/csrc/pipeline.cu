@@ -124,7 +124,7 @@ void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
         // split is decided once per plan from the block values.
         if (want_work && nbr > 0 && !sparse_built && tier1_kernel_choice(h) == Tier1Kernel::Auto &&
             reinterpret_cast<uintptr_t>(v) % 16 == 0) {
-            sparse_rows_build<IT>(h, nbr, M, rp, ci, v, sparse);
+            sparse_rows_build<VT, IT>(h, nbr, M, rp, ci, v, SP_DENSE_NNZ_F16, sparse);
             sparse_built = true;
             work_built = false;  // the work list must leave those rows out
         }
@@ -139,9 +139,25 @@ void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
         if (!(split && work.empty))
             bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map,
                                   work_built ? &work : nullptr);
-        if (split) sparse_rows_execute<IT>(h, sparse, B, C, M, K, N, map);
+        if (split) sparse_rows_execute<VT, IT>(h, sparse, B, C, M, K, N, map);
     } else {
-        bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
+        // fp32: the same split, at a higher fill (the SIMT block kernel pays per nonzero column
+        // of a block, a gather per nonzero). A single product splits only when the block kernel
+        // would take long against the split's one host round trip.
+        const bool want_split = !one_shot || (double)nnzb * (double)N >= (double)(1 << 22);
+        if (want_split && nbr > 0 && !sparse_built &&
+            tier1_kernel_choice(h) == Tier1Kernel::Auto && reinterpret_cast<uintptr_t>(v) % 16 == 0) {
+            sparse_rows_build<VT, IT>(h, nbr, M, rp, ci, v, SP_DENSE_NNZ_F32, sparse);
+            sparse_built = true;
+        }
+        if (sparse_built && sparse.nbrs > 0) {
+            if (sparse.ndense > 0)
+                bcsr_spmm_f32_rows<IT>(h, sparse.dense_list.get(), sparse.ndense, rp, ci, v, B, C,
+                                       M, K, N, map);
+            sparse_rows_execute<VT, IT>(h, sparse, B, C, M, K, N, map);
+        } else {
+            bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
+        }
     }
 }
 

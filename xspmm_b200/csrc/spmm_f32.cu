@@ -32,16 +32,16 @@ template <typename IT, bool VEC>
 __global__ void __launch_bounds__(F32_WARPS * 32, 4)
 bcsr_spmm_f32_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_ind,
                      const float* __restrict__ vals, const float* __restrict__ B,
-                     float* __restrict__ C, const IT* __restrict__ row_map, int64_t M, int64_t K,
-                     int64_t N, int64_t units, int64_t ntiles, int S,
-                     unsigned* __restrict__ err) {
+                     float* __restrict__ C, const IT* __restrict__ row_map,
+                     const int32_t* __restrict__ br_list, int64_t M, int64_t K, int64_t N,
+                     int64_t units, int64_t ntiles, int S, unsigned* __restrict__ err) {
     __shared__ float As[F32_WARPS][16][16];
     __shared__ double red[F32_WARPS][16][F32_TN];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t unit = (int64_t)blockIdx.x * (F32_WARPS / S) + warp / S;
     const int sub = warp % S;
     const bool active = unit < units;
-    const int64_t br = active ? unit / ntiles : 0;
+    const int64_t br = active ? (br_list ? (int64_t)br_list[unit / ntiles] : unit / ntiles) : 0;
     const int64_t col = (active ? unit % ntiles : 0) * F32_TN + lane;
 
     double acc[16];
@@ -113,10 +113,11 @@ bcsr_spmm_f32_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_
     }
 }
 
+// br_list (device, optional): the block rows to compute, nbr of them; all block rows if null.
 template <typename IT>
-void bcsr_spmm_f32_impl(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const float* v,
-                        const float* B, float* C, int64_t M, int64_t K, int64_t N,
-                        const IT* map) {
+void bcsr_spmm_f32_impl(Handle& h, const int32_t* br_list, int64_t nbr, const IT* rp,
+                        const IT* ci, const float* v, const float* B, float* C, int64_t M,
+                        int64_t K, int64_t N, const IT* map) {
     if (nbr == 0 || N == 0 || M == 0) return;
     const int64_t ntiles = ceil_div(N, F32_TN);
     const int64_t units = nbr * ntiles;
@@ -129,10 +130,10 @@ void bcsr_spmm_f32_impl(Handle& h, int64_t nbr, const IT* rp, const IT* ci, cons
     const bool vec = reinterpret_cast<uintptr_t>(v) % 16 == 0;
     if (vec)
         bcsr_spmm_f32_kernel<IT, true><<<(unsigned)grid, F32_WARPS * 32, 0, h.stream>>>(
-            rp, ci, v, B, C, map, M, K, N, units, ntiles, S, h.d_err);
+            rp, ci, v, B, C, map, br_list, M, K, N, units, ntiles, S, h.d_err);
     else
         bcsr_spmm_f32_kernel<IT, false><<<(unsigned)grid, F32_WARPS * 32, 0, h.stream>>>(
-            rp, ci, v, B, C, map, M, K, N, units, ntiles, S, h.d_err);
+            rp, ci, v, B, C, map, br_list, M, K, N, units, ntiles, S, h.d_err);
     after_launch(h, "bcsr_spmm_f32");
 }
 
@@ -142,13 +143,26 @@ template <>
 void bcsr_spmm<float, int32_t>(Handle& h, int64_t nbr, int64_t, int64_t, const int32_t* rp,
                                const int32_t* ci, const float* v, const float* B, float* C,
                                int64_t M, int64_t K, int64_t N, const int32_t* map) {
-    bcsr_spmm_f32_impl<int32_t>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+    bcsr_spmm_f32_impl<int32_t>(h, nullptr, nbr, rp, ci, v, B, C, M, K, N, map);
 }
 template <>
 void bcsr_spmm<float, int64_t>(Handle& h, int64_t nbr, int64_t, int64_t, const int64_t* rp,
                                const int64_t* ci, const float* v, const float* B, float* C,
                                int64_t M, int64_t K, int64_t N, const int64_t* map) {
-    bcsr_spmm_f32_impl<int64_t>(h, nbr, rp, ci, v, B, C, M, K, N, map);
+    bcsr_spmm_f32_impl<int64_t>(h, nullptr, nbr, rp, ci, v, B, C, M, K, N, map);
 }
+
+template <typename IT>
+void bcsr_spmm_f32_rows(Handle& h, const int32_t* br_list, int64_t nlist, const IT* rp,
+                        const IT* ci, const float* v, const float* B, float* C, int64_t M,
+                        int64_t K, int64_t N, const IT* map) {
+    bcsr_spmm_f32_impl<IT>(h, br_list, nlist, rp, ci, v, B, C, M, K, N, map);
+}
+template void bcsr_spmm_f32_rows<int32_t>(Handle&, const int32_t*, int64_t, const int32_t*,
+                                          const int32_t*, const float*, const float*, float*,
+                                          int64_t, int64_t, int64_t, const int32_t*);
+template void bcsr_spmm_f32_rows<int64_t>(Handle&, const int32_t*, int64_t, const int64_t*,
+                                          const int64_t*, const float*, const float*, float*,
+                                          int64_t, int64_t, int64_t, const int64_t*);
 
 }  // namespace xspmm_b200

@@ -1,19 +1,19 @@
 // spmm_sparse.cu -- Tier-1 for block rows whose 16x16 blocks are nearly empty.
 //
 // The block product (src/common/spmm_math.hpp:59-122) multiplies every 16x16 block as a dense
-// tile: per block it reads the 512-byte block and gathers a 16 x N slab of B. On graph-like
+// tile: per block it reads the block (512 bytes in fp16) and gathers a 16 x N slab of B. On graph-like
 // matrices a block holds one or two nonzeros (R-MAT: ~1.4 of 256, so ~99 % of that traffic and
 // of the tensor work multiplies zeros). A plan therefore splits the block rows once:
-//   * block rows averaging more than SP_DENSE_NNZ nonzeros per block stay on the tensor-core
-//     kernels;
+//   * block rows averaging more than a threshold of nonzeros per block stay on the block kernels
+//     (SP_DENSE_NNZ_F16 for the tensor-core kernels, SP_DENSE_NNZ_F32 for the fp32 SIMT one);
 //   * the others are extracted, row by row, into a compact (column, value) list in column order
 //     (blocks ascending, then the column inside the block) -- the nonzeros of the BCSR values,
 //     read once -- and each product then gathers one B row per nonzero: 6 + 2N bytes per
-//     nonzero instead of 512 + 32N per block.
+//     nonzero instead of 512 + 32N per block in fp16 (8 + 4N against 1024 + 64N in fp32).
 // The result is the same sum, C[16br+i, n] = sum over the row's nonzeros a * B[col, n],
-// accumulated in fp64 in column order and rounded once to fp32 (the block kernels accumulate in
-// fp32). A row of a split block row with no nonzero is written as zeros, as the block product
-// writes it.
+// accumulated in fp64 in column order and rounded once to fp32 (the tensor-core kernels
+// accumulate in fp32; the fp32 SIMT kernel also in fp64, in the same column order). A row of a
+// split block row with no nonzero is written as zeros, as the block product writes it.
 //
 // Kernels: a warp per row and 128-column tile (4 columns per lane) for rows of up to SP_LONG
 // nonzeros; longer rows (hub rows) are cut into chunks of SP_CHUNK nonzeros, a CTA each, whose
@@ -31,12 +31,45 @@ constexpr int SP_WARPS = 8;
 constexpr int64_t SP_LONG = 256;    // rows with more nonzeros are cut into chunks
 constexpr int64_t SP_CHUNK = 2048;  // nonzeros per chunk of a long row
 
-__device__ __forceinline__ int nz_half(uint16_t bits) { return (bits & 0x7FFFu) != 0; }
+// Value-type helpers: 8 consecutive block values of a lane (one 16x16 block row-major: lane l
+// holds row l/2, columns (l&1)*8 .. +7), the nonzero test (the sign bit ignored, so -0 counts as
+// zero), and 4 consecutive elements of a B row as floats.
+template <typename VT> struct SpVT;
+template <> struct SpVT<__half> {
+    __device__ static void load8(const __half* p, __half (&o)[8]) {
+        const uint4 x = *reinterpret_cast<const uint4*>(p);
+        *reinterpret_cast<uint4*>(o) = x;
+    }
+    __device__ static bool nz(__half x) { return (__half_as_ushort(x) & 0x7FFFu) != 0; }
+    __device__ static float f(__half x) { return __half2float(x); }
+    __device__ static void b4(const __half* p, float (&o)[4]) {  // 8-byte aligned
+        const uint2 x = __ldg(reinterpret_cast<const uint2*>(p));
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&x.x));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&x.y));
+        o[0] = f0.x; o[1] = f0.y; o[2] = f1.x; o[3] = f1.y;
+    }
+    static constexpr int b4_align = 8;
+};
+template <> struct SpVT<float> {
+    __device__ static void load8(const float* p, float (&o)[8]) {
+        const float4 x0 = *reinterpret_cast<const float4*>(p);
+        const float4 x1 = *(reinterpret_cast<const float4*>(p) + 1);
+        o[0] = x0.x; o[1] = x0.y; o[2] = x0.z; o[3] = x0.w;
+        o[4] = x1.x; o[5] = x1.y; o[6] = x1.z; o[7] = x1.w;
+    }
+    __device__ static bool nz(float x) { return (__float_as_uint(x) & 0x7FFFFFFFu) != 0; }
+    __device__ static float f(float x) { return x; }
+    __device__ static void b4(const float* p, float (&o)[4]) {  // 16-byte aligned
+        const float4 x = __ldg(reinterpret_cast<const float4*>(p));
+        o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w;
+    }
+    static constexpr int b4_align = 16;
+};
 
 // Per-row nonzero counts (rows of block row br = 16 br .. 16 br + 15), a warp per block row:
 // lane 2i and 2i+1 read row i's two halves of every block (8 halves each).
-template <typename IT>
-__global__ void sp_row_count_kernel(const IT* __restrict__ rp, const __half* __restrict__ v,
+template <typename VT, typename IT>
+__global__ void sp_row_count_kernel(const IT* __restrict__ rp, const VT* __restrict__ v,
                                     int64_t nbr, int64_t M, int32_t* __restrict__ rowcnt) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -45,11 +78,10 @@ __global__ void sp_row_count_kernel(const IT* __restrict__ rp, const __half* __r
         const int64_t j0 = rp[br], j1 = rp[br + 1];
         int c = 0;
         for (int64_t j = j0; j < j1; ++j) {
-            const uint4 x = reinterpret_cast<const uint4*>(v + j * 256)[lane];
-            const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+            VT h[8];
+            SpVT<VT>::load8(v + j * 256 + lane * 8, h);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                c += nz_half((uint16_t)(w[q] & 0xFFFFu)) + nz_half((uint16_t)(w[q] >> 16));
+            for (int q = 0; q < 8; ++q) c += SpVT<VT>::nz(h[q]);
         }
         c += __shfl_xor_sync(0xffffffffu, c, 1);
         const int64_t r = br * 16 + (lane >> 1);
@@ -58,11 +90,11 @@ __global__ void sp_row_count_kernel(const IT* __restrict__ rp, const __half* __r
 }
 
 // Extracts the nonzeros of the listed block rows into rows [rptr[r], rptr[r+1]) in column order.
-template <typename IT>
+template <typename VT, typename IT>
 __global__ void sp_extract_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci,
-                                  const __half* __restrict__ v, const int32_t* __restrict__ brs,
+                                  const VT* __restrict__ v, const int32_t* __restrict__ brs,
                                   int64_t nbrs, int64_t M, const int64_t* __restrict__ rptr,
-                                  int32_t* __restrict__ col, __half* __restrict__ val) {
+                                  int32_t* __restrict__ col, VT* __restrict__ val) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < nbrs;
@@ -73,17 +105,11 @@ __global__ void sp_extract_kernel(const IT* __restrict__ rp, const IT* __restric
         const int64_t j0 = rp[br], j1 = rp[br + 1];
         for (int64_t j = j0; j < j1; ++j) {
             const int64_t bc = (int64_t)ci[j];
-            const uint4 x = reinterpret_cast<const uint4*>(v + j * 256)[lane];
-            const uint32_t w[4] = {x.x, x.y, x.z, x.w};
-            uint16_t h[8];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                h[2 * q] = (uint16_t)(w[q] & 0xFFFFu);
-                h[2 * q + 1] = (uint16_t)(w[q] >> 16);
-            }
+            VT h[8];
+            SpVT<VT>::load8(v + j * 256 + lane * 8, h);
             int c = 0;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) c += nz_half(h[q]);
+            for (int q = 0; q < 8; ++q) c += SpVT<VT>::nz(h[q]);
             const int c_lo = __shfl_sync(0xffffffffu, c, lane & ~1);  // the row's first half
             const int c_all = c_lo + __shfl_sync(0xffffffffu, c, lane | 1);
             if (r < M) {
@@ -91,9 +117,9 @@ __global__ void sp_extract_kernel(const IT* __restrict__ rp, const IT* __restric
                 const int k0 = (lane & 1) * 8;
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    if (nz_half(h[q])) {
+                    if (SpVT<VT>::nz(h[q])) {
                         col[o] = (int32_t)(bc * 16 + k0 + q);
-                        val[o] = __ushort_as_half(h[q]);
+                        val[o] = h[q];
                         ++o;
                     }
                 }
@@ -104,11 +130,11 @@ __global__ void sp_extract_kernel(const IT* __restrict__ rp, const IT* __restric
 }
 
 // C[map(r), tile] for rows with at most SP_LONG nonzeros: a warp per (row, 128-column tile).
-template <typename IT, bool VEC>
+template <typename VT, typename IT, bool VEC>
 __global__ void __launch_bounds__(SP_WARPS * 32)
 sp_gather_short_kernel(const int32_t* __restrict__ rows, int64_t nrows,
                        const int64_t* __restrict__ rptr, const int32_t* __restrict__ col,
-                       const __half* __restrict__ val, const __half* __restrict__ B,
+                       const VT* __restrict__ val, const VT* __restrict__ B,
                        float* __restrict__ C, const IT* __restrict__ row_map, int64_t M,
                        int64_t K, int64_t N, unsigned* __restrict__ err) {
     const int lane = threadIdx.x & 31;
@@ -123,7 +149,7 @@ sp_gather_short_kernel(const int32_t* __restrict__ rows, int64_t nrows,
     for (int64_t base = e0; base < e1; base += 32) {
         const int cnt = (int)min((int64_t)32, e1 - base);
         const int64_t my_c = lane < cnt ? (int64_t)col[base + lane] : 0;
-        const float my_a = lane < cnt ? __half2float(val[base + lane]) : 0.0f;
+        const float my_a = lane < cnt ? SpVT<VT>::f(val[base + lane]) : 0.0f;
         for (int u0 = 0; u0 < cnt; u0 += 4) {
             float bb[4][4];
             float a[4];
@@ -132,16 +158,13 @@ sp_gather_short_kernel(const int32_t* __restrict__ rows, int64_t nrows,
                 const int64_t c = __shfl_sync(0xffffffffu, my_c, (u0 + u) & 31);
                 a[u] = __shfl_sync(0xffffffffu, my_a, (u0 + u) & 31);
                 const bool live = u0 + u < cnt && c < K;
-                const __half* src = B + c * N + n0;
+                const VT* src = B + c * N + n0;
                 if (VEC && live && n0 + 4 <= N) {
-                    const uint2 x = __ldg(reinterpret_cast<const uint2*>(src));
-                    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&x.x));
-                    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&x.y));
-                    bb[u][0] = f0.x; bb[u][1] = f0.y; bb[u][2] = f1.x; bb[u][3] = f1.y;
+                    SpVT<VT>::b4(src, bb[u]);
                 } else {
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
-                        bb[u][q] = (live && n0 + q < N) ? __half2float(src[q]) : 0.0f;
+                        bb[u][q] = (live && n0 + q < N) ? SpVT<VT>::f(src[q]) : 0.0f;
                 }
             }
 #pragma unroll
@@ -176,10 +199,10 @@ sp_gather_short_kernel(const int32_t* __restrict__ rows, int64_t nrows,
 // warp order into the chunk's fp64 partial; then sp_reduce_kernel adds a row's chunk partials in
 // chunk order and rounds once. (One CTA per hub row of ~40K nonzeros set the time of the whole
 // product.)
-template <bool VEC>
+template <typename VT, bool VEC>
 __global__ void __launch_bounds__(SP_WARPS * 32)
 sp_gather_chunk_kernel(const SparseChunk* __restrict__ chunks, const int32_t* __restrict__ col,
-                       const __half* __restrict__ val, const __half* __restrict__ B,
+                       const VT* __restrict__ val, const VT* __restrict__ B,
                        double* __restrict__ ws, int64_t K, int64_t N) {
     __shared__ double red[SP_WARPS][SP_TN];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -191,7 +214,7 @@ sp_gather_chunk_kernel(const SparseChunk* __restrict__ chunks, const int32_t* __
     for (int64_t base = w0; base < w1; base += 32) {
         const int cnt = (int)min((int64_t)32, w1 - base);
         const int64_t my_c = lane < cnt ? (int64_t)col[base + lane] : 0;
-        const float my_a = lane < cnt ? __half2float(val[base + lane]) : 0.0f;
+        const float my_a = lane < cnt ? SpVT<VT>::f(val[base + lane]) : 0.0f;
         for (int u0 = 0; u0 < cnt; u0 += 4) {
             float bb[4][4];
             float a[4];
@@ -200,16 +223,13 @@ sp_gather_chunk_kernel(const SparseChunk* __restrict__ chunks, const int32_t* __
                 const int64_t c = __shfl_sync(0xffffffffu, my_c, (u0 + u) & 31);
                 a[u] = __shfl_sync(0xffffffffu, my_a, (u0 + u) & 31);
                 const bool live = u0 + u < cnt && c < K;
-                const __half* src = B + c * N + n0;
+                const VT* src = B + c * N + n0;
                 if (VEC && live && n0 + 4 <= N) {
-                    const uint2 x = __ldg(reinterpret_cast<const uint2*>(src));
-                    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&x.x));
-                    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&x.y));
-                    bb[u][0] = f0.x; bb[u][1] = f0.y; bb[u][2] = f1.x; bb[u][3] = f1.y;
+                    SpVT<VT>::b4(src, bb[u]);
                 } else {
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
-                        bb[u][q] = (live && n0 + q < N) ? __half2float(src[q]) : 0.0f;
+                        bb[u][q] = (live && n0 + q < N) ? SpVT<VT>::f(src[q]) : 0.0f;
                 }
             }
 #pragma unroll
@@ -263,9 +283,9 @@ unsigned sp_grid(Handle& h, int64_t warps_wanted) {
 
 }  // namespace
 
-template <typename IT>
+template <typename VT, typename IT>
 void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT* ci,
-                       const __half* v, SparseRows& out) {
+                       const VT* v, int64_t dense_nnz, SparseRows& out) {
     cudaStream_t s = h.stream;
     out = SparseRows();
     out.dense_br.assign(nbr, 1);
@@ -274,7 +294,7 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
                "block values not 16-byte aligned");
     XS_REQUIRE(M < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "too many rows");
     DevBuf<int32_t> d_cnt(M, s);
-    sp_row_count_kernel<IT><<<sp_grid(h, nbr), 256, 0, s>>>(rp, v, nbr, M, d_cnt.get());
+    sp_row_count_kernel<VT, IT><<<sp_grid(h, nbr), 256, 0, s>>>(rp, v, nbr, M, d_cnt.get());
     after_launch(h, "sparse_row_count");
     std::vector<int32_t> cnt(M);
     std::vector<IT> hrp(nbr + 1);
@@ -282,18 +302,19 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
                                   cudaMemcpyDeviceToHost, s));
     XS_CHECK_CUDA(cudaMemcpyAsync(hrp.data(), rp, (nbr + 1) * sizeof(IT), cudaMemcpyDeviceToHost, s));
     XS_CHECK_CUDA(cudaStreamSynchronize(s));
-    // Block rows averaging at most SP_DENSE_NNZ nonzeros per block go to the gather kernels
+    // Block rows averaging at most dense_nnz nonzeros per block go to the gather kernels
     // (block rows with no block stay: the block kernels write their zeros); rptr is a prefix
     // over all rows, with empty ranges for the rows left on the block kernels.
-    std::vector<int32_t> brs, short_rows, long_rows;
+    std::vector<int32_t> brs, short_rows, long_rows, dense_list;
     std::vector<int64_t> rptr(M + 1, 0);
     for (int64_t br = 0; br < nbr; ++br) {
         const int64_t nb = (int64_t)hrp[br + 1] - (int64_t)hrp[br];
         const int64_t r0 = br * 16, r1 = std::min<int64_t>(M, r0 + 16);
         int64_t nz = 0;
         for (int64_t r = r0; r < r1; ++r) nz += cnt[r];
-        const bool sparse = nb > 0 && nz <= SP_DENSE_NNZ * nb;
+        const bool sparse = nb > 0 && nz <= dense_nnz * nb;
         out.dense_br[br] = sparse ? 0 : 1;
+        if (!sparse) dense_list.push_back((int32_t)br);
         if (sparse) {
             brs.push_back((int32_t)br);
             for (int64_t r = r0; r < r1; ++r)
@@ -315,13 +336,18 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
     out.nshort = (int64_t)short_rows.size();
     out.nlong = (int64_t)long_rows.size();
     out.nchunks = (int64_t)chunks.size();
+    out.ndense = (int64_t)dense_list.size();
     if (out.nbrs == 0) return;
     out.rptr = DevBuf<int64_t>(M + 1, s);
     out.brs = DevBuf<int32_t>(brs.size(), s);
     out.short_rows = DevBuf<int32_t>(std::max<size_t>(short_rows.size(), 1), s);
     out.long_rows = DevBuf<int32_t>(std::max<size_t>(long_rows.size(), 1), s);
     out.col = DevBuf<int32_t>(std::max<int64_t>(out.nnz, 1), s);
-    out.val = DevBuf<__half>(std::max<int64_t>(out.nnz, 1), s);
+    out.val = DevBuf<uint8_t>(std::max<int64_t>(out.nnz, 1) * sizeof(VT), s);
+    out.dense_list = DevBuf<int32_t>(std::max<int64_t>(out.ndense, 1), s);
+    if (out.ndense > 0)
+        XS_CHECK_CUDA(cudaMemcpyAsync(out.dense_list.get(), dense_list.data(),
+                                      dense_list.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     XS_CHECK_CUDA(cudaMemcpyAsync(out.rptr.get(), rptr.data(), (M + 1) * sizeof(int64_t),
                                   cudaMemcpyHostToDevice, s));
     XS_CHECK_CUDA(cudaMemcpyAsync(out.brs.get(), brs.data(), brs.size() * sizeof(int32_t),
@@ -339,29 +365,31 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
         XS_CHECK_CUDA(cudaMemcpyAsync(out.long_first.get(), long_first.data(),
                                       long_first.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     }
-    sp_extract_kernel<IT><<<sp_grid(h, out.nbrs), 256, 0, s>>>(
-        rp, ci, v, out.brs.get(), out.nbrs, M, out.rptr.get(), out.col.get(), out.val.get());
+    sp_extract_kernel<VT, IT><<<sp_grid(h, out.nbrs), 256, 0, s>>>(
+        rp, ci, v, out.brs.get(), out.nbrs, M, out.rptr.get(), out.col.get(),
+        reinterpret_cast<VT*>(out.val.get()));
     after_launch(h, "sparse_extract");
     XS_CHECK_CUDA(cudaStreamSynchronize(s));  // the host vectors go out of scope
 }
 
-template <typename IT>
-void sparse_rows_execute(Handle& h, const SparseRows& sp, const __half* B, float* C, int64_t M,
+template <typename VT, typename IT>
+void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C, int64_t M,
                          int64_t K, int64_t N, const IT* map) {
     if (sp.nbrs == 0 || N == 0) return;
+    const VT* val = reinterpret_cast<const VT*>(sp.val.get());
     const int64_t ntiles = ceil_div(N, SP_TN);
     XS_REQUIRE(ntiles <= 65535, XSPMM_STATUS_UNSUPPORTED, "N too large for the gather kernels");
-    const bool vec = N % 4 == 0 && reinterpret_cast<uintptr_t>(B) % 8 == 0 &&
+    const bool vec = N % 4 == 0 && reinterpret_cast<uintptr_t>(B) % SpVT<VT>::b4_align == 0 &&
                      reinterpret_cast<uintptr_t>(C) % 16 == 0;
     if (sp.nshort > 0) {
         dim3 grid((unsigned)ceil_div(sp.nshort, SP_WARPS), (unsigned)ntiles);
         if (vec)
-            sp_gather_short_kernel<IT, true><<<grid, SP_WARPS * 32, 0, h.stream>>>(
-                sp.short_rows.get(), sp.nshort, sp.rptr.get(), sp.col.get(), sp.val.get(), B, C,
+            sp_gather_short_kernel<VT, IT, true><<<grid, SP_WARPS * 32, 0, h.stream>>>(
+                sp.short_rows.get(), sp.nshort, sp.rptr.get(), sp.col.get(), val, B, C,
                 map, M, K, N, h.d_err);
         else
-            sp_gather_short_kernel<IT, false><<<grid, SP_WARPS * 32, 0, h.stream>>>(
-                sp.short_rows.get(), sp.nshort, sp.rptr.get(), sp.col.get(), sp.val.get(), B, C,
+            sp_gather_short_kernel<VT, IT, false><<<grid, SP_WARPS * 32, 0, h.stream>>>(
+                sp.short_rows.get(), sp.nshort, sp.rptr.get(), sp.col.get(), val, B, C,
                 map, M, K, N, h.d_err);
         after_launch(h, "sparse_gather_short");
     }
@@ -370,11 +398,11 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const __half* B, float
         dim3 grid((unsigned)sp.nchunks, (unsigned)ntiles);
         XS_REQUIRE(sp.nchunks < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED, "too many chunks");
         if (vec)
-            sp_gather_chunk_kernel<true><<<grid, SP_WARPS * 32, 0, h.stream>>>(
-                sp.chunks.get(), sp.col.get(), sp.val.get(), B, ws.get(), K, N);
+            sp_gather_chunk_kernel<VT, true><<<grid, SP_WARPS * 32, 0, h.stream>>>(
+                sp.chunks.get(), sp.col.get(), val, B, ws.get(), K, N);
         else
-            sp_gather_chunk_kernel<false><<<grid, SP_WARPS * 32, 0, h.stream>>>(
-                sp.chunks.get(), sp.col.get(), sp.val.get(), B, ws.get(), K, N);
+            sp_gather_chunk_kernel<VT, false><<<grid, SP_WARPS * 32, 0, h.stream>>>(
+                sp.chunks.get(), sp.col.get(), val, B, ws.get(), K, N);
         after_launch(h, "sparse_gather_chunk");
         const int64_t total = sp.nlong * N;
         const unsigned rgrid = (unsigned)std::max<int64_t>(
@@ -386,12 +414,14 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const __half* B, float
     }
 }
 
-#define XS_INST_SP(IT)                                                                            \
-    template void sparse_rows_build<IT>(Handle&, int64_t, int64_t, const IT*, const IT*,          \
-                                        const __half*, SparseRows&);                              \
-    template void sparse_rows_execute<IT>(Handle&, const SparseRows&, const __half*, float*,      \
-                                          int64_t, int64_t, int64_t, const IT*);
-XS_INST_SP(int32_t)
-XS_INST_SP(int64_t)
+#define XS_INST_SP(VT, IT)                                                                        \
+    template void sparse_rows_build<VT, IT>(Handle&, int64_t, int64_t, const IT*, const IT*,      \
+                                            const VT*, int64_t, SparseRows&);                     \
+    template void sparse_rows_execute<VT, IT>(Handle&, const SparseRows&, const VT*, float*,      \
+                                              int64_t, int64_t, int64_t, const IT*);
+XS_INST_SP(__half, int32_t)
+XS_INST_SP(__half, int64_t)
+XS_INST_SP(float, int32_t)
+XS_INST_SP(float, int64_t)
 
 }  // namespace xspmm_b200
