@@ -327,3 +327,36 @@ def test_plan_fp32_split_matches_block_kernel(executor):
     xs.spmm(executor, A, Bd, C, P.N, 16, False)
     e = errors(ref, C.cpu().numpy(), 1e-5)
     assert e["max_rel_guarded"] <= 1e-5, e
+
+
+@pytest.mark.parametrize("N,index_dtype", [(96, torch.int32), (33, torch.int64)])
+def test_plan_fp32_cut_long_block_rows(executor, N, index_dtype):
+    """fp32 arrowhead (dense first 16 rows and columns): block row 0 holds every block column
+    while the others hold two, so a plan cuts it into pieces whose fp64 partials are added in a
+    fixed order. C within 1e-5 (guarded) of the fp64 oracle, the same bits on every product, and
+    within 1e-5 of the uncut block kernel."""
+    from xspmm_b200 import generators as gen
+    n = 1500
+    rp, ci, v = gen.arrowhead(n, 16, seed=N)
+    P = synth.Problem("arrowhead", n, n, N, rp, ci, v.astype(np.float32), None)
+    B = np.random.default_rng(N).uniform(-1.0, 1.0, (n, N)).astype(np.float32)
+    A = xs.CSRMatrix.from_host(executor, n, n, rp, ci, P.values, index_dtype=index_dtype)
+    ref, _ = _oracle_tier2(P, B, False)
+    Bd = torch.as_tensor(B).to(executor.device)
+    with xs.SpMMPlan(executor, A, 16, False) as plan:
+        C1 = torch.full((n, N), float("nan"), device=executor.device)
+        C2 = torch.full((n, N), float("nan"), device=executor.device)
+        plan.execute(Bd, C1, N)
+        plan.execute(Bd, C2, N)
+    assert torch.equal(C1, C2)
+    e = errors(ref, C1.cpu().numpy(), 1e-5)
+    assert e["max_rel_guarded"] <= 1e-5, e
+    executor.set_tier1_kernel("mma")
+    try:
+        with xs.SpMMPlan(executor, A, 16, False) as plan:
+            C3 = torch.full((n, N), float("nan"), device=executor.device)
+            plan.execute(Bd, C3, N)
+    finally:
+        executor.set_tier1_kernel("auto")
+    e = errors(ref, C3.cpu().numpy(), 1e-5)
+    assert e["max_rel_guarded"] <= 1e-5, e

@@ -85,14 +85,14 @@ struct SparseChunk {
 };
 struct SparseRows {
     std::vector<uint8_t> dense_br;
+    std::vector<int64_t> host_rp;  // the block row pointers, read back once at build
     DevBuf<int64_t> rptr;  // [M+1]: row r's nonzeros are [rptr[r], rptr[r+1]) (empty if dense)
     DevBuf<int32_t> col;
     DevBuf<uint8_t> val;   // nnz values of the matrix's value type
     DevBuf<int32_t> brs, short_rows, long_rows;
     DevBuf<SparseChunk> chunks;    // long rows cut into chunks
     DevBuf<int32_t> long_first;    // [nlong+1] first chunk of each long row
-    DevBuf<int32_t> dense_list;    // [ndense] block rows left on the block kernels, ascending
-    int64_t nbrs = 0, nnz = 0, nshort = 0, nlong = 0, nchunks = 0, ndense = 0;
+    int64_t nbrs = 0, nnz = 0, nshort = 0, nlong = 0, nchunks = 0;
 };
 template <typename VT, typename IT>
 void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT* ci,
@@ -100,11 +100,26 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
 template <typename VT, typename IT>
 void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C, int64_t M,
                          int64_t K, int64_t N, const IT* map);
-// The fp32 block kernel over the listed block rows only (spmm_f32.cu).
+// Work list of the fp32 block kernel inside a plan (spmm_f32.cu): the block rows to compute
+// (those a SparseRows split leaves), each a piece of blocks [j0, j1); block rows far above the
+// average length are cut into several pieces whose fp64 partials (workspace slots) are added in
+// piece order afterwards.
+struct F32Piece {
+    int64_t j0, j1;
+    int32_t br, slot;  // slot -1: the piece is the whole block row and writes C itself
+};
+struct F32Work {
+    DevBuf<F32Piece> pieces;
+    DevBuf<int32_t> long_br, long_first;  // cut block rows, [nlong+1] first slot of each
+    int64_t npieces = 0, nlong = 0, nslots = 0;
+    bool built = false;
+};
+// hrp: the block row pointers on the host (nbr+1); keep: block rows to include (all if null).
+void f32_work_build(Handle& h, int64_t nbr, const std::vector<int64_t>& hrp,
+                    const std::vector<uint8_t>* keep, F32Work& out);
 template <typename IT>
-void bcsr_spmm_f32_rows(Handle& h, const int32_t* br_list, int64_t nlist, const IT* rp,
-                        const IT* ci, const float* v, const float* B, float* C, int64_t M,
-                        int64_t K, int64_t N, const IT* map);
+void bcsr_spmm_f32_work(Handle& h, const F32Work& w, const IT* rp, const IT* ci, const float* v,
+                        const float* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map);
 
 // Which Tier-1 fp16 kernel runs: the handle's setting (xspmm_set_tier1_kernel) if not auto, else
 // the environment XSPMM_TIER1_KERNEL = mma | tc | auto (default auto).

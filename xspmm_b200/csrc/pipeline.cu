@@ -144,17 +144,19 @@ void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
         // fp32: the same split, at a higher fill (the SIMT block kernel pays per nonzero column
         // of a block, a gather per nonzero). A single product splits only when the block kernel
         // would take long against the split's one host round trip.
-        const bool want_split = !one_shot || (double)nnzb * (double)N >= (double)(1 << 22);
+        // The block rows left to the block kernel run from a work list that cuts rows far
+        // above the average length.
+        const bool want_split = !one_shot || (double)nnzb * (double)N >= (double)(1 << 21);
         if (want_split && nbr > 0 && !sparse_built &&
             tier1_kernel_choice(h) == Tier1Kernel::Auto && reinterpret_cast<uintptr_t>(v) % 16 == 0) {
             sparse_rows_build<VT, IT>(h, nbr, M, rp, ci, v, SP_DENSE_NNZ_F32, sparse);
             sparse_built = true;
+            f32_work_build(h, nbr, sparse.host_rp, sparse.nbrs > 0 ? &sparse.dense_br : nullptr,
+                           f32work);
         }
-        if (sparse_built && sparse.nbrs > 0) {
-            if (sparse.ndense > 0)
-                bcsr_spmm_f32_rows<IT>(h, sparse.dense_list.get(), sparse.ndense, rp, ci, v, B, C,
-                                       M, K, N, map);
-            sparse_rows_execute<VT, IT>(h, sparse, B, C, M, K, N, map);
+        if (sparse_built) {
+            bcsr_spmm_f32_work<IT>(h, f32work, rp, ci, v, B, C, M, K, N, map);
+            if (sparse.nbrs > 0) sparse_rows_execute<VT, IT>(h, sparse, B, C, M, K, N, map);
         } else {
             bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
         }

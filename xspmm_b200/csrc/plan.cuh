@@ -43,6 +43,7 @@ struct Plan final : PlanBase {
     bool work_built = false;
     SparseRows sparse;  // block rows of nearly empty blocks, on the gather kernels
     bool sparse_built = false;
+    F32Work f32work;  // fp32: the block rows left to the SIMT block kernel, long ones cut
     bool work_sorted = false;
     bool one_shot = false;  // built for a single product (the Tier-2 call)
 
@@ -56,10 +57,12 @@ struct Plan final : PlanBase {
                (int64_t)(work.long_rows.n + work.first_slot.n) * (int64_t)sizeof(int32_t) +
                (int64_t)bv.n * (int64_t)sizeof(VT) +
                (int64_t)(sparse.rptr.n * sizeof(int64_t) + sparse.col.n * sizeof(int32_t) +
-                         sparse.val.n * sizeof(__half) +
+                         sparse.val.n +
                          (sparse.brs.n + sparse.short_rows.n + sparse.long_rows.n +
                           sparse.long_first.n) * sizeof(int32_t) +
                          sparse.chunks.n * sizeof(SparseChunk)) +
+               (int64_t)(f32work.pieces.n * sizeof(F32Piece) +
+                         (f32work.long_br.n + f32work.long_first.n) * sizeof(int32_t)) +
                (int64_t)(tc.gptr.n * sizeof(int64_t) + tc.gcol.n * sizeof(int32_t) +
                          tc.apk.n * sizeof(__half));
     }
@@ -72,6 +75,7 @@ struct Plan final : PlanBase {
         sparse.rptr.s = sparse.col.s = sparse.val.s = s;
         sparse.brs.s = sparse.short_rows.s = sparse.long_rows.s = sparse.long_first.s = s;
         sparse.chunks.s = s;
+        f32work.pieces.s = f32work.long_br.s = f32work.long_first.s = s;
         tc.gptr.s = s;
         tc.gcol.s = s;
         tc.apk.s = s;

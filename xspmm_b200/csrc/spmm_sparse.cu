@@ -302,10 +302,11 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
                                   cudaMemcpyDeviceToHost, s));
     XS_CHECK_CUDA(cudaMemcpyAsync(hrp.data(), rp, (nbr + 1) * sizeof(IT), cudaMemcpyDeviceToHost, s));
     XS_CHECK_CUDA(cudaStreamSynchronize(s));
+    out.host_rp.assign(hrp.begin(), hrp.end());
     // Block rows averaging at most dense_nnz nonzeros per block go to the gather kernels
     // (block rows with no block stay: the block kernels write their zeros); rptr is a prefix
     // over all rows, with empty ranges for the rows left on the block kernels.
-    std::vector<int32_t> brs, short_rows, long_rows, dense_list;
+    std::vector<int32_t> brs, short_rows, long_rows;
     std::vector<int64_t> rptr(M + 1, 0);
     for (int64_t br = 0; br < nbr; ++br) {
         const int64_t nb = (int64_t)hrp[br + 1] - (int64_t)hrp[br];
@@ -314,7 +315,6 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
         for (int64_t r = r0; r < r1; ++r) nz += cnt[r];
         const bool sparse = nb > 0 && nz <= dense_nnz * nb;
         out.dense_br[br] = sparse ? 0 : 1;
-        if (!sparse) dense_list.push_back((int32_t)br);
         if (sparse) {
             brs.push_back((int32_t)br);
             for (int64_t r = r0; r < r1; ++r)
@@ -336,7 +336,6 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
     out.nshort = (int64_t)short_rows.size();
     out.nlong = (int64_t)long_rows.size();
     out.nchunks = (int64_t)chunks.size();
-    out.ndense = (int64_t)dense_list.size();
     if (out.nbrs == 0) return;
     out.rptr = DevBuf<int64_t>(M + 1, s);
     out.brs = DevBuf<int32_t>(brs.size(), s);
@@ -344,10 +343,6 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
     out.long_rows = DevBuf<int32_t>(std::max<size_t>(long_rows.size(), 1), s);
     out.col = DevBuf<int32_t>(std::max<int64_t>(out.nnz, 1), s);
     out.val = DevBuf<uint8_t>(std::max<int64_t>(out.nnz, 1) * sizeof(VT), s);
-    out.dense_list = DevBuf<int32_t>(std::max<int64_t>(out.ndense, 1), s);
-    if (out.ndense > 0)
-        XS_CHECK_CUDA(cudaMemcpyAsync(out.dense_list.get(), dense_list.data(),
-                                      dense_list.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     XS_CHECK_CUDA(cudaMemcpyAsync(out.rptr.get(), rptr.data(), (M + 1) * sizeof(int64_t),
                                   cudaMemcpyHostToDevice, s));
     XS_CHECK_CUDA(cudaMemcpyAsync(out.brs.get(), brs.data(), brs.size() * sizeof(int32_t),
