@@ -71,6 +71,14 @@ constexpr int LIGHT_MASK = (1 << 30) - 1;
 // faster, from measurements on B200 (index kernel ~2 ns per entry, sweep ~10 us per pass).
 constexpr int64_t SWEEP_VISITS = 8192;
 constexpr int HEAVY_MARK = 1 << 30;
+// Seed sets (seed_sets_kernel): a record of SS_REC ints per row -- the count (-1: not available)
+// and up to SS_REC-1 rows within tau of the row, each with bit 31 set when it would add columns
+// to the row's pattern. Rows with patterns longer than SS_PMAX columns, candidates with patterns
+// longer than SS_QMAX, or more than SS_WALK list entries to walk get no record.
+constexpr int SS_REC = 64;
+constexpr int SS_PMAX = 32;
+constexpr int64_t SS_QMAX = 256;
+constexpr int64_t SS_WALK = 8192;
 
 struct ClusterArgs {
     int32_t M;
@@ -102,6 +110,7 @@ struct ClusterArgs {
     int32_t* perm;          // [M] output (int32 view)
     float tau;
     double t_lo;
+    const int32_t* sets;    // [M*SS_REC] seed sets, or null
     unsigned* err;
 };
 
@@ -393,6 +402,109 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
     __syncthreads();
 
     while (sh.n > 0 && !sh.stop) {
+        // Passes decided from seed sets, by warp 0 alone (no CTA barrier): when no row that is
+        // still unclustered in the seed's set would add columns to p, p stays the seed's pattern
+        // for the whole pass, so the pass accepts exactly the unclustered rows of the set (the
+        // rows within tau of the seed's pattern), in decreasing position order. The record is one
+        // L2 round trip; ranking and the replay of fact 4 are the fast path's, below. Any other
+        // pass (no record, a growing row, more than 32 acceptances) runs the CTA-wide code.
+        if (a.sets) {
+            if (warp == 0) {
+                int n_cur = sh.n, out_cur = sh.out;
+                int pf_seed = -1, pf0 = 0;  // first half of the predicted next seed's record
+                while (n_cur > 0) {
+                    const int seed = st.u(n_cur - 1);
+                    if (seed < 0 || seed >= a.M) break;  // the CTA-wide code flags it
+                    const int32_t* rec = a.sets + (int64_t)seed * SS_REC;
+                    const int v0 = seed == pf_seed ? pf0 : rec[lane];
+                    const int cnt = __shfl_sync(0xffffffffu, v0, 0);
+                    if (cnt < 0 || cnt > SS_REC - 1) break;
+                    const int v1 = cnt >= 32 ? rec[32 + lane] : 0;  // second half, rarely used
+                    const int n = n_cur - 1;
+                    // entry j of the set sits at record index 1 + j
+                    const bool e0 = lane >= 1 && lane <= cnt, e1 = 32 + lane <= cnt;
+                    const int x0 = e0 ? (v0 & 0x7fffffff) : 0, x1 = e1 ? (v1 & 0x7fffffff) : 0;
+                    const int p0 = e0 ? st.p(x0) : -1, p1 = e1 ? st.p(x1) : -1;
+                    const bool l0 = p0 >= 0 && p0 < n, l1 = p1 >= 0 && p1 < n;
+                    if (__any_sync(0xffffffffu, (l0 && v0 < 0) || (l1 && v1 < 0))) break;
+                    const unsigned b0 = __ballot_sync(0xffffffffu, l0);
+                    const unsigned b1 = __ballot_sync(0xffffffffu, l1);
+                    const int nr = __popc(b0) + __popc(b1);
+                    if (nr > 32 || out_cur + 1 + nr > a.M) break;
+                    // The next seed is U[n-nr-1] unless that position is a hole of this pass:
+                    // its record loads while this pass is ranked and replayed.
+                    pf_seed = n - nr >= 1 ? st.u(n - nr - 1) : -1;
+                    if (pf_seed >= 0 && pf_seed < a.M)
+                        pf0 = a.sets[(int64_t)pf_seed * SS_REC + lane];
+                    else
+                        pf_seed = -1;
+                    // The rows now at the top 32 positions are the next seeds unless they are
+                    // accepted first: bring the first halves of their records into L1.
+                    {
+                        const int i = n - nr - 1 - lane;
+                        const int r = i >= 0 ? st.u(i) : -1;
+                        if (r >= 0 && r < a.M)
+                            asm volatile("prefetch.global.L1 [%0];"
+                                         ::"l"(a.sets + (int64_t)r * SS_REC));
+                    }
+                    const unsigned lt = (1u << lane) - 1u;
+                    if (l0) sh.sortbuf[__popc(b0 & lt)] = ((uint64_t)(uint32_t)p0 << 32) | (uint32_t)x0;
+                    if (l1)
+                        sh.sortbuf[__popc(b0) + __popc(b1 & lt)] =
+                            ((uint64_t)(uint32_t)p1 << 32) | (uint32_t)x1;
+                    __syncwarp();
+                    const uint64_t kv = lane < nr ? sh.sortbuf[lane] : 0ull;
+                    int rank = 0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const uint64_t kj = __shfl_sync(0xffffffffu, kv, j);
+                        rank += (j < nr && kj > kv) ? 1 : 0;
+                    }
+                    const int rr = (int)(uint32_t)kv, pp = (int)(kv >> 32);
+                    const int hbase = n - nr;
+                    if (lane < nr) sh.holes[lane] = -1;
+                    __syncwarp();
+                    if (lane < nr && pp >= hbase) sh.holes[pp - hbase] = rank;
+                    __syncwarp();
+                    int mv = -1;
+                    if (lane < nr) {
+                        a.perm[out_cur + 1 + rank] = rr;
+                        if (pp < hbase) {  // hole h_rank receives U[chase(n-1-rank)]
+                            int x = n - 1 - rank, steps = 0;
+                            while (x >= hbase && steps <= nr) {
+                                const int hr = sh.holes[x - hbase];
+                                if (hr < 0) break;
+                                x = n - 1 - hr;
+                                ++steps;
+                            }
+                            if (steps > nr || x >= n) flag_error(a.err, DERR_INTERNAL);
+                            else mv = st.u(x);
+                        }
+                    }
+                    __syncwarp();  // every read of U above happens before the writes below
+                    if (lane < nr) {
+                        st.set_p(rr, -1);
+                        if (mv >= 0) {
+                            st.set_u(pp, mv);
+                            st.set_p(mv, pp);
+                        }
+                    }
+                    if (lane == 0) {
+                        a.perm[out_cur] = seed;
+                        st.set_p(seed, -1);
+                    }
+                    __syncwarp();
+                    out_cur += 1 + nr;
+                    n_cur = n - nr;
+                }
+                if (lane == 0) {
+                    sh.n = n_cur;
+                    sh.out = out_cur;
+                }
+            }
+            __syncthreads();
+            if (sh.n == 0) break;
+        }
         // Pass start without a barrier: every thread reads the seed (U.back()) and its pattern,
         // and the first walk of p's columns runs straight from the seed's pattern entries and
         // their precomputed window slices, so the chain of dependent loads before the first
@@ -1016,6 +1128,109 @@ __global__ void qslice_kernel(const int64_t* __restrict__ qptr, const int32_t* _
     }
 }
 
+// Seed set of every row r: the rows x != r with d(q_r, q_x) <= tau, i.e. the rows a pass seeded
+// by r accepts while p stays q_r, each flagged when q_x is not a subset of q_r. One warp per row.
+// By fact 2 every such x has its size in r's window and meets any |q_r| - m + 1 columns of q_r, so
+// the warp walks the window slices of the cheapest |q_r| - m + 1 columns only; a candidate met in
+// several of them is counted in the first (it holds no earlier walked column). |q_r n q_x| comes
+// from x's pattern, searched in q_r (shared memory). Rows whose record would be incomplete get
+// count -1 and are clustered by the general code.
+__global__ void __launch_bounds__(256)
+seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ qcol,
+                 const longlong2* __restrict__ qslice, const int2* __restrict__ ient, int32_t M,
+                 float tau, double t_lo, int32_t* __restrict__ sets) {
+    __shared__ int32_t spat[8][SS_PMAX];  // q_r of each warp's row
+    __shared__ int32_t srank[8][SS_PMAX]; // walk order of q_r's columns (SS_PMAX: not walked)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < M; r += nwarps) {
+        int32_t* out = sets + r * SS_REC;
+        const int64_t s0 = qptr[r], slen = qptr[r + 1] - s0;
+        if (slen == 0 || slen > SS_PMAX) {
+            if (lane == 0) out[0] = -1;
+            continue;
+        }
+        const int pl = (int)slen;
+        const int col = lane < pl ? qcol[s0 + lane] : 0x7fffffff;
+        const longlong2 sl = lane < pl ? qslice[s0 + lane] : make_longlong2(0, 0);
+        const int64_t len = sl.y - sl.x;
+        const int64_t m = min_inter(t_lo, slen);
+        const int need = (int)(slen - m + 1);
+        int rank = 0;  // of this column by (slice length, index)
+        for (int j = 0; j < pl; ++j) {
+            const int64_t lj = __shfl_sync(0xffffffffu, len, j);
+            rank += (lj < len || (lj == len && j < lane)) ? 1 : 0;
+        }
+        const bool walked = lane < pl && rank < need;
+        __syncwarp();
+        spat[warp][lane] = col;
+        srank[warp][lane] = walked ? rank : SS_PMAX;
+        __syncwarp();
+        int64_t total = walked ? len : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+        if (total > SS_WALK) {
+            if (lane == 0) out[0] = -1;
+            continue;
+        }
+        int cnt = 0;
+        bool bad = false;
+        for (int k = 0; k < need; ++k) {
+            const int tk = __ffs(__ballot_sync(0xffffffffu, walked && rank == k)) - 1;
+            const int64_t e_beg = __shfl_sync(0xffffffffu, sl.x, tk);
+            const int64_t e_end = __shfl_sync(0xffffffffu, sl.y, tk);
+            for (int64_t e0 = e_beg; e0 < e_end; e0 += 32) {
+                const int64_t e = e0 + lane;
+                bool acc = false, grow = false;
+                int x = 0;
+                if (e < e_end) {
+                    x = ient[e].x;
+                    if (x != r) {
+                        const int64_t b = qptr[x], qlen = qptr[x + 1] - b;
+                        if (qlen > SS_QMAX) {
+                            bad = true;
+                        } else {
+                            int64_t inter = 0;
+                            bool dup = false;
+                            auto meet = [&](int c) {  // c in q_r? (first index with spat >= c)
+                                int lo = 0, hi = pl;
+                                while (lo < hi) {
+                                    const int mid = (lo + hi) >> 1;
+                                    if (spat[warp][mid] < c) lo = mid + 1; else hi = mid;
+                                }
+                                if (lo < pl && spat[warp][lo] == c) {
+                                    ++inter;
+                                    dup |= srank[warp][lo] < k;
+                                }
+                            };
+                            // the first 8 columns in one round trip, the rest one by one
+                            int cb[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) cb[j] = j < qlen ? qcol[b + j] : 0;
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (j < qlen) meet(cb[j]);
+                            for (int64_t j = 8; j < qlen; ++j) meet(qcol[b + j]);
+                            if (!dup) {
+                                acc = jaccard_distance(inter, slen + qlen - inter) <= tau;
+                                grow = qlen > inter;
+                            }
+                        }
+                    }
+                }
+                const unsigned ba = __ballot_sync(0xffffffffu, acc);
+                if (acc) {
+                    const int at = cnt + __popc(ba & ((1u << lane) - 1u));
+                    if (at < SS_REC - 1) out[1 + at] = grow ? (int)((unsigned)x | 0x80000000u) : x;
+                }
+                cnt += __popc(ba);
+            }
+        }
+        bad = __any_sync(0xffffffffu, bad);
+        if (lane == 0) out[0] = (bad || cnt > SS_REC - 1) ? -1 : cnt;
+    }
+}
+
 __global__ void init_rows_kernel(int32_t* U, int32_t* pos, int32_t* cnt, int32_t M) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -1180,6 +1395,18 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
                                                       iptr.get(), t_lo, qslice.get());
     after_launch(h, "cluster_qslice");
 
+    // Seed sets of every row (one parallel pass over the index), so that most passes of the
+    // greedy loop need one record read instead of a walk; XSPMM_CLUSTER_SEED_SETS=0 turns them off.
+    const char* ss_env = std::getenv("XSPMM_CLUSTER_SEED_SETS");
+    const bool use_sets = !(ss_env && std::strcmp(ss_env, "0") == 0) &&
+                          M * SS_REC * (int64_t)sizeof(int32_t) <= (int64_t(1) << 30);
+    DevBuf<int32_t> sets(use_sets ? M * SS_REC : 0, s);
+    if (use_sets) {
+        seed_sets_kernel<<<grid_1d(h, M * 32, 256), 256, 0, s>>>(
+            qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo, sets.get());
+        after_launch(h, "cluster_seed_sets");
+    }
+
     // State of the greedy loop.
     int sort_cap = 1;
     while (sort_cap < M) sort_cap <<= 1;
@@ -1224,6 +1451,7 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     a.tau = tau;
     a.t_lo = t_lo;
     a.qslice = qslice.get();
+    a.sets = use_sets ? sets.get() : nullptr;
     a.err = h.d_err;
     int smem_optin = 0;
     XS_CHECK_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
