@@ -405,9 +405,10 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
         // Passes decided from seed sets, by warp 0 alone (no CTA barrier): when no row that is
         // still unclustered in the seed's set would add columns to p, p stays the seed's pattern
         // for the whole pass, so the pass accepts exactly the unclustered rows of the set (the
-        // rows within tau of the seed's pattern), in decreasing position order. The record is one
-        // L2 round trip; ranking and the replay of fact 4 are the fast path's, below. Any other
-        // pass (no record, a growing row, more than 32 acceptances) runs the CTA-wide code.
+        // rows within tau of the seed's pattern), in decreasing position order. The record is
+        // usually loaded during the previous pass; the acceptances are ranked across the warp
+        // and replayed as in fact 4. Any other pass (no record, a growing row, more than 32
+        // acceptances) runs the CTA-wide code.
         if (a.sets) {
             if (warp == 0) {
                 int n_cur = sh.n, out_cur = sh.out;
@@ -419,18 +420,47 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     const int v0 = seed == pf_seed ? pf0 : rec[lane];
                     const int cnt = __shfl_sync(0xffffffffu, v0, 0);
                     if (cnt < 0 || cnt > SS_REC - 1) break;
-                    const int v1 = cnt >= 32 ? rec[32 + lane] : 0;  // second half, rarely used
                     const int n = n_cur - 1;
-                    // entry j of the set sits at record index 1 + j
-                    const bool e0 = lane >= 1 && lane <= cnt, e1 = 32 + lane <= cnt;
-                    const int x0 = e0 ? (v0 & 0x7fffffff) : 0, x1 = e1 ? (v1 & 0x7fffffff) : 0;
-                    const int p0 = e0 ? st.p(x0) : -1, p1 = e1 ? st.p(x1) : -1;
-                    const bool l0 = p0 >= 0 && p0 < n, l1 = p1 >= 0 && p1 < n;
-                    if (__any_sync(0xffffffffu, (l0 && v0 < 0) || (l1 && v1 < 0))) break;
-                    const unsigned b0 = __ballot_sync(0xffffffffu, l0);
-                    const unsigned b1 = __ballot_sync(0xffffffffu, l1);
-                    const int nr = __popc(b0) + __popc(b1);
-                    if (nr > 32 || out_cur + 1 + nr > a.M) break;
+                    // Entry j of the set sits at record index 1 + j. Each lane ends up with one
+                    // accepted row and its position (key -1 for none): in place when the set fits
+                    // the first half of the record, else compacted through shared memory.
+                    int key = -1, row = 0, nr;
+                    if (cnt <= 31) {  // uniform across the warp
+                        const bool e0 = lane >= 1 && lane <= cnt;
+                        const int x0 = e0 ? (v0 & 0x7fffffff) : 0;
+                        const int p0 = e0 ? st.p(x0) : -1;
+                        const bool l0 = p0 >= 0 && p0 < n;
+                        if (__any_sync(0xffffffffu, l0 && v0 < 0)) break;
+                        nr = __popc(__ballot_sync(0xffffffffu, l0));
+                        if (l0) {
+                            key = p0;
+                            row = x0;
+                        }
+                    } else {
+                        const int v1 = rec[32 + lane];
+                        const bool e0 = lane >= 1, e1 = 32 + lane <= cnt;
+                        const int x0 = e0 ? (v0 & 0x7fffffff) : 0, x1 = e1 ? (v1 & 0x7fffffff) : 0;
+                        const int p0 = e0 ? st.p(x0) : -1, p1 = e1 ? st.p(x1) : -1;
+                        const bool l0 = p0 >= 0 && p0 < n, l1 = p1 >= 0 && p1 < n;
+                        if (__any_sync(0xffffffffu, (l0 && v0 < 0) || (l1 && v1 < 0))) break;
+                        const unsigned b0 = __ballot_sync(0xffffffffu, l0);
+                        const unsigned b1 = __ballot_sync(0xffffffffu, l1);
+                        nr = __popc(b0) + __popc(b1);
+                        if (nr > 32) break;
+                        const unsigned lt = (1u << lane) - 1u;
+                        if (l0) sh.sortbuf[__popc(b0 & lt)] = ((uint64_t)(uint32_t)p0 << 32) | (uint32_t)x0;
+                        if (l1)
+                            sh.sortbuf[__popc(b0) + __popc(b1 & lt)] =
+                                ((uint64_t)(uint32_t)p1 << 32) | (uint32_t)x1;
+                        __syncwarp();
+                        if (lane < nr) {
+                            const uint64_t kv = sh.sortbuf[lane];
+                            key = (int)(kv >> 32);
+                            row = (int)(uint32_t)kv;
+                        }
+                        __syncwarp();
+                    }
+                    if (out_cur + 1 + nr > a.M) break;
                     // The next seed is U[n-nr-1] unless that position is a hole of this pass:
                     // its record loads while this pass is ranked and replayed.
                     pf_seed = n - nr >= 1 ? st.u(n - nr - 1) : -1;
@@ -447,29 +477,25 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             asm volatile("prefetch.global.L1 [%0];"
                                          ::"l"(a.sets + (int64_t)r * SS_REC));
                     }
-                    const unsigned lt = (1u << lane) - 1u;
-                    if (l0) sh.sortbuf[__popc(b0 & lt)] = ((uint64_t)(uint32_t)p0 << 32) | (uint32_t)x0;
-                    if (l1)
-                        sh.sortbuf[__popc(b0) + __popc(b1 & lt)] =
-                            ((uint64_t)(uint32_t)p1 << 32) | (uint32_t)x1;
-                    __syncwarp();
-                    const uint64_t kv = lane < nr ? sh.sortbuf[lane] : 0ull;
+                    // Rank of each acceptance by decreasing position (positions are distinct):
+                    // independent shuffles of one 32-bit key, so they overlap.
+                    const bool acc = key >= 0;
                     int rank = 0;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const uint64_t kj = __shfl_sync(0xffffffffu, kv, j);
-                        rank += (j < nr && kj > kv) ? 1 : 0;
-                    }
-                    const int rr = (int)(uint32_t)kv, pp = (int)(kv >> 32);
-                    const int hbase = n - nr;
-                    if (lane < nr) sh.holes[lane] = -1;
-                    __syncwarp();
-                    if (lane < nr && pp >= hbase) sh.holes[pp - hbase] = rank;
-                    __syncwarp();
+                    for (int j = 0; j < 32; ++j) rank += __shfl_sync(0xffffffffu, key, j) > key;
+                    const int rr = row, pp = key, hbase = n - nr;
+                    // Fact 4: hole h_t < n-nr receives U[chase(n-1-t)]. Without a hole at or
+                    // above n-nr the chase stops at once.
+                    const unsigned hi = __ballot_sync(0xffffffffu, acc && pp >= hbase);
                     int mv = -1;
-                    if (lane < nr) {
-                        a.perm[out_cur + 1 + rank] = rr;
-                        if (pp < hbase) {  // hole h_rank receives U[chase(n-1-rank)]
+                    if (hi == 0u) {
+                        if (acc) mv = st.u(n - 1 - rank);
+                    } else {
+                        if (lane < nr) sh.holes[lane] = -1;
+                        __syncwarp();
+                        if (acc && pp >= hbase) sh.holes[pp - hbase] = rank;
+                        __syncwarp();
+                        if (acc && pp < hbase) {
                             int x = n - 1 - rank, steps = 0;
                             while (x >= hbase && steps <= nr) {
                                 const int hr = sh.holes[x - hbase];
@@ -480,11 +506,14 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             if (steps > nr || x >= n) flag_error(a.err, DERR_INTERNAL);
                             else mv = st.u(x);
                         }
+                        __syncwarp();
                     }
-                    __syncwarp();  // every read of U above happens before the writes below
-                    if (lane < nr) {
+                    // U is read above at positions >= n-nr only and written below at holes
+                    // < n-nr only, so the two never meet.
+                    if (acc) {
+                        a.perm[out_cur + 1 + rank] = rr;
                         st.set_p(rr, -1);
-                        if (mv >= 0) {
+                        if (pp < hbase && mv >= 0) {
                             st.set_u(pp, mv);
                             st.set_p(mv, pp);
                         }
