@@ -468,21 +468,19 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                         pf0 = a.sets[(int64_t)pf_seed * SS_REC + lane];
                     else
                         pf_seed = -1;
-                    // The rows now at the top 32 positions are the next seeds unless they are
-                    // accepted first: bring the first halves of their records into L1.
-                    {
-                        const int i = n - nr - 1 - lane;
-                        const int r = i >= 0 ? st.u(i) : -1;
-                        if (r >= 0 && r < a.M)
-                            asm volatile("prefetch.global.L1 [%0];"
-                                         ::"l"(a.sets + (int64_t)r * SS_REC));
-                    }
                     // Rank of each acceptance by decreasing position (positions are distinct):
-                    // independent shuffles of one 32-bit key, so they overlap.
+                    // independent shuffles of one 32-bit key, so they overlap; only the lanes
+                    // that can hold one (1..cnt, or 0..nr-1 after compaction), 8 at a time.
                     const bool acc = key >= 0;
+                    const int kmax = cnt <= 31 ? cnt : nr - 1;  // last lane that can hold a key
                     int rank = 0;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) rank += __shfl_sync(0xffffffffu, key, j) > key;
+                    for (int g = 0; g < 32; g += 8) {
+                        if (g > kmax) break;  // uniform across the warp
+#pragma unroll
+                        for (int j = g; j < g + 8; ++j)
+                            rank += __shfl_sync(0xffffffffu, key, j) > key;
+                    }
                     const int rr = row, pp = key, hbase = n - nr;
                     // Fact 4: hole h_t < n-nr receives U[chase(n-1-t)]. Without a hole at or
                     // above n-nr the chase stops at once.
