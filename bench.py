@@ -44,8 +44,8 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 
 # DRAM bytes (read + write) of one cluster_kernel launch on the cfg2 workload, from the ncu capture
-# summarised in profiles/cluster_kernel_cfg2.md (1.074 MB read, nothing written back).
-CLUSTER_TRAFFIC_BYTES = 1074432 + 0
+# summarised in profiles/cluster_kernel_cfg2.md (351 KB read, nothing written back).
+CLUSTER_TRAFFIC_BYTES = 350976 + 0
 
 
 def peaks():
