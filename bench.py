@@ -703,8 +703,9 @@ def run_vendor_compare(args):
     examples/02_spmm_benchmark.cpp:81, plus dtype, the plan-reusing product and block counts).
     Times in ms: xSpMM stage times from SpMMTimings of one Tier-2 call after warm-up (as the
     reference prints them); vendor and plan times averaged over 10 calls after 3 warm-ups with
-    CUDA events (the reference's BenchTimer). Vendor CSR/BSR = cuSPARSE SpMM through
-    torch.sparse (BSR only for fp32, the type cuSPARSE's block kernel takes), dense = cuBLAS
+    CUDA events (the reference's BenchTimer). Vendor CSR = cuSPARSE SpMM through torch.sparse;
+    Vendor BSR = torch's 16x16 BSR product (fp32 only), which torch runs with its own Triton
+    block kernel rather than cuSPARSE; dense = cuBLAS
     through torch.matmul (TF32 off, as cublasSgemm). N = M = K, B = ones, as the reference."""
     import torch
 

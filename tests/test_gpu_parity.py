@@ -33,12 +33,11 @@ def _np(t):
 # ------------------------------------------------------------------------------------------------
 # structure: clustering, permutation, conversion, unpermute -- bit-exact
 # ------------------------------------------------------------------------------------------------
-@pytest.fixture(params=["auto", "sweep", "index", "index-nosets"])
+@pytest.fixture(params=["auto", "bits", "sweep", "index", "index-nosets"])
 def cluster_kernel(request, monkeypatch):
-    """Clustering through the automatic choice (the shared-memory bitset sweep for inputs this
-    small), forced through the cluster-wide sweep, and through the inverted-index kernel that the
-    largest inputs take -- with its per-row seed sets (passes decided from a precomputed record)
-    and without them (every pass walks the index)."""
+    """Clustering through the automatic choice, forced through the shared-memory bitset sweep,
+    the cluster-wide sweep, and the inverted-index kernel -- with its per-row seed sets (passes
+    decided from a precomputed record) and without them (every pass walks the index)."""
     kind = request.param.split("-")[0]
     monkeypatch.setenv("XSPMM_CLUSTER_KERNEL", kind)
     monkeypatch.setenv("XSPMM_CLUSTER_SEED_SETS", "0" if request.param.endswith("nosets") else "1")

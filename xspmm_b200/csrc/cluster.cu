@@ -70,6 +70,13 @@ constexpr int LIGHT_MASK = (1 << 30) - 1;
 // Expected inverted-list entries per pass above which the cluster sweep (cluster_bits.cu) is
 // faster, from measurements on B200 (index kernel ~2 ns per entry, sweep ~10 us per pass).
 constexpr int64_t SWEEP_VISITS = 8192;
+// Below this many expected entries per pass the index path (with seed sets) is chosen even when
+// the bitsets fit: measured on the reference's benchmark patterns at 4096 rows, the index path
+// won at up to ~400 (arrowhead, block diagonal, 0.1 % random, power law) and the bitsets from
+// ~6,000 (1 % and 10 % random). At 1024 rows the bitset rounds are so cheap that they won on
+// nearly every pattern, so below INDEX_MIN_ROWS rows the bitsets are kept whenever they fit.
+constexpr int64_t INDEX_VISITS = 1024;
+constexpr int64_t INDEX_MIN_ROWS = 4096;
 constexpr int HEAVY_MARK = 1 << 30;
 // Seed sets (seed_sets_kernel): a record of SS_REC ints per row -- the count (-1: not available)
 // and up to SS_REC-1 rows within tau of the row, each with bit 31 set when it would add columns
@@ -1355,19 +1362,21 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
         return;
     }
     // Three exact implementations (cluster_bits.cu, this file): row bitsets in one SM's shared
-    // memory (whenever they fit); row patterns spread over a cluster's shared memory (when they
-    // fit and the inverted lists are long, see SWEEP_VISITS); the inverted index otherwise.
+    // memory (when they fit and index passes would be expensive, see INDEX_VISITS); row patterns
+    // spread over a cluster's shared memory (when they fit and the inverted lists are long, see
+    // SWEEP_VISITS); the inverted index with seed sets otherwise.
     // XSPMM_CLUSTER_KERNEL = bits | sweep | index forces one (bits and sweep fail if the matrix
     // does not fit them).
     const char* ck = std::getenv("XSPMM_CLUSTER_KERNEL");
     const bool want_index = ck && std::strcmp(ck, "index") == 0;
     const bool want_bits = ck && std::strcmp(ck, "bits") == 0;
     const bool want_sweep = ck && std::strcmp(ck, "sweep") == 0;
-    if (!want_index && !want_sweep &&
-        cluster_jaccard_bits<IT>(h, M, K, row_ptr, col_ind, tau, w, perm))
+    if (want_bits) {
+        XS_REQUIRE(cluster_jaccard_bits<IT>(h, M, K, row_ptr, col_ind, tau, w, perm),
+                   XSPMM_STATUS_UNSUPPORTED,
+                   "bitset clustering: the row patterns do not fit in shared memory");
         return;
-    XS_REQUIRE(!want_bits, XSPMM_STATUS_UNSUPPORTED,
-               "bitset clustering: the row patterns do not fit in shared memory");
+    }
     const int64_t nbc = ceil_div(K, w);
     XS_REQUIRE(nbc < (int64_t(1) << 31) / NCLS, XSPMM_STATUS_UNSUPPORTED,
                "clustering supports at most 2^26 block columns");
@@ -1393,6 +1402,11 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     // each on a B200), at least npat^2 / (nbc M) (equal when the columns are evenly used, as in
     // random structure); the cluster sweep's pass costs ~10 us whatever the structure.
     const double visits_lb = (double)npat * (double)npat / ((double)nbc * (double)M);
+    // Where index passes are cheap the index path with seed sets beats the bitset sweep, whose
+    // rounds cost the same whatever the structure; elsewhere the bitsets win when they fit.
+    if (!want_index && !want_sweep && (visits_lb > (double)INDEX_VISITS || M < INDEX_MIN_ROWS) &&
+        cluster_jaccard_bits<IT>(h, M, K, row_ptr, col_ind, tau, w, perm))
+        return;
     if (want_sweep || (!want_index && visits_lb > (double)SWEEP_VISITS)) {
         if (cluster_jaccard_sweep<IT>(h, M, nbc, qptr.get(), qcol.get(), tau, perm)) return;
         XS_REQUIRE(!want_sweep, XSPMM_STATUS_UNSUPPORTED,
