@@ -1165,8 +1165,9 @@ __global__ void qslice_kernel(const int64_t* __restrict__ qptr, const int32_t* _
 // Seed set of every row r: the rows x != r with d(q_r, q_x) <= tau, i.e. the rows a pass seeded
 // by r accepts while p stays q_r, each flagged when q_x is not a subset of q_r. One warp per row.
 // By fact 2 every such x has its size in r's window and meets any |q_r| - m + 1 columns of q_r, so
-// the warp walks the window slices of the cheapest |q_r| - m + 1 columns only; a candidate met in
-// several of them is counted in the first (it holds no earlier walked column). |q_r n q_x| comes
+// the warp walks the window slices of the cheapest |q_r| - m + 1 columns only, skipping entries
+// whose size is outside the window; a candidate met in several of them is counted in the first
+// (it holds no earlier walked column). |q_r n q_x| comes
 // from x's pattern, searched in q_r (shared memory). Rows whose record would be incomplete get
 // count -1 and are clustered by the general code.
 __global__ void __launch_bounds__(256)
@@ -1188,7 +1189,7 @@ seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ q
         const int col = lane < pl ? qcol[s0 + lane] : 0x7fffffff;
         const longlong2 sl = lane < pl ? qslice[s0 + lane] : make_longlong2(0, 0);
         const int64_t len = sl.y - sl.x;
-        const int64_t m = min_inter(t_lo, slen);
+        const int64_t m = min_inter(t_lo, slen), ub = max_len(t_lo, slen);
         const int need = (int)(slen - m + 1);
         int rank = 0;  // of this column by (slice length, index)
         for (int j = 0; j < pl; ++j) {
@@ -1218,8 +1219,11 @@ seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ q
                 bool acc = false, grow = false;
                 int x = 0;
                 if (e < e_end) {
-                    x = ient[e].x;
-                    if (x != r) {
+                    const int2 en = ient[e];
+                    x = en.x;
+                    // fact 2: sizes outside [m, |q_r|/t] cannot pass (the top size class of
+                    // the index holds every size from 32 up, hub rows included)
+                    if (x != r && en.y >= m && en.y <= ub) {
                         const int64_t b = qptr[x], qlen = qptr[x + 1] - b;
                         if (qlen > SS_QMAX) {
                             bad = true;
