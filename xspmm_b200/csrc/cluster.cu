@@ -86,6 +86,7 @@ constexpr int SS_REC = 64;
 constexpr int SS_PMAX = 32;
 constexpr int64_t SS_QMAX = 256;
 constexpr int64_t SS_WALK = 8192;
+constexpr int SS_BMCOLS = 8192;  // block columns up to which seed_sets_kernel uses bitmaps
 
 struct ClusterArgs {
     int32_t M;
@@ -1173,11 +1174,19 @@ __global__ void qslice_kernel(const int64_t* __restrict__ qptr, const int32_t* _
 __global__ void __launch_bounds__(256)
 seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ qcol,
                  const longlong2* __restrict__ qslice, const int2* __restrict__ ient, int32_t M,
-                 float tau, double t_lo, int32_t* __restrict__ sets) {
+                 float tau, double t_lo, int32_t nbc, int32_t* __restrict__ sets) {
     __shared__ int32_t spat[8][SS_PMAX];  // q_r of each warp's row
     __shared__ int32_t srank[8][SS_PMAX]; // walk order of q_r's columns (SS_PMAX: not walked)
+    // With at most SS_BMCOLS block columns: q_r as a bitmap, and the columns whose lists were
+    // walked already, so a candidate column is two loads and a bit test instead of a search.
+    __shared__ uint32_t pbm[8][SS_BMCOLS / 32];
+    __shared__ uint32_t ebm[8][SS_BMCOLS / 32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const bool use_bm = nbc <= SS_BMCOLS;
+    if (use_bm)
+        for (int i = lane; i < SS_BMCOLS / 32; i += 32) pbm[warp][i] = ebm[warp][i] = 0u;
+    __syncwarp();
     for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < M; r += nwarps) {
         int32_t* out = sets + r * SS_REC;
         const int64_t s0 = qptr[r], slen = qptr[r + 1] - s0;
@@ -1208,12 +1217,18 @@ seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ q
             if (lane == 0) out[0] = -1;
             continue;
         }
+        if (use_bm && lane < pl) atomicOr(&pbm[warp][col >> 5], 1u << (col & 31));
+        __syncwarp();
         int cnt = 0;
         bool bad = false;
         for (int k = 0; k < need; ++k) {
             const int tk = __ffs(__ballot_sync(0xffffffffu, walked && rank == k)) - 1;
             const int64_t e_beg = __shfl_sync(0xffffffffu, sl.x, tk);
             const int64_t e_end = __shfl_sync(0xffffffffu, sl.y, tk);
+            if (k > 0 && use_bm) {  // list k-1 is done: its column now counts as walked
+                if (walked && rank == k - 1) atomicOr(&ebm[warp][col >> 5], 1u << (col & 31));
+                __syncwarp();
+            }
             for (int64_t e0 = e_beg; e0 < e_end; e0 += 32) {
                 const int64_t e = e0 + lane;
                 bool acc = false, grow = false;
@@ -1231,6 +1246,14 @@ seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ q
                             int64_t inter = 0;
                             bool dup = false;
                             auto meet = [&](int c) {  // c in q_r? (first index with spat >= c)
+                                if (use_bm) {
+                                    const uint32_t bit = 1u << (c & 31);
+                                    if (pbm[warp][c >> 5] & bit) {
+                                        ++inter;
+                                        dup |= (ebm[warp][c >> 5] & bit) != 0u;
+                                    }
+                                    return;
+                                }
                                 int lo = 0, hi = pl;
                                 while (lo < hi) {
                                     const int mid = (lo + hi) >> 1;
@@ -1266,6 +1289,14 @@ seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ q
         }
         bad = __any_sync(0xffffffffu, bad);
         if (lane == 0) out[0] = (bad || cnt > SS_REC - 1) ? -1 : cnt;
+        if (use_bm) {  // clear this row's bits for the next one
+            __syncwarp();
+            if (lane < pl) {
+                atomicAnd(&pbm[warp][col >> 5], ~(1u << (col & 31)));
+                atomicAnd(&ebm[warp][col >> 5], ~(1u << (col & 31)));
+            }
+            __syncwarp();
+        }
     }
 }
 
@@ -1448,7 +1479,8 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     DevBuf<int32_t> sets(use_sets ? M * SS_REC : 0, s);
     if (use_sets) {
         seed_sets_kernel<<<grid_1d(h, M * 32, 256), 256, 0, s>>>(
-            qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo, sets.get());
+            qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo,
+            (int32_t)nbc, sets.get());
         after_launch(h, "cluster_seed_sets");
     }
 
