@@ -1171,7 +1171,7 @@ __global__ void qslice_kernel(const int64_t* __restrict__ qptr, const int32_t* _
 // (it holds no earlier walked column). |q_r n q_x| comes
 // from x's pattern, searched in q_r (shared memory). Rows whose record would be incomplete get
 // count -1 and are clustered by the general code.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 5)
 seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ qcol,
                  const longlong2* __restrict__ qslice, const int2* __restrict__ ient, int32_t M,
                  float tau, double t_lo, int32_t nbc, int32_t* __restrict__ sets) {
