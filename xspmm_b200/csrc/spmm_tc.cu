@@ -25,17 +25,27 @@
 // layout). Two MMAs per stage share one tcgen05.commit: a commit after every 16-deep MMA leaves
 // the tensor pipe idle about half of the time.
 //
-// Roles (160 threads, two CTAs per SM): warp 0 allocates TMEM and its lane 0 issues tcgen05.mma
-// and tcgen05.commit (which frees a stage once its MMAs have read it); warps 1..4 are four
-// producers taking the stages in turn (one issuing thread cannot keep the tensor pipe busy),
-// and afterwards the epilogue: each reads its TMEM lane quarter (warp % 4) with tcgen05.ld.
-// A whole tile is stored to C directly, every lane one row, through the optional row map (so
-// the Tier-2 unpermute stays fused). When the grid would not fill the GPU, the union list is
-// split (split-K) over the CTAs of a thread-block cluster: each writes its partial tile to an
-// L2-resident workspace in a store-coalesced order, and after a cluster barrier each CTA sums
-// its share of the rows over the partials in rank order (deterministic) and stores them. Every
-// mbarrier wait is bounded; a timeout sets an error flag and the CTA still waits (bounded) for
-// its own loads before freeing TMEM and exiting.
+// Accumulation. The tensor core's accumulation into an fp32 TMEM accumulator is not specified to
+// round like IEEE FADD, and a single accumulator carried over the hundreds of union entries of a
+// long block row drifts beyond the 1e-3 tolerance (an emulation with truncating additions gives
+// 1.5e-2 on the 4096 x 11008 pruned-LLM matrix; IEEE fp32 in the reference's block order gives
+// 1.4e-3 there). So union entries are taken in groups of TC_FLUSH_G = 16: a group accumulates in
+// TMEM from zero, then its partial is added to a running fp32 sum with round-to-nearest FADD.
+// TMEM holds two 128 x 256 accumulators used in turn, so the MMAs of group t+1 run while group t
+// is being added.
+//
+// Roles (384 threads, one CTA per SM, all 512 TMEM columns): warp 0 allocates TMEM and its
+// lane 0 issues tcgen05.mma and tcgen05.commit (which frees a stage once its MMAs have read it,
+// and marks an accumulator full after a group); warps 1..3 are producers taking the stages in
+// turn (one issuing thread cannot keep the tensor pipe busy); warps 4..11 are flushers: warp w
+// reads TMEM lane quarter w % 4 (rows) and one 128-column half, keeps its 32 rows x 128 columns
+// of running sums in registers, and at the end stores them to C directly, every lane one row,
+// through the optional row map (so the Tier-2 unpermute stays fused). When the grid would not
+// fill the GPU, the union list is split (split-K) over the CTAs of a thread-block cluster: each
+// writes its partial tile to an L2-resident workspace in a store-coalesced order, and after a
+// cluster barrier each CTA sums its share of the rows over the partials in rank order
+// (deterministic) and stores them. Every mbarrier wait is bounded; a timeout sets an error flag
+// and the CTA still waits (bounded) for its own loads and MMAs before freeing TMEM and exiting.
 #include "ops.cuh"
 #include "blockcols.cuh"
 
@@ -52,19 +62,31 @@ namespace {
 constexpr int TC_GROUP = 8;                        // block rows per tile (M = 128)
 constexpr int TC_BN = 256;                         // columns per tile = the MMA's N
 constexpr int TC_KPS = 2;                          // union entries (MMAs) per stage
-constexpr int TC_STAGES = 4;
+constexpr int TC_STAGES = 9;
 constexpr int A_TILE = TC_GROUP * 512;             // 4 KB: one union entry's stacked A
 constexpr int B_BOX = 16 * 128;                    // 16 rows x 64 fp16 = 2 KB
 constexpr int B_SLAB = (TC_BN / 64) * B_BOX;       // 8 KB: one union entry's B rows
 constexpr int A_STAGE = TC_KPS * A_TILE;           // 8 KB
 constexpr int STAGE_BYTES = TC_KPS * (A_TILE + B_SLAB);  // 24 KB (multiple of 1024)
-constexpr int TC_PRODUCERS = 4;                   // warps 1..4 issue loads, then store C
-constexpr int TC_THREADS = 32 * (1 + TC_PRODUCERS);
+constexpr int TC_PRODUCERS = 3;                   // warps 1..3 issue the loads
+constexpr int TC_FLUSHERS = 8;                    // warps 4..11 sum the TMEM partials, store C
+constexpr int TC_FIRST_FLUSHER = 1 + TC_PRODUCERS;
+constexpr int TC_THREADS = 32 * (1 + TC_PRODUCERS + TC_FLUSHERS);
 static_assert(TC_STAGES % TC_PRODUCERS == 0, "each producer owns fixed stage slots");
-constexpr int TMEM_COLS = 256;
+static_assert(TC_FIRST_FLUSHER % 4 == 0, "flusher w reads TMEM lane quarter w % 4");
+// Union entries accumulated inside the tensor core before the partial is added, with IEEE
+// round-to-nearest, to the running sum in registers. The tensor core's own accumulation is not
+// specified to round to nearest; a chain of hundreds of MMAs into one accumulator drifts beyond
+// the 1e-3 tolerance on long block rows, a chain of 16 does not.
+constexpr int TC_FLUSH_G = 16;
+static_assert(TC_FLUSH_G % TC_KPS == 0, "groups end on stage boundaries");
+constexpr int TC_ACC_COLS = 256;                   // one accumulator: 128 lanes x 256 fp32
+constexpr int TMEM_COLS = 2 * TC_ACC_COLS;         // two accumulators, used in turn
 constexpr long long WAIT_LIMIT = 1ll << 22;        // polls of an mbarrier before giving up
 constexpr size_t TC_SMEM = (size_t)TC_STAGES * STAGE_BYTES + 1024 + 256;
-static_assert(2 * TC_STAGES * 8 + 3 * 8 <= 256, "barrier area");
+static_assert(TC_SMEM <= 232448, "shared memory per CTA");
+// full + empty per stage, acc_full[2], acc_empty[2], done, redbar, then the TMEM address
+static_assert((2 * TC_STAGES + 6) * 8 + 4 <= 256, "barrier area");
 
 // ---- PTX wrappers ---------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -153,16 +175,14 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
             smem_u32(bar))
         : "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+// 32 TMEM lanes (this warp's quarter) x 16 consecutive 32-bit columns, one per register.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
           "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
-          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
-          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
-          "=r"(v[31])
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -198,9 +218,11 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * STAGE_BYTES);
     uint64_t* empty = full + TC_STAGES;
-    uint64_t* accum = empty + TC_STAGES;
-    uint64_t* redbar = accum + 2;  // split-K bulk copies of the partials
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    uint64_t* acc_full = empty + TC_STAGES;  // [2]: accumulator b holds a finished group
+    uint64_t* acc_empty = acc_full + 2;      // [2]: accumulator b has been read by the flushers
+    uint64_t* done = acc_empty + 2;          // every MMA of this CTA has completed
+    uint64_t* redbar = done + 1;             // split-K bulk copies of the partials
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(redbar + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int bid = blockIdx.x;
@@ -218,7 +240,11 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], TC_FLUSHERS);
+        }
+        mbar_init(done, 1);
         mbar_init(redbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
@@ -235,38 +261,56 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    bool have = false;  // the accumulator is complete (set by warps 1..4)
     // Stage j holds union entries j*KPS .. j*KPS+KPS-1 (fewer in the last stage): one MMA each,
     // and one commit per stage -- a commit after every 16-deep MMA leaves the tensor pipe idle
-    // about half the time.
+    // about half the time. Union entries form groups of TC_FLUSH_G; group t accumulates into
+    // TMEM accumulator t % 2 from zero, and the flushers add it to their running sums while the
+    // next group accumulates into the other one.
     const int nst = (nk + TC_KPS - 1) / TC_KPS;
+    const int ngroups = (nk + TC_FLUSH_G - 1) / TC_FLUSH_G;
     if (warp == 0) {
         if (lane == 0) {  // MMA issuer
-            for (int j = 0; j < nst; ++j) {
+            bool ok = true;
+            int mmas = 0;
+            for (int j = 0; j < nst && ok; ++j) {
                 const int s = j % TC_STAGES;
                 if (!mbar_wait(&full[s], (j / TC_STAGES) & 1, err)) break;
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
                 const int ne = min(TC_KPS, nk - j * TC_KPS);
 #pragma unroll
-                for (int kk = 0; kk < TC_KPS; ++kk)
-                    if (kk < ne)
-                        tc_mma(tmem, desc_a(sa + kk * A_TILE), desc_b(sa + A_STAGE + kk * B_SLAB),
-                               TC_IDESC, (j > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < TC_KPS; ++kk) {
+                    if (kk >= ne) break;
+                    const int e = j * TC_KPS + kk;
+                    const int t = e / TC_FLUSH_G, b = t & 1;
+                    const bool first = (e % TC_FLUSH_G) == 0;
+                    if (first && t >= 2) {  // wait until group t-2 has left accumulator b
+                        if (!mbar_wait(&acc_empty[b], ((t >> 1) - 1) & 1, err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
+                    tc_mma(tmem + (uint32_t)(b * TC_ACC_COLS), desc_a(sa + kk * A_TILE),
+                           desc_b(sa + A_STAGE + kk * B_SLAB), TC_IDESC, first ? 0u : 1u);
+                    ++mmas;
+                    if ((e % TC_FLUSH_G) == TC_FLUSH_G - 1 || e == nk - 1)
+                        tc_commit(&acc_full[b]);
+                }
                 tc_commit(&empty[s]);
             }
-            // commit even after a timeout: it arrives only once the MMAs already issued are
-            // done, so TMEM is never read or freed under them
-            if (nk > 0) tc_commit(accum);
-            else mbar_arrive(accum);
+            // arrives once every MMA issued above has completed (also after a timeout), so
+            // TMEM is never freed under a running MMA
+            if (mmas > 0) tc_commit(done);
+            else mbar_arrive(done);
         }
-    } else {
-        // Warps 1..4: loads, then the epilogue. Producer p issues the stages j = p (mod 4), so it
-        // alone refills the slots s = p (mod 4) (the stage count is a multiple of 4) and its
-        // waits on them stay in phase order. A single issuing thread cannot keep the tensor pipe
-        // fed; four can. Per stage: one bulk copy of the stage's packed A tiles (consecutive in
-        // memory) and per entry the 16 x 256 B slab (one 3-D box when N % 64 == 0, else four
-        // 64-column boxes). The warp loads the union columns of 32 / KPS stages at once.
+    } else if (warp < TC_FIRST_FLUSHER) {
+        // Warps 1..3: loads. Producer p issues the stages j = p (mod 3), so it alone refills the
+        // slots s = p (mod 3) (the stage count is a multiple of 3) and its waits on them stay in
+        // phase order. A single issuing thread cannot keep the tensor pipe fed; several can. Per
+        // stage: one bulk copy of the stage's packed A tiles (consecutive in memory) and per
+        // entry the 16 x 256 B slab (one 3-D box when N % 64 == 0, else four 64-column boxes).
+        // The warp loads the union columns of 32 / KPS stages at once.
         const int p = warp - 1;
         constexpr int SPC = 32 / TC_KPS;  // stages per prefetch chunk
         int issued = 0;
@@ -314,101 +358,110 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
                 ++issued;
             }
         }
-
-        // wait for the accumulator; then make sure none of this producer's loads is still in
-        // flight (bounded; they all completed unless a wait timed out) before the stage buffers
-        // are reused for the reduction
-        have = mbar_wait(accum, 0, err);
-        tc_fence_after();
-        if (issued > 0) {  // this producer's slots: its last STAGES/4 stages
+        // none of this producer's loads may still be in flight when the stage buffers are
+        // reused for the split-K reduction or the CTA exits (bounded; they all completed unless
+        // a wait timed out): its slots hold its last STAGES/PRODUCERS stages
+        if (issued > 0 && lane == 0) {
             const int last = p + (issued - 1) * TC_PRODUCERS;
-#pragma unroll
+#pragma unroll 1
             for (int t = 0; t < TC_STAGES / TC_PRODUCERS; ++t) {
                 const int j = last - t * TC_PRODUCERS;
                 if (j >= p) mbar_wait(&full[j % TC_STAGES], (j / TC_STAGES) & 1, err);
             }
         }
         __syncwarp();
+    } else {
+        // Warps 4..11: after every group, read this warp's 32 rows x 128 columns of the
+        // accumulator (lane quarter fq, column half fh) and add them to the running sums with
+        // round-to-nearest FADD, then hand the accumulator back to the MMA issuer.
+        const int fq = warp & 3, fh = (warp - TC_FIRST_FLUSHER) >> 2;
+        float sum[TC_BN / 2];
+#pragma unroll
+        for (int i = 0; i < TC_BN / 2; ++i) sum[i] = 0.0f;
+        bool have = true;  // every group was added
+        const uint32_t lane_base = tmem + ((uint32_t)(fq * 32) << 16) + (uint32_t)(fh * (TC_BN / 2));
+#pragma unroll 1
+        for (int t = 0; t < ngroups; ++t) {
+            const int b = t & 1;
+            if (!mbar_wait(&acc_full[b], (t >> 1) & 1, err)) {
+                have = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a = lane_base + (uint32_t)(b * TC_ACC_COLS);
+#pragma unroll
+            for (int c = 0; c < TC_BN / 2; c += 16) {
+                uint32_t v[16];
+                tmem_ld16(a + (uint32_t)c, v);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) sum[c + i] = __fadd_rn(sum[c + i], __uint_as_float(v[i]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        if (!have) {
+#pragma unroll
+            for (int i = 0; i < TC_BN / 2; ++i) sum[i] = 0.0f;
+        }
+        const int c_first = fh * (TC_BN / 2);  // this warp's first column within the tile
+        if (splits == 1) {
+            // Whole tile: every lane stores its row's 128 columns (through the optional row map,
+            // so the Tier-2 unpermute stays fused).
+            const int64_t grow = (int64_t)g * 128 + fq * 32 + lane;
+            if (grow < M) {
+                const int64_t orow = row_map ? (int64_t)row_map[grow] : grow;
+                if (orow >= 0 && orow < M) {
+                    float* dst = C + orow * N + n0 + c_first;
+                    const int64_t ncol = N - (n0 + c_first);  // valid columns from dst on
+                    if (ncol >= TC_BN / 2) {
+                        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+                        for (int e = 0; e < TC_BN / 8; ++e)
+                            d4[e] = make_float4(sum[4 * e], sum[4 * e + 1], sum[4 * e + 2],
+                                                sum[4 * e + 3]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < TC_BN / 2; ++e)
+                            if (e < ncol) dst[e] = sum[e];
+                    }
+                } else {
+                    flag_error(err, DERR_PERM_OUT_OF_RANGE);
+                }
+            }
+        } else {
+            // Split tile: this CTA's partial goes to the workspace, grouped by owner CTA (see
+            // below): owner k's rows form one block of 64 float4 columns x nr rows, element
+            // (lr, ce) at ce*nr + (lr ^ (ce & 15)).
+            const int nr = 128 / splits;
+            const int row = fq * 32 + lane;
+            const int own = row / nr, lr = row - own * nr;
+            float4* blk = ws + ((size_t)(blockIdx.x / splits) * splits + split) * 8192 +
+                          (size_t)own * 64 * nr;
+#pragma unroll
+            for (int e = 0; e < TC_BN / 8; ++e) {
+                const int ce = c_first / 4 + e;
+                blk[ce * nr + (lr ^ (ce & 15))] =
+                    make_float4(sum[4 * e], sum[4 * e + 1], sum[4 * e + 2], sum[4 * e + 3]);
+            }
+        }
     }
     __syncwarp();
 
-    if (splits == 1) {
-        // Epilogue of a whole tile: each epilogue warp reads its TMEM lane quarter (warp % 4),
-        // 32 columns at a time, and every lane stores its row (through the optional row map,
-        // so the Tier-2 unpermute stays fused).
-        if (warp >= 1) {
-            const int q = warp & 3;
-            const int64_t grow = (int64_t)g * 128 + q * 32 + lane;
-            float* dst = nullptr;
-            if (grow < M) {
-                const int64_t orow = row_map ? (int64_t)row_map[grow] : grow;
-                if (orow >= 0 && orow < M) dst = C + orow * N;
-                else flag_error(err, DERR_PERM_OUT_OF_RANGE);
-            }
-#pragma unroll 1
-            for (int c0 = 0; c0 < TC_BN && n0 + c0 < N; c0 += 32) {
-                uint32_t v[32];
-                if (nk > 0 && have) {
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] = 0u;
-                }
-                const int64_t col = (int64_t)n0 + c0;
-                if (dst) {
-                    if (col + 32 <= N) {
-                        float4* d4 = reinterpret_cast<float4*>(dst + col);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            d4[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                                                __uint_as_float(v[4 * e + 2]),
-                                                __uint_as_float(v[4 * e + 3]));
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (col + e < N) dst[col + e] = __uint_as_float(v[e]);
-                    }
-                }
-            }
-        }
-    } else {
+    if (splits > 1) {
         // Split tile: the `splits` CTAs of the cluster (S = 2, 4 or 8) each hold a partial
-        // 128 x 256 sum; rows [k*nr, (k+1)*nr) belong to CTA k (nr = 128/S). Each CTA writes its
-        // partial to the workspace straight from TMEM, grouped by owner: owner k's rows form one
-        // block of 64 float4 columns x nr rows, element (lr, ce) at ce*nr + (lr ^ (ce & 15)) --
-        // a warp store (32 consecutive rows, one float4 column) stays within 512 bytes, and the
-        // owner's copy in shared memory reads conflict-free along ce. After a cluster barrier
-        // (which publishes the stores) each owner pulls its S blocks with bulk copies, in two
-        // halves of 32 float4 columns, adds them in rank order (a fixed order: the result does
-        // not depend on timing) and stores its rows of C, one warp per 512-byte row segment,
-        // through the row map. The partials stay in L2.
+        // 128 x 256 sum; rows [k*nr, (k+1)*nr) belong to CTA k (nr = 128/S). The flushers wrote
+        // this CTA's partial to the workspace grouped by owner -- a warp store (32 consecutive
+        // rows, one float4 column) stays within 512 bytes, and the owner's copy in shared memory
+        // reads conflict-free along ce. After a cluster barrier (which publishes the stores)
+        // each owner pulls its S blocks with bulk copies, in two halves of 32 float4 columns,
+        // adds them in rank order (a fixed order: the result does not depend on timing) and
+        // stores its rows of C, one warp per 512-byte row segment, through the row map. The
+        // partials stay in L2.
         const int S = splits;
         const int nr = 128 / S;
         const int tile = blockIdx.x / S;
         float4* tile_ws = ws + (size_t)tile * S * 8192;
-        if (warp >= 1) {
-            const int q = warp & 3;
-            const int row = q * 32 + lane;
-            const int own = row / nr, lr = row - own * nr;
-            float4* blk = tile_ws + (size_t)split * 8192 + (size_t)own * 64 * nr;
-#pragma unroll 1
-            for (int ch = 0; ch < TC_BN / 32 && n0 + ch * 32 < N; ++ch) {
-                uint32_t v[32];
-                if (nk > 0 && have) {
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ch * 32), v);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] = 0u;
-                }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int ce = ch * 8 + e;
-                    blk[ce * nr + (lr ^ (ce & 15))] =
-                        make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                                    __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
-                }
-            }
-        }
         // the stores above are read by other CTAs' bulk copies (async proxy)
         asm volatile("fence.proxy.async.global;" ::: "memory");
         cluster_sync_all();
@@ -454,6 +507,7 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
+        mbar_wait(done, 0, err);  // bounded; completes once the last MMA has
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(TMEM_COLS)
@@ -680,9 +734,9 @@ bool tc_supported(int64_t nbr, int64_t nbc, int64_t nnzb, const void* vals, cons
            reinterpret_cast<uintptr_t>(B) % 16 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0;
 }
 
-// Stand-in with the SpMM kernel's block size and shared memory, for occupancy queries: the
-// runtime counts a kernel that allocates TMEM as one CTA per SM, but two of these CTAs (256 TMEM
-// columns each) do run side by side.
+// Stand-in with the SpMM kernel's block size and shared memory, for occupancy queries of cluster
+// launches without the TMEM allocation in the way (the kernel's shared memory already limits it
+// to one CTA per SM).
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_occupancy_stand_in(int* p) {
     if (p) p[threadIdx.x] = 0;
 }
