@@ -79,14 +79,16 @@ constexpr int64_t INDEX_VISITS = 1024;
 constexpr int64_t INDEX_MIN_ROWS = 4096;
 constexpr int HEAVY_MARK = 1 << 30;
 // Seed sets (seed_sets_kernel): a record of SS_REC ints per row -- the count (-1: not available)
-// and up to SS_REC-1 rows within tau of the row, each with bit 31 set when it would add columns
-// to the row's pattern. Rows with patterns longer than SS_PMAX columns, candidates with patterns
-// longer than SS_QMAX, or more than SS_WALK list entries to walk get no record.
+// and, for sets of up to SS_REC-1 rows, the rows within tau of the row, each with bit 31 set when
+// it would add columns to the row's pattern; larger sets, up to SS_CAP rows, sit in a pool and the
+// record's first row slot holds their offset there. A row whose walk would exceed SS_WALK_MAX
+// list entries, or whose set exceeds SS_CAP rows, gets no record.
 constexpr int SS_REC = 64;
-constexpr int SS_PMAX = 32;
-constexpr int64_t SS_QMAX = 256;
-constexpr int64_t SS_WALK = 8192;
-constexpr int SS_BMCOLS = 8192;  // block columns up to which seed_sets_kernel uses bitmaps
+constexpr int SS_CAP = 1023;
+constexpr int64_t SS_WALK_MAX = int64_t(1) << 24;
+constexpr int SS_BM_MAX = 65536;  // block columns up to which seed_sets_kernel uses bitmaps
+constexpr int SS_RUN_SET = 8;     // set size up to which a seed is tested for a singleton run
+static_assert(SS_CAP <= SORT_CAP, "a pool record is settled in the shared sort buffer");
 
 struct ClusterArgs {
     int32_t M;
@@ -119,6 +121,7 @@ struct ClusterArgs {
     float tau;
     double t_lo;
     const int32_t* sets;    // [M*SS_REC] seed sets, or null
+    const int32_t* spool;   // rows of the seed sets larger than SS_REC-1, or null
     unsigned* err;
 };
 
@@ -422,6 +425,51 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                 int n_cur = sh.n, out_cur = sh.out;
                 int pf_seed = -1, pf0 = 0;  // first half of the predicted next seed's record
                 while (n_cur > 0) {
+                    // Singleton run: lane i looks at the seed s_i = U[n-1-i] of the i-th pass
+                    // from now. When the passes before it accepted nothing, s_i's pass accepts
+                    // nothing either exactly when no row of its (complete) set is unclustered at
+                    // a position below its own -- the seeds s_0..s_{i-1} have left by then. The
+                    // leading lanes for which that holds are clustered alone, at once. Sets of
+                    // more than SS_RUN_SET rows end the run.
+                    {
+                        const int pi = n_cur - 1 - lane;
+                        int si = -1;
+                        bool single = false;
+                        if (pi >= 0) {
+                            si = st.u(pi);
+                            if (si >= 0 && si < a.M) {
+                                const int32_t* rc = a.sets + (int64_t)si * SS_REC;
+                                const int c = rc[0];
+                                if (c >= 0 && c <= SS_RUN_SET) {
+                                    int xs[SS_RUN_SET];
+#pragma unroll
+                                    for (int j = 0; j < SS_RUN_SET; ++j)
+                                        xs[j] = j < c ? (rc[1 + j] & 0x7fffffff) : -1;
+                                    single = true;
+#pragma unroll
+                                    for (int j = 0; j < SS_RUN_SET; ++j) {
+                                        if (xs[j] < 0 || xs[j] >= a.M) continue;
+                                        const int px = st.p(xs[j]);
+                                        if (px >= 0 && px < pi) single = false;
+                                    }
+                                }
+                            }
+                        }
+                        const unsigned sb = __ballot_sync(0xffffffffu, single);
+                        const int run = sb == 0xffffffffu ? 32 : __ffs(~sb) - 1;
+                        if (run > 0) {
+                            if (out_cur + run > a.M) break;
+                            if (lane < run) {
+                                a.perm[out_cur + lane] = si;
+                                st.set_p(si, -1);
+                            }
+                            __syncwarp();
+                            out_cur += run;
+                            n_cur -= run;
+                            pf_seed = -1;
+                            continue;
+                        }
+                    }
                     const int seed = st.u(n_cur - 1);
                     if (seed < 0 || seed >= a.M) break;  // the CTA-wide code flags it
                     const int32_t* rec = a.sets + (int64_t)seed * SS_REC;
@@ -539,6 +587,109 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
             }
             __syncthreads();
             if (sh.n == 0) break;
+        }
+        // A pass decided from a pool record (a set of SS_REC..SS_CAP rows), by the whole CTA:
+        // when no unclustered row of the set adds columns to p, the pass accepts exactly the
+        // unclustered rows of the set. They are sorted by decreasing position (the order the
+        // reference appends them in) and their removals replayed as in fact 4, the holes found
+        // by bisection in the sorted positions.
+        if (a.sets && a.spool) {
+            const int n_old = sh.n;
+            const int seed = st.u(n_old - 1);
+            const int c = (seed >= 0 && seed < a.M) ? a.sets[(int64_t)seed * SS_REC] : -1;
+            if (c > SS_REC - 1 && c <= SS_CAP) {  // uniform: every thread read the same record
+                const int32_t* mem = a.spool + a.sets[(int64_t)seed * SS_REC + 1];
+                const int n = n_old - 1;
+                const int out0 = sh.out;
+                constexpr int PER = (SS_CAP + CL_THREADS) / CL_THREADS;
+                int xr[PER], xp[PER];
+                bool grow = false;
+#pragma unroll
+                for (int q = 0; q < PER; ++q) {
+                    const int i = tid + q * CL_THREADS;
+                    xr[q] = -1;
+                    xp[q] = -1;
+                    if (i < c) {
+                        const int v = mem[i];
+                        const int x = v & 0x7fffffff;
+                        const int px = (x >= 0 && x < a.M) ? st.p(x) : -1;
+                        if (px >= 0 && px < n) {
+                            xr[q] = x;
+                            xp[q] = px;
+                            grow |= v < 0;
+                        }
+                    }
+                }
+                if (tid == 0) sh.nr = 0;
+                const int any_grow = __syncthreads_or(grow);
+                if (!any_grow) {
+#pragma unroll
+                    for (int q = 0; q < PER; ++q)
+                        if (xr[q] >= 0)
+                            sh.sortbuf[atomicAdd(&sh.nr, 1)] =
+                                ((uint64_t)(uint32_t)xp[q] << 32) | (uint32_t)xr[q];
+                    __syncthreads();
+                    const int nr = sh.nr;
+                    if (nr > 1) cta_bitonic_sort(sh.sortbuf, nr, pow2_at_least(nr), true);
+                    if (out0 + 1 + nr > a.M) {
+                        if (tid == 0) { flag_error(a.err, DERR_INTERNAL); sh.stop = 1; }
+                        __syncthreads();
+                        break;
+                    }
+                    for (int t = tid; t < nr; t += CL_THREADS) {
+                        const int r = (int)(uint32_t)sh.sortbuf[t];
+                        a.perm[out0 + 1 + t] = r;
+                        st.set_p(r, -1);
+                    }
+                    // holes sortbuf[t] >> 32, decreasing; those >= n-nr are a prefix
+                    int ktop;
+                    {
+                        int lo = 0, hi = nr;
+                        while (lo < hi) {
+                            const int mid = (lo + hi) >> 1;
+                            if ((int)(sh.sortbuf[mid] >> 32) >= n - nr) lo = mid + 1; else hi = mid;
+                        }
+                        ktop = lo;
+                    }
+                    for (int t = ktop + tid; t < nr; t += CL_THREADS) {
+                        const int h = (int)(sh.sortbuf[t] >> 32);
+                        int x = n - 1 - t, steps = 0;
+                        for (;;) {
+                            int lo = 0, hi = ktop;
+                            while (lo < hi) {
+                                const int mid = (lo + hi) >> 1;
+                                if ((int)(sh.sortbuf[mid] >> 32) > x) lo = mid + 1; else hi = mid;
+                            }
+                            if (lo < ktop && (int)(sh.sortbuf[lo] >> 32) == x && steps <= nr) {
+                                x = n - 1 - lo;
+                                ++steps;
+                            } else {
+                                break;
+                            }
+                        }
+                        if (steps > nr || x >= n) {
+                            flag_error(a.err, DERR_INTERNAL);
+                            continue;
+                        }
+                        const int r = st.u(x);
+                        st.set_u(h, r);
+                        st.set_p(r, h);
+                    }
+                    if (tid == 0) {
+                        a.perm[out0] = seed;
+                        st.set_p(seed, -1);
+                        sh.out = out0 + 1 + nr;
+                        sh.n = n - nr;
+                        sh.pass += 1;
+                        sh.nr = 0;
+                    }
+                    __syncthreads();
+                    continue;
+                }
+                __syncthreads();
+                if (tid == 0) sh.nr = 0;
+                __syncthreads();
+            }
         }
         // Pass start without a barrier: every thread reads the seed (U.back()) and its pattern,
         // and the first walk of p's columns runs straight from the seed's pattern entries and
@@ -1166,138 +1317,271 @@ __global__ void qslice_kernel(const int64_t* __restrict__ qptr, const int32_t* _
 // Seed set of every row r: the rows x != r with d(q_r, q_x) <= tau, i.e. the rows a pass seeded
 // by r accepts while p stays q_r, each flagged when q_x is not a subset of q_r. One warp per row.
 // By fact 2 every such x has its size in r's window and meets any |q_r| - m + 1 columns of q_r, so
-// the warp walks the window slices of the cheapest |q_r| - m + 1 columns only, skipping entries
-// whose size is outside the window; a candidate met in several of them is counted in the first
-// (it holds no earlier walked column). |q_r n q_x| comes
-// from x's pattern, searched in q_r (shared memory). Rows whose record would be incomplete get
-// count -1 and are clustered by the general code.
-__global__ void __launch_bounds__(256, 5)
+// the warp walks the window slices of |q_r| - m + 1 columns only (the cheapest ones), skipping
+// entries whose size is outside the window; a candidate met in several of them is counted in the
+// first (it holds no column walked before). |q_r n q_x| comes from x's pattern, looked up in q_r:
+// a shared-memory bitmap of q_r (BM: up to SS_BM_MAX block columns, any pattern size), or a
+// binary search in a copy of q_r (patterns up to 32 columns). A candidate is dropped as soon as
+// the columns left in its pattern cannot lift the intersection to the test's bound.
+//
+// Pass 1 (pool == null) handles every row: the record gets the set size (or -1: unavailable --
+// empty pattern, a set above SS_CAP rows, a walk above SS_WALK_MAX entries, or a pattern the
+// lookup cannot hold) and its first SS_REC-1 rows. Pass 2 (pool != null) walks again the rows
+// whose sets have more than SS_REC-1 rows, writes them to the pool at poff[r] (the same walk, so
+// the same rows), and stores that offset in the record's first row slot.
+template <bool BM>
+__global__ void __launch_bounds__(256)
 seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ qcol,
                  const longlong2* __restrict__ qslice, const int2* __restrict__ ient, int32_t M,
-                 float tau, double t_lo, int32_t nbc, int32_t* __restrict__ sets) {
-    __shared__ int32_t spat[8][SS_PMAX];  // q_r of each warp's row
-    __shared__ int32_t srank[8][SS_PMAX]; // walk order of q_r's columns (SS_PMAX: not walked)
-    // With at most SS_BMCOLS block columns: q_r as a bitmap, and the columns whose lists were
-    // walked already, so a candidate column is two loads and a bit test instead of a search.
-    __shared__ uint32_t pbm[8][SS_BMCOLS / 32];
-    __shared__ uint32_t ebm[8][SS_BMCOLS / 32];
+                 float tau, double t_lo, int32_t nbcw, int32_t* __restrict__ sets,
+                 int32_t* __restrict__ pool, const int64_t* __restrict__ poff) {
+    extern __shared__ uint32_t ss_dyn[];
+    __shared__ int32_t spat[8][32];   // q_r of each warp's row (without bitmaps)
+    __shared__ int32_t srank[8][32];  // walk order of q_r's columns (32: not walked)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    const bool use_bm = nbc <= SS_BMCOLS;
-    if (use_bm)
-        for (int i = lane; i < SS_BMCOLS / 32; i += 32) pbm[warp][i] = ebm[warp][i] = 0u;
-    __syncwarp();
-    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < M; r += nwarps) {
+    const int nw = blockDim.x >> 5;
+    // BM: q_r as a bitmap, and the columns whose lists were walked already
+    uint32_t* pbm = ss_dyn + (size_t)warp * 2 * nbcw;
+    uint32_t* ebm = pbm + nbcw;
+    if constexpr (BM) {
+        for (int i = lane; i < 2 * nbcw; i += 32) pbm[i] = 0u;
+        __syncwarp();
+    }
+    // I >= t_lo * U = t_lo * (|q_r| + |q_x| - I) for an accepted x: the least intersection
+    const double ilo_f = t_lo / (1.0 + t_lo);
+    const int64_t nwarps = (int64_t)gridDim.x * nw;
+    for (int64_t r = (int64_t)blockIdx.x * nw + warp; r < M; r += nwarps) {
         int32_t* out = sets + r * SS_REC;
+        int32_t* pout = nullptr;
+        int pcap = 0;  // pass 2: the set size found by pass 1 (the pool slots of this row)
+        if (pool != nullptr) {  // pass 2: only the rows whose sets overflow the record
+            pcap = out[0];
+            if (pcap <= SS_REC - 1) continue;
+            pout = pool + poff[r];
+        }
         const int64_t s0 = qptr[r], slen = qptr[r + 1] - s0;
-        if (slen == 0 || slen > SS_PMAX) {
+        if (slen == 0 || (!BM && slen > 32)) {
             if (lane == 0) out[0] = -1;
             continue;
         }
-        const int pl = (int)slen;
-        const int col = lane < pl ? qcol[s0 + lane] : 0x7fffffff;
-        const longlong2 sl = lane < pl ? qslice[s0 + lane] : make_longlong2(0, 0);
-        const int64_t len = sl.y - sl.x;
         const int64_t m = min_inter(t_lo, slen), ub = max_len(t_lo, slen);
-        const int need = (int)(slen - m + 1);
-        int rank = 0;  // of this column by (slice length, index)
-        for (int j = 0; j < pl; ++j) {
-            const int64_t lj = __shfl_sync(0xffffffffu, len, j);
-            rank += (lj < len || (lj == len && j < lane)) ? 1 : 0;
-        }
-        const bool walked = lane < pl && rank < need;
-        __syncwarp();
-        spat[warp][lane] = col;
-        srank[warp][lane] = walked ? rank : SS_PMAX;
-        __syncwarp();
-        int64_t total = walked ? len : 0;
+        const int64_t need = slen - m + 1;
+        // Which columns to walk: the `need` ones with the shortest window slices. Up to 32
+        // columns, by rank (slice length, index); beyond, by a length threshold T found by
+        // bisection: every column shorter than T, and the first ones (by index) of length T.
+        int64_t T = 0, ties = 0;
+        if (slen > 32) {
+            int64_t lo = 0, hi = 0;  // hi: the longest slice
+            for (int64_t j = lane; j < slen; j += 32) {
+                const longlong2 s2 = qslice[s0 + j];
+                hi = max(hi, (int64_t)(s2.y - s2.x));
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-        if (total > SS_WALK) {
-            if (lane == 0) out[0] = -1;
-            continue;
+            for (int o = 16; o > 0; o >>= 1) hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+            while (lo < hi) {  // smallest T with #(len <= T) >= need
+                const int64_t mid = lo + (hi - lo) / 2;
+                int64_t c = 0;
+                for (int64_t j = lane; j < slen; j += 32) {
+                    const longlong2 s2 = qslice[s0 + j];
+                    c += (s2.y - s2.x) <= mid ? 1 : 0;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+                if (c >= need) hi = mid; else lo = mid + 1;
+            }
+            T = lo;
+            int64_t below = 0;
+            for (int64_t j = lane; j < slen; j += 32) {
+                const longlong2 s2 = qslice[s0 + j];
+                below += (s2.y - s2.x) < T ? 1 : 0;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) below += __shfl_xor_sync(0xffffffffu, below, o);
+            ties = need - below;  // columns of length exactly T to take, first by index
         }
-        if (use_bm && lane < pl) atomicOr(&pbm[warp][col >> 5], 1u << (col & 31));
-        __syncwarp();
-        int cnt = 0;
-        bool bad = false;
-        for (int k = 0; k < need; ++k) {
-            const int tk = __ffs(__ballot_sync(0xffffffffu, walked && rank == k)) - 1;
-            const int64_t e_beg = __shfl_sync(0xffffffffu, sl.x, tk);
-            const int64_t e_end = __shfl_sync(0xffffffffu, sl.y, tk);
-            if (k > 0 && use_bm) {  // list k-1 is done: its column now counts as walked
-                if (walked && rank == k - 1) atomicOr(&ebm[warp][col >> 5], 1u << (col & 31));
+        const int pl = (int)(slen < 32 ? slen : 32);
+        int col = 0x7fffffff, rank = 32;
+        longlong2 sl = make_longlong2(0, 0);
+        if (slen <= 32) {
+            col = lane < pl ? qcol[s0 + lane] : 0x7fffffff;
+            sl = lane < pl ? qslice[s0 + lane] : make_longlong2(0, 0);
+            const int64_t len = sl.y - sl.x;
+            int rk = 0;  // rank of this column by (slice length, index)
+            for (int j = 0; j < pl; ++j) {
+                const int64_t lj = __shfl_sync(0xffffffffu, len, j);
+                rk += (lj < len || (lj == len && j < lane)) ? 1 : 0;
+            }
+            rank = (lane < pl && rk < need) ? rk : 32;
+            if constexpr (!BM) {
+                __syncwarp();
+                spat[warp][lane] = col;
+                srank[warp][lane] = rank;
                 __syncwarp();
             }
-            for (int64_t e0 = e_beg; e0 < e_end; e0 += 32) {
+        }
+        // Column j of q_r is walked iff chosen(j); the walk takes them by rank (<= 32 columns)
+        // or by index (beyond). Returns the chosen flag of this lane's column j0 + lane, with
+        // the running count of ties at T seen before this chunk.
+        auto chosen = [&](int64_t j, int64_t len, int64_t& tseen) {
+            if (slen <= 32) return j < slen && rank < 32;
+            bool w = j < slen && len < T;
+            const bool tie = j < slen && len == T;
+            const unsigned tb = __ballot_sync(0xffffffffu, tie);
+            const int64_t tr = tseen + __popc(tb & ((1u << lane) - 1u));
+            if (tie && tr < ties) w = true;
+            tseen += __popc(tb);
+            return w;
+        };
+        // total walk (bounded) and, with bitmaps, q_r into the bitmap
+        int64_t total = 0;
+        {
+            int64_t tseen = 0;
+            for (int64_t j0 = 0; j0 < slen; j0 += 32) {
+                const int64_t j = j0 + lane;
+                int64_t len = 0;
+                int c = 0;
+                if (j < slen) {
+                    const longlong2 s2 = slen <= 32 ? sl : qslice[s0 + j];
+                    len = s2.y - s2.x;
+                    c = slen <= 32 ? col : qcol[s0 + j];
+                }
+                const bool w = chosen(j, len, tseen);
+                total += w ? len : 0;
+                if constexpr (BM) {
+                    if (j < slen) atomicOr(&pbm[c >> 5], 1u << (c & 31));
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+        }
+        __syncwarp();
+        int cnt = 0;
+        bool over = total > SS_WALK_MAX;
+        // One chosen column's window slice [e_beg, e_end); k: its walk order (without bitmaps).
+        auto walk = [&](int c, int64_t e_beg, int64_t e_end, int k) {
+            for (int64_t e0 = e_beg; e0 < e_end && !over; e0 += 32) {
                 const int64_t e = e0 + lane;
                 bool acc = false, grow = false;
                 int x = 0;
                 if (e < e_end) {
                     const int2 en = ient[e];
                     x = en.x;
-                    // fact 2: sizes outside [m, |q_r|/t] cannot pass (the top size class of
-                    // the index holds every size from 32 up, hub rows included)
-                    if (x != r && en.y >= m && en.y <= ub) {
-                        const int64_t b = qptr[x], qlen = qptr[x + 1] - b;
-                        if (qlen > SS_QMAX) {
-                            bad = true;
-                        } else {
-                            int64_t inter = 0;
-                            bool dup = false;
-                            auto meet = [&](int c) {  // c in q_r? (first index with spat >= c)
-                                if (use_bm) {
-                                    const uint32_t bit = 1u << (c & 31);
-                                    if (pbm[warp][c >> 5] & bit) {
-                                        ++inter;
-                                        dup |= (ebm[warp][c >> 5] & bit) != 0u;
-                                    }
-                                    return;
-                                }
-                                int lo = 0, hi = pl;
-                                while (lo < hi) {
-                                    const int mid = (lo + hi) >> 1;
-                                    if (spat[warp][mid] < c) lo = mid + 1; else hi = mid;
-                                }
-                                if (lo < pl && spat[warp][lo] == c) {
-                                    ++inter;
-                                    dup |= srank[warp][lo] < k;
-                                }
-                            };
-                            // the first 8 columns in one round trip, the rest one by one
+                    if (x != (int)r && en.y >= m && en.y <= ub) {
+                        const int64_t qlen = en.y;
+                        const int64_t b = qptr[x];
+                        // floor: never above the least intersection an accepted row has
+                        const int64_t inone = (int64_t)floor(ilo_f * (double)(slen + qlen));
+                        int64_t inter = 0;
+                        bool dup = false, dead = false;
+                        for (int64_t j0 = 0; j0 < qlen && !dup && !dead; j0 += 8) {
                             int cb[8];
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) cb[j] = j < qlen ? qcol[b + j] : 0;
+                            for (int j = 0; j < 8; ++j) cb[j] = j0 + j < qlen ? qcol[b + j0 + j] : -1;
 #pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                if (j < qlen) meet(cb[j]);
-                            for (int64_t j = 8; j < qlen; ++j) meet(qcol[b + j]);
-                            if (!dup) {
-                                acc = jaccard_distance(inter, slen + qlen - inter) <= tau;
-                                grow = qlen > inter;
+                            for (int j = 0; j < 8; ++j) {
+                                const int cc = cb[j];
+                                if (cc < 0) break;
+                                if constexpr (BM) {
+                                    const uint32_t bit = 1u << (cc & 31);
+                                    if (pbm[cc >> 5] & bit) {
+                                        ++inter;
+                                        dup |= (ebm[cc >> 5] & bit) != 0u;
+                                    }
+                                } else {
+                                    int lo = 0, hi = pl;
+                                    while (lo < hi) {
+                                        const int mid = (lo + hi) >> 1;
+                                        if (spat[warp][mid] < cc) lo = mid + 1; else hi = mid;
+                                    }
+                                    if (lo < pl && spat[warp][lo] == cc) {
+                                        ++inter;
+                                        dup |= srank[warp][lo] < k;
+                                    }
+                                }
                             }
+                            dead = inter + (qlen - min(qlen, j0 + 8)) < inone;
+                        }
+                        if (!dup && !dead) {
+                            acc = jaccard_distance(inter, slen + qlen - inter) <= tau;
+                            grow = qlen > inter;
                         }
                     }
                 }
                 const unsigned ba = __ballot_sync(0xffffffffu, acc);
                 if (acc) {
                     const int at = cnt + __popc(ba & ((1u << lane) - 1u));
-                    if (at < SS_REC - 1) out[1 + at] = grow ? (int)((unsigned)x | 0x80000000u) : x;
+                    const int v = grow ? (int)((unsigned)x | 0x80000000u) : x;
+                    if (pout) {
+                        if (at < pcap) pout[at] = v;
+                    } else if (at < SS_REC - 1) {
+                        out[1 + at] = v;
+                    }
                 }
                 cnt += __popc(ba);
+                if (cnt > SS_CAP) over = true;  // uniform across the warp
+            }
+            if constexpr (BM) {  // c is done: later lists count a candidate holding it as seen
+                __syncwarp();
+                if (lane == 0) ebm[c >> 5] |= 1u << (c & 31);
+                __syncwarp();
+            }
+        };
+        if (slen <= 32) {
+            for (int k = 0; k < need && !over; ++k) {
+                const int tk = __ffs(__ballot_sync(0xffffffffu, rank == k)) - 1;
+                walk(__shfl_sync(0xffffffffu, col, tk), __shfl_sync(0xffffffffu, sl.x, tk),
+                     __shfl_sync(0xffffffffu, sl.y, tk), k);
+            }
+        } else {
+            int64_t tseen = 0;
+            for (int64_t j0 = 0; j0 < slen && !over; j0 += 32) {
+                const int64_t j = j0 + lane;
+                longlong2 s2 = make_longlong2(0, 0);
+                int c = 0;
+                if (j < slen) {
+                    s2 = qslice[s0 + j];
+                    c = qcol[s0 + j];
+                }
+                unsigned wb = __ballot_sync(0xffffffffu, chosen(j, s2.y - s2.x, tseen));
+                while (wb && !over) {
+                    const int t = __ffs(wb) - 1;
+                    wb &= wb - 1;
+                    walk(__shfl_sync(0xffffffffu, c, t), __shfl_sync(0xffffffffu, s2.x, t),
+                         __shfl_sync(0xffffffffu, s2.y, t), 0);
+                }
             }
         }
-        bad = __any_sync(0xffffffffu, bad);
-        if (lane == 0) out[0] = (bad || cnt > SS_REC - 1) ? -1 : cnt;
-        if (use_bm) {  // clear this row's bits for the next one
+        if (lane == 0) {
+            if (pout) out[1] = (int32_t)poff[r];
+            else out[0] = over ? -1 : cnt;
+        }
+        if constexpr (BM) {  // clear this row's bits for the next one
             __syncwarp();
-            if (lane < pl) {
-                atomicAnd(&pbm[warp][col >> 5], ~(1u << (col & 31)));
-                atomicAnd(&ebm[warp][col >> 5], ~(1u << (col & 31)));
+            for (int64_t j = lane; j < slen; j += 32) {
+                const int c = qcol[s0 + j];
+                pbm[c >> 5] = 0u;
+                ebm[c >> 5] = 0u;
             }
             __syncwarp();
         }
     }
+}
+
+// Sizes of the sets that overflow their record (more than SS_REC-1 rows), 0 for the others.
+__global__ void seed_sets_overflow_kernel(const int32_t* __restrict__ sets, int32_t M,
+                                          int64_t* __restrict__ ocnt) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < M;
+         r += (int64_t)gridDim.x * blockDim.x) {
+        const int c = sets[r * SS_REC];
+        ocnt[r] = c > SS_REC - 1 ? c : 0;
+    }
+}
+
+// Records whose overflow could not be kept (the pool would not fit): unavailable.
+__global__ void seed_sets_drop_overflow_kernel(int32_t* __restrict__ sets, int32_t M) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < M;
+         r += (int64_t)gridDim.x * blockDim.x)
+        if (sets[r * SS_REC] > SS_REC - 1) sets[r * SS_REC] = -1;
 }
 
 __global__ void init_rows_kernel(int32_t* U, int32_t* pos, int32_t* cnt, int32_t M) {
@@ -1477,11 +1761,49 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     const bool use_sets = !(ss_env && std::strcmp(ss_env, "0") == 0) &&
                           M * SS_REC * (int64_t)sizeof(int32_t) <= (int64_t(1) << 30);
     DevBuf<int32_t> sets(use_sets ? M * SS_REC : 0, s);
+    DevBuf<int32_t> spool;
     if (use_sets) {
-        seed_sets_kernel<<<grid_1d(h, M * 32, 256), 256, 0, s>>>(
-            qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo,
-            (int32_t)nbc, sets.get());
-        after_launch(h, "cluster_seed_sets");
+        // With bitmaps (q_r and the walked columns, 2 bits per block column per warp) as many
+        // warps per CTA as fit 96 KB, so two CTAs share an SM; without, eight.
+        const bool bm = nbc <= SS_BM_MAX;
+        const int64_t nbcw = bm ? ceil_div(nbc, 32) : 0;
+        const int warps = bm ? (int)std::max<int64_t>(1, std::min<int64_t>(8, 98304 / (8 * nbcw)))
+                             : 8;
+        const size_t dsm = bm ? (size_t)warps * 2 * nbcw * sizeof(uint32_t) : 0;
+        const unsigned g_ss = (unsigned)std::max<int64_t>(
+            1, std::min<int64_t>(ceil_div(M, warps), (int64_t)sm_count(h.device) * 16));
+        auto launch = [&](int32_t* pool, const int64_t* poff) {
+            if (bm) {
+                XS_CHECK_CUDA(cudaFuncSetAttribute(seed_sets_kernel<true>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)dsm));
+                seed_sets_kernel<true><<<g_ss, 32 * warps, dsm, s>>>(
+                    qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo,
+                    (int32_t)nbcw, sets.get(), pool, poff);
+            } else {
+                seed_sets_kernel<false><<<g_ss, 32 * warps, 0, s>>>(
+                    qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo, 0,
+                    sets.get(), pool, poff);
+            }
+            after_launch(h, "cluster_seed_sets");
+        };
+        launch(nullptr, nullptr);
+        // Sets of more than SS_REC-1 rows: into a pool at scanned offsets (second walk of those
+        // rows only), or dropped (no record) if the pool would not fit 32-bit offsets.
+        DevBuf<int64_t> poff(M + 1, s);
+        seed_sets_overflow_kernel<<<grid_1d(h, M, 256), 256, 0, s>>>(sets.get(), (int32_t)M,
+                                                                    poff.get());
+        after_launch(h, "cluster_seed_sets_overflow");
+        exclusive_scan<int64_t>(h, poff.get(), poff.get(), M);
+        const int64_t pool_n = read_scalar<int64_t>(h, poff.get() + M);
+        if (pool_n > 0 && pool_n < (int64_t(1) << 31)) {
+            spool = DevBuf<int32_t>(pool_n, s);
+            launch(spool.get(), poff.get());
+        } else if (pool_n > 0) {
+            seed_sets_drop_overflow_kernel<<<grid_1d(h, M, 256), 256, 0, s>>>(sets.get(),
+                                                                            (int32_t)M);
+            after_launch(h, "cluster_seed_sets_drop");
+        }
     }
 
     // State of the greedy loop.
@@ -1529,6 +1851,7 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
     a.t_lo = t_lo;
     a.qslice = qslice.get();
     a.sets = use_sets ? sets.get() : nullptr;
+    a.spool = spool.get();
     a.err = h.d_err;
     int smem_optin = 0;
     XS_CHECK_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
