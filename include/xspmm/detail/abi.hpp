@@ -27,6 +27,7 @@ struct Abi;
         static constexpr auto unpermute = xspmm_unpermute_dense_##VS##_##IS;                       \
         static constexpr auto plan_csr = xspmm_plan_csr_##VS##f32_##IS;                            \
         static constexpr auto plan_bcsr = xspmm_plan_bcsr_##VS##f32_##IS;                          \
+        static constexpr auto dist_plan_csr = xspmm_dist_plan_csr_##VS##f32_##IS;                  \
     };
 XSPMM_ABI_ROW(__half, int32_t, f16, i32)
 XSPMM_ABI_ROW(__half, int64_t, f16, i64)

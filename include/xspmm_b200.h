@@ -50,6 +50,20 @@ typedef struct xspmm_timings {
 } xspmm_timings_t;
 
 /* ---------------------------------------------------------------------------------------------
+ * Environment variables. Results never depend on them (every path is exact for the structure and
+ * within the SpMM tolerance for C); they select among equivalent kernels, for comparisons and
+ * tests. Unset means automatic.
+ *   XSPMM_CLUSTER_KERNEL = index | bits | sweep   clustering path (read at every clustering
+ *       call): the inverted index, row bitsets in one SM's shared memory, or the row patterns
+ *       spread over a thread-block cluster. bits and sweep return UNSUPPORTED when the matrix
+ *       does not fit them.
+ *   XSPMM_CLUSTER_SEED_SETS = 0                    the index path without the per-row seed sets
+ *       (every pass walks the index; read at every clustering call).
+ *   XSPMM_TIER1_KERNEL = mma | tc                  default fp16 Tier-1 kernel of every handle
+ *       whose xspmm_set_tier1_kernel is automatic (read once per process).
+ * ------------------------------------------------------------------------------------------- */
+
+/* ---------------------------------------------------------------------------------------------
  * Handle. Replaces the role of xspmm::CudaExecutor (include/xspmm/core/executor.hpp:37-51,
  * src/core/executor.cpp:80-108): it binds a device (made current inside every call, so handles on
  * different devices can be used from one thread) and a stream. stream == NULL means the legacy
@@ -156,8 +170,10 @@ xspmm_status_t xspmm_permute_rows_f32_i64(xspmm_handle_t h, int64_t M, int64_t K
  * Its scratch is a fixed 270,336-byte array compiled into the library (every GPU that loads the
  * library holds it until exit), so M is limited to 2,097,152 rows; larger M returns
  * INVALID_ARGUMENT. The first call on a device looks up the array's device address, so make that
- * first call before any stream capture. All calls on a device share the array: calls that overlap
- * on the GPU race and must be serialized by the caller.
+ * first call before any stream capture; the address is looked up again when the device's context
+ * has changed (after cudaDeviceReset), so that call too should come before a capture. All calls
+ * on a device share the array: calls that overlap on the GPU race and must be serialized by the
+ * caller.
  * ------------------------------------------------------------------------------------------- */
 xspmm_status_t xspmm_permute_rows_noalloc_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
     const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t value_bytes,
@@ -294,6 +310,78 @@ xspmm_status_t xspmm_plan_bcsr_f32f32_i64(xspmm_handle_t h, int64_t nbr, int64_t
 xspmm_status_t xspmm_plan_execute(xspmm_plan_t plan, const void* B, float* C, int64_t N);
 xspmm_status_t xspmm_plan_get_info(xspmm_plan_t plan, xspmm_plan_info_t* info);
 xspmm_status_t xspmm_plan_destroy(xspmm_plan_t plan);
+
+/* ---------------------------------------------------------------------------------------------
+ * Multi-GPU: one matrix split by block rows over an NCCL communicator (one process or thread per
+ * GPU). The reference runs on one device only; these entries replace a caller's loop of Tier-1
+ * calls (xspmm::spmm(const BCSRMatrix&, B, C, N), include/xspmm/xspmm.hpp:14-18, launched in
+ * src/cuda/unstructured_mtx_mul.cu:31-51) over block-row slices, with the Tier-2 preparation
+ * (src/cuda/unstructured_mtx_mul.cu:56-130) done once per rank and the reference's unpermute
+ * (src/cuda/mtx_permutation.cu:71-85) applied when C is gathered.
+ *
+ * xspmm_dist_unique_id: a new communicator's id (id_bytes >= 128), made on one rank and handed to
+ *   the others by the caller (a file, a socket, MPI, torch.distributed...).
+ * xspmm_dist_comm_init: joins the communicator on the handle's device (NCCL, non-blocking init).
+ *   It waits at most timeout_ms (<= 0: 60 s) for every rank to join: a rank that never joins gives
+ *   TIMEOUT, an NCCL failure NCCL_ERROR; the communicator is aborted in both cases.
+ * xspmm_dist_comm_wrap: uses an ncclComm_t the caller created (NCCL 2.27+; not destroyed here).
+ * xspmm_dist_plan_csr_*: every rank passes the whole CSR A on its own device (as for
+ *   xspmm_plan_csr_*). Each rank clusters (deterministic: the same permutation everywhere),
+ *   counts the permuted matrix's 16 x 16 blocks, splits the block rows into nranks contiguous
+ *   ranges balanced by nonzero blocks plus row_weight per block row, and builds the BCSR of its
+ *   own range only. The CSR may be freed once the call returns. Synchronizes.
+ * xspmm_dist_plan_execute: C_local (rows [row_begin, row_end) of the clustered matrix, N
+ *   columns, fp32) = this rank's rows of A * B. With bcast_root >= 0, B (K x N, every rank's own
+ *   buffer) is first broadcast in place from that rank (waits for it, within timeout_ms); with
+ *   bcast_root < 0, B must already hold the same values on every rank. The product is
+ *   asynchronous on the handle's stream.
+ * xspmm_dist_gather: the root receives every rank's C_local and writes C (M x N, fp32, the
+ *   caller's row order); the other ranks send theirs (C may be NULL there). Synchronous, within
+ *   timeout_ms. Every rank of the communicator must make the same execute / gather calls in the
+ *   same order.
+ * A timeout aborts the communicator (TIMEOUT); any NCCL error too (NCCL_ERROR); after that every
+ * call on it or its plans returns NCCL_ERROR. hw_block_size must be 16.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct xspmm_dist_comm_s* xspmm_dist_comm_t;
+typedef struct xspmm_dist_plan_s* xspmm_dist_plan_t;
+
+typedef struct xspmm_dist_plan_info {
+    int64_t rows, cols;                   /* M, K of the whole matrix */
+    int64_t row_begin, row_end;           /* this rank's rows of the clustered matrix */
+    int64_t block_begin, block_end;       /* this rank's block rows */
+    int64_t nnz_blocks, nnz_blocks_total; /* blocks held by this rank, by all ranks */
+    int32_t clustered, value_bytes;
+    int64_t device_bytes;                 /* device memory this rank's plan owns */
+} xspmm_dist_plan_info_t;
+
+/* The block-row split of xspmm_dist_plan_csr_* (host only, no device work): bounds[0..parts]
+ * with bounds[0] = 0, bounds[parts] = nbr; range p is the first block row whose prefix of
+ * nonzero blocks plus row_weight per block row reaches p / parts of the total. */
+xspmm_status_t xspmm_dist_partition(const int64_t* bcsr_row_ptr, int64_t nbr, int32_t parts,
+    double row_weight, int64_t* bounds);
+xspmm_status_t xspmm_dist_unique_id(unsigned char* id, int32_t id_bytes);
+xspmm_status_t xspmm_dist_comm_init(xspmm_handle_t h, int32_t nranks, int32_t rank,
+    const unsigned char* id, int32_t id_bytes, int32_t timeout_ms, xspmm_dist_comm_t* comm);
+xspmm_status_t xspmm_dist_comm_wrap(void* nccl_comm, int32_t device, xspmm_dist_comm_t* comm);
+xspmm_status_t xspmm_dist_comm_destroy(xspmm_dist_comm_t comm);
+xspmm_status_t xspmm_dist_plan_csr_f16f32_i32(xspmm_handle_t h, xspmm_dist_comm_t comm, int32_t M,
+    int32_t K, int32_t nnz, const int32_t* row_ptr, const int32_t* col_ind, const void* values,
+    int32_t hw_block_size, int enable_clustering, double row_weight, xspmm_dist_plan_t* out);
+xspmm_status_t xspmm_dist_plan_csr_f16f32_i64(xspmm_handle_t h, xspmm_dist_comm_t comm, int64_t M,
+    int64_t K, int64_t nnz, const int64_t* row_ptr, const int64_t* col_ind, const void* values,
+    int64_t hw_block_size, int enable_clustering, double row_weight, xspmm_dist_plan_t* out);
+xspmm_status_t xspmm_dist_plan_csr_f32f32_i32(xspmm_handle_t h, xspmm_dist_comm_t comm, int32_t M,
+    int32_t K, int32_t nnz, const int32_t* row_ptr, const int32_t* col_ind, const void* values,
+    int32_t hw_block_size, int enable_clustering, double row_weight, xspmm_dist_plan_t* out);
+xspmm_status_t xspmm_dist_plan_csr_f32f32_i64(xspmm_handle_t h, xspmm_dist_comm_t comm, int64_t M,
+    int64_t K, int64_t nnz, const int64_t* row_ptr, const int64_t* col_ind, const void* values,
+    int64_t hw_block_size, int enable_clustering, double row_weight, xspmm_dist_plan_t* out);
+xspmm_status_t xspmm_dist_plan_get_info(xspmm_dist_plan_t plan, xspmm_dist_plan_info_t* info);
+xspmm_status_t xspmm_dist_plan_execute(xspmm_dist_plan_t plan, void* B, float* C_local, int64_t N,
+    int32_t bcast_root, int32_t timeout_ms);
+xspmm_status_t xspmm_dist_gather(xspmm_dist_plan_t plan, const float* C_local, float* C,
+    int64_t N, int32_t root, int32_t timeout_ms);
+xspmm_status_t xspmm_dist_plan_destroy(xspmm_dist_plan_t plan);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -30,6 +30,15 @@ class Timings(ctypes.Structure):
         "total_pipeline_ms")]
 
 
+class DistPlanInfo(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+                ("row_begin", ctypes.c_int64), ("row_end", ctypes.c_int64),
+                ("block_begin", ctypes.c_int64), ("block_end", ctypes.c_int64),
+                ("nnz_blocks", ctypes.c_int64), ("nnz_blocks_total", ctypes.c_int64),
+                ("clustered", ctypes.c_int32), ("value_bytes", ctypes.c_int32),
+                ("device_bytes", ctypes.c_int64)]
+
+
 class PlanInfo(ctypes.Structure):
     _fields_ = [("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
                 ("block_rows", ctypes.c_int64), ("block_cols", ctypes.c_int64),
@@ -105,6 +114,20 @@ def lib():
     L.xspmm_plan_destroy.argtypes = [_P]
     L.xspmm_permute_rows_noalloc_i32.argtypes = [_P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P,
                                                   _P, _P]
+    L.xspmm_dist_partition.argtypes = [_P, _I64, _I32, ctypes.c_double, _P]
+    L.xspmm_dist_unique_id.argtypes = [_P, _I32]
+    L.xspmm_dist_comm_init.argtypes = [_P, _I32, _I32, _P, _I32, _I32, ctypes.POINTER(_P)]
+    L.xspmm_dist_comm_wrap.argtypes = [_P, _I32, ctypes.POINTER(_P)]
+    L.xspmm_dist_comm_destroy.argtypes = [_P]
+    for suf, IT in (("i32", _I32), ("i64", _I64)):
+        for vt in ("f16f32", "f32f32"):
+            getattr(L, f"xspmm_dist_plan_csr_{vt}_{suf}").argtypes = [
+                _P, _P, IT, IT, IT, _P, _P, _P, IT, ctypes.c_int, ctypes.c_double,
+                ctypes.POINTER(_P)]
+    L.xspmm_dist_plan_get_info.argtypes = [_P, ctypes.POINTER(DistPlanInfo)]
+    L.xspmm_dist_plan_execute.argtypes = [_P, _P, _P, _I64, _I32, _I32]
+    L.xspmm_dist_gather.argtypes = [_P, _P, _P, _I64, _I32, _I32]
+    L.xspmm_dist_plan_destroy.argtypes = [_P]
     _lib = L
     return L
 

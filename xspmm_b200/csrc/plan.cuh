@@ -9,8 +9,11 @@
 #pragma once
 #include <memory>
 #include <type_traits>
+#include <vector>
 
 #include "ops.cuh"
+
+struct xspmm_dist_comm_s;
 
 namespace xspmm_b200 {
 
@@ -96,6 +99,24 @@ void plan_from_bcsr(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT*
 // Whether the automatic Tier-1 choice (or the handle's forced kernel) would take tcgen05 for
 // this matrix at some N.
 bool plan_wants_tc(const Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb);
+
+// A rank's share of a matrix split by block rows over an NCCL communicator (dist.cu).
+struct DistPlanBase {
+    int64_t M = 0, K = 0, nbc = 0;
+    int64_t row_begin = 0, row_end = 0;      // this rank's rows of the clustered matrix
+    int64_t block_begin = 0, block_end = 0;  // and block rows
+    int64_t nnzb = 0, nnzb_total = 0;        // this rank's blocks, and all ranks'
+    bool clustered = false;
+    int value_bytes = 0;
+    std::vector<int64_t> rank_rows;          // rows of rank r: [rank_rows[r], rank_rows[r+1])
+    virtual ~DistPlanBase() = default;
+    virtual void execute(Handle& h, xspmm_dist_comm_s* c, void* B, float* C_local, int64_t N,
+                         int root, int timeout_ms) = 0;
+    virtual void gather(Handle& h, xspmm_dist_comm_s* c, const float* C_local, float* C,
+                        int64_t N, int root, int timeout_ms) = 0;
+    virtual int64_t device_bytes() const = 0;
+    virtual void rebind_stream(cudaStream_t s) = 0;
+};
 
 }  // namespace xspmm_b200
 
