@@ -14,6 +14,8 @@
 // streams or handles at the same time) race on it and must be serialized by the caller.
 #include "ops.cuh"
 
+#include <cuda.h>
+
 #include <mutex>
 
 namespace {
@@ -28,15 +30,36 @@ static __device__ __align__(256) unsigned char g_permute_scratch[SCRATCH_BYTES];
 constexpr int MAX_DEVICES = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_addr[MAX_DEVICES] = {};
+CUcontext g_scratch_ctx[MAX_DEVICES] = {};
 
-// Device address of the scratch array on the current device, looked up once per device. In host
-// code g_permute_scratch names a host-side stand-in, not device memory, so the address must come
-// from cudaGetSymbolAddress with the device current.
+// The context current on the calling thread (driver entry point fetched through the runtime, so
+// the library needs no link against libcuda).
+CUcontext current_context() {
+    using Fn = CUresult (*)(CUcontext*);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(p);
+    });
+    CUcontext c = nullptr;
+    if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+
+// Device address of the scratch array on the current device. In host code g_permute_scratch names
+// a host-side stand-in, not device memory, so the address comes from cudaGetSymbolAddress with the
+// device current. It is looked up at a device's first call and again whenever the device's
+// context has changed since (after cudaDeviceReset the old address is no longer valid).
 void* scratch_on(int device) {
     XS_REQUIRE(device >= 0 && device < MAX_DEVICES, XSPMM_STATUS_UNSUPPORTED,
                "device ordinal above 63");
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_addr[device]) {
+    const CUcontext ctx = current_context();
+    if (!g_scratch_addr[device] || ctx == nullptr || ctx != g_scratch_ctx[device]) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_permute_scratch);
         if (e != cudaSuccess || p == nullptr)
@@ -44,6 +67,7 @@ void* scratch_on(int device) {
                                     std::string("cudaGetSymbolAddress(scratch): ") +
                                         cudaGetErrorString(e));
         g_scratch_addr[device] = p;
+        g_scratch_ctx[device] = ctx;
     }
     return g_scratch_addr[device];
 }
