@@ -424,6 +424,10 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
             if (warp == 0) {
                 int n_cur = sh.n, out_cur = sh.out;
                 int pf_seed = -1, pf0 = 0;  // first half of the predicted next seed's record
+                // A run is looked for at the start and after a pass that accepted nothing, not
+                // after one that found none or accepted rows (matrices whose passes mostly
+                // accept, like hidden blocks, would pay a record round trip per pass for nothing).
+                bool try_run = true;
                 while (n_cur > 0) {
                     // Singleton run: lane i looks at the seed s_i = U[n-1-i] of the i-th pass
                     // from now. When the passes before it accepted nothing, s_i's pass accepts
@@ -431,7 +435,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     // a position below its own -- the seeds s_0..s_{i-1} have left by then. The
                     // leading lanes for which that holds are clustered alone, at once. Sets of
                     // more than SS_RUN_SET rows end the run.
-                    {
+                    if (try_run) {
                         const int pi = n_cur - 1 - lane;
                         int si = -1;
                         bool single = false;
@@ -457,6 +461,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                         }
                         const unsigned sb = __ballot_sync(0xffffffffu, single);
                         const int run = sb == 0xffffffffu ? 32 : __ffs(~sb) - 1;
+                        try_run = run == 32;  // the run ended at a seed that accepts something
                         if (run > 0) {
                             if (out_cur + run > a.M) break;
                             if (lane < run) {
@@ -579,6 +584,7 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                     __syncwarp();
                     out_cur += 1 + nr;
                     n_cur = n - nr;
+                    try_run = nr == 0;
                 }
                 if (lane == 0) {
                     sh.n = n_cur;
