@@ -101,3 +101,19 @@ def test_unpermute_restatement():
     perm = rng.permutation(9)
     out = oracle.unpermute_dense(X, perm)
     assert np.array_equal(out[perm], X)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="compiled reference not built here")
+@pytest.mark.parametrize("name,kw", [("cfg5", dict(scale=15)), ("cfg4", dict(n=1 << 16))])
+def test_fast_clustering_pinned_at_the_largest_reference_sizes(name, kw):
+    """The oracle's fast exact clustering equals the reference's own loop (compiled from its
+    sources) on the R-MAT generator at 2^15 rows and the banded one at 2^16 rows -- about the
+    largest the reference's dense-bitset loop finishes in seconds (10 s and 9 s here). The GPU
+    tests compare full-size results with the fast clustering's digests."""
+    P = synth.CONFIGS[name](**kw)
+    perm = oracle.ref_cluster(P.row_ptr, P.col_ind, P.M, P.K)
+    assert np.array_equal(oracle.cluster_fast(P.row_ptr, P.col_ind, P.M, P.K), perm)
+    rp, ci, v = oracle.ref_permute(P.row_ptr, P.col_ind, P.values, perm, P.K)
+    for a, b in zip(oracle.csr_to_bcsr(rp, ci, v, P.M, P.K),
+                    oracle.ref_csr_to_bcsr(rp, ci, v, P.M, P.K)):
+        assert np.array_equal(a, b)
