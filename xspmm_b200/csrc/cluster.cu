@@ -88,6 +88,11 @@ constexpr int SS_CAP = 1023;
 constexpr int64_t SS_WALK_MAX = int64_t(1) << 24;
 constexpr int SS_BM_MAX = 65536;  // block columns up to which seed_sets_kernel uses bitmaps
 constexpr int SS_RUN_SET = 8;     // set size up to which a seed is tested for a singleton run
+// Rows whose walk exceeds SS_HEAVY list entries get their seed set from seed_sets_heavy_kernel
+// (a CTA per row, hit estimates in a count-min sketch of 2 x SSH_SKETCH counters).
+constexpr int64_t SS_HEAVY = 4096;
+constexpr int SSH_SKETCH_LOG = 13;
+constexpr int SSH_SKETCH = 1 << SSH_SKETCH_LOG;
 static_assert(SS_CAP <= SORT_CAP, "a pool record is settled in the shared sort buffer");
 
 struct ClusterArgs {
@@ -176,6 +181,18 @@ __device__ int64_t cta_excl_scan64(int64_t v, int64_t* s_warp, int64_t* total) {
     }
     __syncthreads();
     const int64_t r = s_warp[warp] + inc - v;
+    __syncthreads();
+    return r;
+}
+
+__device__ int64_t cta_max64_cl(int64_t v, int64_t* s_warp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) s_warp[warp] = v;
+    __syncthreads();
+    int64_t r = s_warp[0];
+    for (int w = 1; w < CL_THREADS / 32; ++w) r = max(r, s_warp[w]);
     __syncthreads();
     return r;
 }
@@ -1340,7 +1357,9 @@ __global__ void __launch_bounds__(256)
 seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ qcol,
                  const longlong2* __restrict__ qslice, const int2* __restrict__ ient, int32_t M,
                  float tau, double t_lo, int32_t nbcw, int32_t* __restrict__ sets,
-                 int32_t* __restrict__ pool, const int64_t* __restrict__ poff) {
+                 int32_t* __restrict__ pool, const int64_t* __restrict__ poff,
+                 int32_t* __restrict__ hlist, int32_t* __restrict__ nheavy,
+                 uint8_t* __restrict__ hflag) {
     extern __shared__ uint32_t ss_dyn[];
     __shared__ int32_t spat[8][32];   // q_r of each warp's row (without bitmaps)
     __shared__ int32_t srank[8][32];  // walk order of q_r's columns (32: not walked)
@@ -1361,13 +1380,22 @@ seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ q
         int32_t* pout = nullptr;
         int pcap = 0;  // pass 2: the set size found by pass 1 (the pool slots of this row)
         if (pool != nullptr) {  // pass 2: only the rows whose sets overflow the record
+            if (hflag != nullptr && hflag[r]) continue;  // seed_sets_heavy_kernel's
             pcap = out[0];
             if (pcap <= SS_REC - 1) continue;
             pout = pool + poff[r];
         }
         const int64_t s0 = qptr[r], slen = qptr[r + 1] - s0;
         if (slen == 0 || (!BM && slen > 32)) {
-            if (lane == 0) out[0] = -1;
+            // without bitmaps, longer patterns go to seed_sets_heavy_kernel when it runs
+            const bool to_heavy = slen > 0 && hlist != nullptr && pool == nullptr;
+            if (lane == 0) {
+                out[0] = -1;
+                if (to_heavy) {
+                    hflag[r] = 1;
+                    hlist[atomicAdd(nheavy, 1)] = (int32_t)r;
+                }
+            }
             continue;
         }
         const int64_t m = min_inter(t_lo, slen), ub = max_len(t_lo, slen);
@@ -1463,6 +1491,13 @@ seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ q
         __syncwarp();
         int cnt = 0;
         bool over = total > SS_WALK_MAX;
+        // a long walk goes to seed_sets_heavy_kernel (pass 1 lists it; pass 2 never sees it)
+        const bool defer = !over && hlist != nullptr && total > SS_HEAVY;
+        if (defer && lane == 0) {
+            hflag[r] = 1;
+            hlist[atomicAdd(nheavy, 1)] = (int32_t)r;
+        }
+        over |= defer;
         // One chosen column's window slice [e_beg, e_end); k: its walk order (without bitmaps).
         auto walk = [&](int c, int64_t e_beg, int64_t e_end, int k) {
             for (int64_t e0 = e_beg; e0 < e_end && !over; e0 += 32) {
@@ -1570,6 +1605,191 @@ seed_sets_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ q
             }
             __syncwarp();
         }
+    }
+}
+
+// Seed sets of the rows whose walk is long (more than SS_HEAVY list entries; hub-like rows of
+// hundreds of block columns against other long rows): one CTA per row, every thread on the walk.
+// A candidate x met through a walked column can only pass when |q_r n q_x| reaches the bound
+// floor(t/(1+t) (|q_r| + |q_x|)), and |q_r n q_x| <= h_x + (m - 1), h_x = the walked columns x
+// holds (the other columns of q_r number m - 1). A first walk counts h_x in a count-min sketch
+// (two hashed counter arrays in shared memory; the smaller counter can only overestimate h_x), a
+// second walk reads the pattern of a candidate only when its estimate passes that bound -- rejected
+// candidates cost no pattern read, and the survivors are evaluated exactly. A candidate is counted
+// at its smallest walked column (it holds no walked column with a smaller index), so both walks
+// run over all walked columns at once. Same record format and passes as seed_sets_kernel.
+__global__ void __launch_bounds__(CL_THREADS)
+seed_sets_heavy_kernel(const int64_t* __restrict__ qptr, const int32_t* __restrict__ qcol,
+                       const longlong2* __restrict__ qslice, const int2* __restrict__ ient,
+                       int32_t M, float tau, double t_lo, int32_t nbcw,
+                       int32_t* __restrict__ sets, int32_t* __restrict__ pool,
+                       const int64_t* __restrict__ poff, const int32_t* __restrict__ hlist,
+                       const int32_t* __restrict__ nheavy) {
+    extern __shared__ uint32_t hs_dyn[];
+    uint32_t* pbm = hs_dyn;                 // q_r
+    uint32_t* cbm = pbm + nbcw;             // the walked columns
+    uint32_t* sk = cbm + nbcw;              // sketch: 2 x SSH_SKETCH counters
+    __shared__ int64_t s_w64[32];
+    __shared__ int64_t s_tot64;
+    __shared__ int s_w[32];
+    __shared__ int s_tot;
+    __shared__ int64_t s_off[CL_THREADS + 1];
+    __shared__ int64_t s_beg[CL_THREADS];
+    __shared__ int s_col[CL_THREADS];
+    __shared__ int s_cnt;
+    const int tid = threadIdx.x;
+    const double ilo_f = t_lo / (1.0 + t_lo);
+    const int nh = *nheavy;
+    auto h1 = [](uint32_t x) { return (x * 2654435761u) >> (32 - SSH_SKETCH_LOG); };
+    auto h2 = [](uint32_t x) { return ((x ^ 0x9e3779b9u) * 2246822519u) >> (32 - SSH_SKETCH_LOG); };
+    for (int hi = blockIdx.x; hi < nh; hi += gridDim.x) {
+        const int r = hlist[hi];
+        int32_t* out = sets + (int64_t)r * SS_REC;
+        int32_t* pout = nullptr;
+        int pcap = 0;
+        if (pool != nullptr) {
+            pcap = out[0];
+            if (pcap <= SS_REC - 1) continue;  // uniform: every thread read the same record
+            pout = pool + poff[r];
+        }
+        const int64_t s0 = qptr[r], slen = qptr[r + 1] - s0;
+        const int64_t m = min_inter(t_lo, slen), ub = max_len(t_lo, slen);
+        const int64_t need = slen - m + 1;
+        // threshold T: the smallest slice length with #(len <= T) >= need (bisection)
+        int64_t lo = 0, hi2 = 0;
+        for (int64_t j = tid; j < slen; j += CL_THREADS) {
+            const longlong2 s2 = qslice[s0 + j];
+            hi2 = max(hi2, (int64_t)(s2.y - s2.x));
+        }
+        hi2 = cta_max64_cl(hi2, s_w64);
+        while (lo < hi2) {
+            const int64_t mid = lo + (hi2 - lo) / 2;
+            int64_t c = 0;
+            for (int64_t j = tid; j < slen; j += CL_THREADS) {
+                const longlong2 s2 = qslice[s0 + j];
+                c += (s2.y - s2.x) <= mid ? 1 : 0;
+            }
+            int64_t tot;
+            cta_excl_scan64(c, s_w64, &s_tot64);
+            tot = s_tot64;
+            __syncthreads();
+            if (tot >= need) hi2 = mid; else lo = mid + 1;
+        }
+        const int64_t T = lo;
+        // q_r and the walked columns into their bitmaps; clear the sketch
+        for (int i = tid; i < 2 * SSH_SKETCH; i += CL_THREADS) sk[i] = 0u;
+        int64_t below = 0;
+        for (int64_t j = tid; j < slen; j += CL_THREADS) {
+            const longlong2 s2 = qslice[s0 + j];
+            below += (s2.y - s2.x) < T ? 1 : 0;
+        }
+        cta_excl_scan64(below, s_w64, &s_tot64);
+        const int64_t ties = need - s_tot64;
+        __syncthreads();
+        int64_t tseen = 0;
+        for (int64_t c0 = 0; c0 < slen; c0 += CL_THREADS) {
+            const int64_t j = c0 + tid;
+            int64_t len = -1;
+            int col = 0;
+            if (j < slen) {
+                const longlong2 s2 = qslice[s0 + j];
+                len = s2.y - s2.x;
+                col = qcol[s0 + j];
+                atomicOr(&pbm[col >> 5], 1u << (col & 31));
+            }
+            const int tie = (len == T) ? 1 : 0;
+            const int tr = cta_excl_scan(tie, s_w, &s_tot);
+            const bool w = j < slen && (len < T || (tie && tseen + tr < ties));
+            tseen += s_tot;
+            if (w) atomicOr(&cbm[col >> 5], 1u << (col & 31));
+        }
+        if (tid == 0) s_cnt = 0;
+        __syncthreads();
+        // The two walks: over chunks of CL_THREADS pattern entries, each thread holding one
+        // (walked) column's window slice, flattened so that the CTA's threads share the entries.
+        auto walk = [&](auto&& f) {
+            for (int64_t c0 = 0; c0 < slen; c0 += CL_THREADS) {
+                const int64_t j = c0 + tid;
+                int64_t beg = 0, len = 0;
+                int col = 0;
+                if (j < slen) {
+                    col = qcol[s0 + j];
+                    if (cbm[col >> 5] & (1u << (col & 31))) {
+                        const longlong2 s2 = qslice[s0 + j];
+                        beg = s2.x;
+                        len = s2.y - s2.x;
+                    }
+                }
+                const int64_t off = cta_excl_scan64(len, s_w64, &s_tot64);
+                s_off[tid] = off;
+                s_beg[tid] = beg;
+                s_col[tid] = col;
+                if (tid == 0) s_off[CL_THREADS] = s_tot64;
+                const int64_t tot = s_tot64;
+                __syncthreads();
+                // entry t of the flattened range belongs to the thread k with off_k <= t < off_{k+1}
+                for (int64_t t = tid; t < tot; t += CL_THREADS) {
+                    int a = 0, b = CL_THREADS;
+                    while (b - a > 1) {
+                        const int mid = (a + b) >> 1;
+                        if (s_off[mid] <= t) a = mid; else b = mid;
+                    }
+                    f(ient[s_beg[a] + (t - s_off[a])], s_col[a]);
+                }
+                __syncthreads();
+            }
+        };
+        // walk 1: h_x estimates
+        walk([&](int2 en, int) {
+            if (en.x == r || en.y < m || en.y > ub) return;
+            atomicAdd(&sk[h1((uint32_t)en.x)], 1u);
+            atomicAdd(&sk[SSH_SKETCH + h2((uint32_t)en.x)], 1u);
+        });
+        // walk 2: candidates whose estimate can pass, evaluated exactly at their smallest walked
+        // column
+        walk([&](int2 en, int ca) {
+            const int x = en.x;
+            if (x == r || en.y < m || en.y > ub) return;
+            const int64_t qlen = en.y;
+            const int64_t inone = (int64_t)floor(ilo_f * (double)(slen + qlen));
+            const int64_t est = min(sk[h1((uint32_t)x)], sk[SSH_SKETCH + h2((uint32_t)x)]);
+            if (est + (m - 1) < inone) return;
+            const int64_t b = qptr[x];
+            int64_t inter = 0;
+            bool dup = false;
+            for (int64_t j = 0; j < qlen; ++j) {
+                const int cc = qcol[b + j];
+                const uint32_t bit = 1u << (cc & 31);
+                if (cc < ca && (cbm[cc >> 5] & bit)) {
+                    dup = true;  // counted at a smaller walked column
+                    break;
+                }
+                inter += (pbm[cc >> 5] & bit) ? 1 : 0;
+                if (inter + (qlen - j - 1) < inone) break;
+            }
+            if (dup) return;
+            if (jaccard_distance(inter, slen + qlen - inter) <= tau) {
+                const int v = qlen > inter ? (int)((unsigned)x | 0x80000000u) : x;
+                const int at = atomicAdd(&s_cnt, 1);
+                if (pout) {
+                    if (at < pcap) pout[at] = v;
+                } else if (at < SS_REC - 1) {
+                    out[1 + at] = v;
+                }
+            }
+        });
+        __syncthreads();
+        if (tid == 0) {
+            if (pout) out[1] = (int32_t)poff[r];
+            else out[0] = s_cnt > SS_CAP ? -1 : s_cnt;
+        }
+        // clear this row's bits
+        for (int64_t j = tid; j < slen; j += CL_THREADS) {
+            const int c = qcol[s0 + j];
+            pbm[c >> 5] = 0u;
+            cbm[c >> 5] = 0u;
+        }
+        __syncthreads();
     }
 }
 
@@ -1778,6 +1998,20 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
         const size_t dsm = bm ? (size_t)warps * 2 * nbcw * sizeof(uint32_t) : 0;
         const unsigned g_ss = (unsigned)std::max<int64_t>(
             1, std::min<int64_t>(ceil_div(M, warps), (int64_t)sm_count(h.device) * 16));
+        // Rows with long walks: a CTA each (seed_sets_heavy_kernel), when its bitmaps of q_r and
+        // of the walked columns plus the sketch fit shared memory.
+        const int64_t hw = ceil_div(nbc, 32);
+        const size_t hsm = (size_t)(2 * hw + 2 * SSH_SKETCH) * sizeof(uint32_t);
+        const bool heavy = hsm <= 200 * 1024;
+        DevBuf<int32_t> hlist(heavy ? M : 0, s), nheavy(heavy ? 1 : 0, s);
+        DevBuf<uint8_t> hflag(heavy ? M : 0, s);
+        if (heavy) {
+            XS_CHECK_CUDA(cudaMemsetAsync(nheavy.get(), 0, sizeof(int32_t), s));
+            XS_CHECK_CUDA(cudaMemsetAsync(hflag.get(), 0, (size_t)M, s));
+            XS_CHECK_CUDA(cudaFuncSetAttribute(seed_sets_heavy_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)hsm));
+        }
         auto launch = [&](int32_t* pool, const int64_t* poff) {
             if (bm) {
                 XS_CHECK_CUDA(cudaFuncSetAttribute(seed_sets_kernel<true>,
@@ -1785,13 +2019,20 @@ void cluster_jaccard(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row
                                                    (int)dsm));
                 seed_sets_kernel<true><<<g_ss, 32 * warps, dsm, s>>>(
                     qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo,
-                    (int32_t)nbcw, sets.get(), pool, poff);
+                    (int32_t)nbcw, sets.get(), pool, poff, hlist.get(), nheavy.get(),
+                    hflag.get());
             } else {
                 seed_sets_kernel<false><<<g_ss, 32 * warps, 0, s>>>(
                     qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo, 0,
-                    sets.get(), pool, poff);
+                    sets.get(), pool, poff, hlist.get(), nheavy.get(), hflag.get());
             }
             after_launch(h, "cluster_seed_sets");
+            if (heavy) {
+                seed_sets_heavy_kernel<<<(unsigned)sm_count(h.device) * 2, CL_THREADS, hsm, s>>>(
+                    qptr.get(), qcol.get(), qslice.get(), ient.get(), (int32_t)M, tau, t_lo,
+                    (int32_t)hw, sets.get(), pool, poff, hlist.get(), nheavy.get());
+                after_launch(h, "cluster_seed_sets_heavy");
+            }
         };
         launch(nullptr, nullptr);
         // Sets of more than SS_REC-1 rows: into a pool at scanned offsets (second walk of those
