@@ -217,7 +217,8 @@ def run_gpu(args):
     import torch.distributed as dist
 
     import xspmm_b200 as xs
-    from xspmm_b200.shard import BlockRowShard, broadcast_b, partition_block_rows
+    from xspmm_b200 import dist as xd
+    from xspmm_b200.shard import broadcast_b
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -314,30 +315,22 @@ def run_gpu(args):
         torch.cuda.empty_cache()
     barrier()
 
-    # ---- the plan: clustering (every rank, deterministic), permutation, conversion, shard -------
-    e = [ev() for _ in range(4)]
+    # ---- the plan, through the multi-GPU C ABI (xspmm_dist_*): every rank clusters (the result is
+    # deterministic), counts the permuted matrix's blocks and keeps only its own block rows ---------
+    uid = xd.share_unique_id() if world > 1 else xd.unique_id()
+    comm = xd.DistComm(ex, world, rank, uid, timeout_ms=300000)
+    e = [ev() for _ in range(3)]
     e[0].record(stream)
     perm = torch.empty(P.M, dtype=torch.int32, device=dev)
-    xs.compute_1d_jaccard_clustering(ex, A, 0.5, 16, perm)
+    xs.compute_1d_jaccard_clustering(ex, A, 0.5, 16, perm)  # the clustering stage alone
     e[1].record(stream)
-    Ap = xs.apply_permutation(ex, A, perm)
+    shard = xd.DistPlan(comm, A)  # clustering, permutation, block count, own block rows, plan
     e[2].record(stream)
-    Ab = xs.csr_to_bcsr(ex, Ap, 16, 16)
-    e[3].record(stream)
     torch.cuda.synchronize()
     clustering_ms = rmax(e[0].elapsed_time(e[1]))
-    permutation_ms = rmax(e[1].elapsed_time(e[2]))
-    conversion_ms = rmax(e[2].elapsed_time(e[3]))
-    del Ap
-    nnzb = Ab.num_blocks
-    row_ptr_host = Ab.row_ptr.cpu().numpy()
-    bounds = partition_block_rows(row_ptr_host, world)
-    p0 = ev(); p1 = ev()
-    p0.record(stream)
-    shard = BlockRowShard(Ab, int(bounds[rank]), int(bounds[rank + 1]))
-    p1.record(stream)
-    torch.cuda.synchronize()
-    shard_prep_ms = rmax(p0.elapsed_time(p1))
+    plan_build_ms = rmax(e[1].elapsed_time(e[2]))
+    sinfo = shard.info()
+    nnzb = sinfo["nnz_blocks_total"]
     B = torch.as_tensor(P.B).to(dev) if rank == 0 else torch.zeros((P.K, N), dtype=torch.float16,
                                                                     device=dev)
     b_bcast_ms = None
@@ -408,9 +401,7 @@ def run_gpu(args):
     def e2e_step():
         if rank == 0:
             B.copy_(h_B, non_blocking=True)
-        if world > 1:
-            broadcast_b(B, src=0)
-        shard.execute(B, C, N)
+        shard.execute(B, C, N, bcast_root=0 if world > 1 else -1)  # B broadcast by the library
         h_C.copy_(C, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -427,11 +418,14 @@ def run_gpu(args):
     e2e_h2d = int(P.K * N * 2)  # B, once per step (rank 0)
     e2e_d2h = int(rsum(shard.num_rows * N * 4))
 
-    per_rank_blocks = int(shard.nnz_blocks)
+    per_rank_blocks = int(sinfo["nnz_blocks"])
     blocks_all = [int(x) for x in ([per_rank_blocks] if world == 1 else
                                    _gather_ints(dist, dev, per_rank_blocks, world))]
+    bytes_all = [int(x) for x in ([sinfo["device_bytes"]] if world == 1 else
+                                  _gather_ints(dist, dev, int(sinfo["device_bytes"]), world))]
     launches_all = int(rsum(launches))
     shard.close()
+    comm.close()
 
     if rank != 0:
         barrier()
@@ -442,7 +436,7 @@ def run_gpu(args):
     padded = 2.0 * nnzb * 256 * N
     alg_bytes = P.nnz * (4 + 2) + (P.M + 1) * 4 + P.K * N * 2 + P.M * N * 4
     achieved = alg_bytes / (ms * 1e-3) / 1e9
-    plan_ms = clustering_ms + permutation_ms + conversion_ms + shard_prep_ms
+    plan_ms = plan_build_ms
     out = {
         "metric": METRIC,
         "value": round(flops / (ms * 1e-3) / 1e12, 5),
@@ -457,9 +451,12 @@ def run_gpu(args):
         "dtype": "f16",
         "data": "synthetic (seeded generator of the config; no dataset)",
         "config": _config(args, P, label, N, world),
-        "clustering_plus_conversion_ms": round(clustering_ms + permutation_ms + conversion_ms, 3),
-        "plan_ms": {"clustering": round(clustering_ms, 3), "permutation": round(permutation_ms, 3),
-                    "conversion": round(conversion_ms, 3), "shard_prep": round(shard_prep_ms, 3)},
+        "clustering_plus_conversion_ms": round(plan_build_ms, 3),
+        "plan_ms": {"clustering": round(clustering_ms, 3),
+                    "plan_build": round(plan_build_ms, 3),
+                    "note": "plan_build = the rank's xspmm_dist_plan_csr call: clustering, "
+                            "permutation, block count, its own block rows' BCSR, product set-up "
+                            "(max over ranks); clustering = the clustering call alone"},
         "nnzb_after_clustering": nnzb,
         "padded_tflops": round(padded / (ms * 1e-3) / 1e12, 4),
         "padded_frac_of_bf16_peak": round(padded / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 5),
@@ -479,6 +476,7 @@ def run_gpu(args):
                 "d2h_bytes_per_step": e2e_d2h},
         "b_broadcast_ms": None if b_bcast_ms is None else round(b_bcast_ms, 4),
         "per_rank_blocks": blocks_all,
+        "per_rank_plan_device_bytes": bytes_all,
         "c_check": {"sampled_rows": chk_rows, "max_rel_guarded": chk_err, "tol": 1e-3,
                     "reference": "fp64 product of the host CSR rows"},
         "gpu_launches": launches_all,

@@ -19,11 +19,13 @@
 // Before the MMA kernel, the 8 blocks of every union entry are packed into one contiguous
 // 128 x 16 tile (zeros for missing blocks), already in the shared-memory image of the K-major
 // SWIZZLE_32B canonical layout, so one plain bulk copy stages it (a tensor map with 32-byte rows
-// would split it into 128 requests). A pipeline stage holds two union entries: their two A tiles
-// (one 8 KB bulk copy -- consecutive entries are adjacent) and their two 16 x 256 B slabs (one
+// would split it into 128 requests). A pipeline stage holds four union entries: their four A tiles
+// (one 16 KB bulk copy -- consecutive entries are adjacent) and their four 16 x 256 B slabs (one
 // 3-D box each when N % 64 == 0, else four 64-column SWIZZLE_128B boxes; MN-major canonical
-// layout). Two MMAs per stage share one tcgen05.commit: a commit after every 16-deep MMA leaves
-// the tensor pipe idle about half of the time.
+// layout). The MMAs of a stage share one tcgen05.commit: with one CTA per SM every stage costs the
+// issuing thread a wait and a commit, and four MMAs per stage ran 1.35x faster than two (pruned
+// LLM, N = 4096) -- a commit after every 16-deep MMA leaves the tensor pipe idle about half of the
+// time.
 //
 // Accumulation. The tensor core's accumulation into an fp32 TMEM accumulator is not specified to
 // round like IEEE FADD, and a single accumulator carried over the hundreds of union entries of a
@@ -61,13 +63,13 @@ namespace {
 
 constexpr int TC_GROUP = 8;                        // block rows per tile (M = 128)
 constexpr int TC_BN = 256;                         // columns per tile = the MMA's N
-constexpr int TC_KPS = 2;                          // union entries (MMAs) per stage
-constexpr int TC_STAGES = 9;
+constexpr int TC_KPS = 4;                          // union entries (MMAs) per stage
+constexpr int TC_STAGES = 3;
 constexpr int A_TILE = TC_GROUP * 512;             // 4 KB: one union entry's stacked A
 constexpr int B_BOX = 16 * 128;                    // 16 rows x 64 fp16 = 2 KB
 constexpr int B_SLAB = (TC_BN / 64) * B_BOX;       // 8 KB: one union entry's B rows
-constexpr int A_STAGE = TC_KPS * A_TILE;           // 8 KB
-constexpr int STAGE_BYTES = TC_KPS * (A_TILE + B_SLAB);  // 24 KB (multiple of 1024)
+constexpr int A_STAGE = TC_KPS * A_TILE;           // 16 KB
+constexpr int STAGE_BYTES = TC_KPS * (A_TILE + B_SLAB);  // 48 KB (multiple of 1024)
 constexpr int TC_PRODUCERS = 3;                   // warps 1..3 issue the loads
 constexpr int TC_FLUSHERS = 8;                    // warps 4..11 sum the TMEM partials, store C
 constexpr int TC_FIRST_FLUSHER = 1 + TC_PRODUCERS;
@@ -262,8 +264,7 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
     const uint32_t tmem = *tmem_slot;
 
     // Stage j holds union entries j*KPS .. j*KPS+KPS-1 (fewer in the last stage): one MMA each,
-    // and one commit per stage -- a commit after every 16-deep MMA leaves the tensor pipe idle
-    // about half the time. Union entries form groups of TC_FLUSH_G; group t accumulates into
+    // and one commit per stage. Union entries form groups of TC_FLUSH_G; group t accumulates into
     // TMEM accumulator t % 2 from zero, and the flushers add it to their running sums while the
     // next group accumulates into the other one.
     const int nst = (nk + TC_KPS - 1) / TC_KPS;
