@@ -110,9 +110,17 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------
 # workloads (synthetic, seeded)
 # ------------------------------------------------------------------------------------------------
-def _workload(name):
-    """(label, N, full-size problem factory, CPU-sample factory, sample description)."""
+def _workload(name, rows_log2=0):
+    """(label, N, problem factory, CPU-sample factory, sample description). rows_log2 > 0 builds
+    the banded / R-MAT generator at 2^rows_log2 rows instead of full size (profiling cases)."""
     from xspmm_b200 import synth
+    if name == "cfg5" and rows_log2:
+        return (f"cfg5_gnn_rmat_2^{rows_log2}", 128,
+                lambda N: synth.cfg5_rmat(scale=rows_log2, N=N),
+                lambda N: synth.cfg5_rmat(scale=15, N=N), "R-MAT 2^15 rows, seed 42")
+    if name == "cfg4" and rows_log2:
+        return (f"cfg4_banded_2^{rows_log2}", 64, lambda N: synth.cfg4_banded(n=1 << rows_log2, N=N),
+                lambda N: synth.cfg4_banded(n=1 << 15, N=N), "banded 2^15 rows, seed 42")
     if name == "cfg5":
         return ("cfg5_gnn_rmat_2^20", 128, lambda N: synth.cfg5_rmat(N=N),
                 lambda N: synth.cfg5_rmat(scale=15, N=N),
@@ -249,7 +257,7 @@ def run_gpu(args):
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
-    label, N0, make, _, _ = _workload(args.workload)
+    label, N0, make, _, _ = _workload(args.workload, args.rows_log2)
     N = args.n_cols or N0
     P = make(N)  # every rank builds the same seeded matrix on its host
     ex = xs.CudaExecutor(local)
@@ -362,9 +370,11 @@ def run_gpu(args):
     wall0 = time.perf_counter()
     for i in range(args.steps):
         flush.fill_(float(i))
+        torch.cuda.nvtx.range_push("timed_step")  # ncu --nvtx --nvtx-include timed_step/
         starts[i].record(stream)
         shard.execute(B, C, N)
         ends[i].record(stream)
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     wall = time.perf_counter() - wall0
@@ -509,7 +519,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    label, N0, make, make_sample, desc = _workload(args.workload)
+    label, N0, make, make_sample, desc = _workload(args.workload, args.rows_log2)
     N = args.n_cols or N0
     P = make(N)  # the full workload, for the config description only
     S = make_sample(N)
@@ -792,6 +802,8 @@ def main():
     ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg2"], default="cfg5",
                     help="cfg5: GNN R-MAT 2^20 (the largest single-GPU config); cfg4: banded 2M")
     ap.add_argument("--n-cols", type=int, default=0, help="N (default: the config's)")
+    ap.add_argument("--rows-log2", type=int, default=0,
+                    help="cfg4/cfg5 at 2^k rows instead of full size (small profiling cases)")
     ap.add_argument("--tier2-steps", type=int, default=2,
                     help="timed one-call Tier-2 pipelines (rank 0), after one warm-up")
     ap.add_argument("--cpu-budget", type=float, default=10.0)

@@ -83,13 +83,18 @@ struct SparseChunk {
     int64_t e0, e1;  // nonzeros [e0, e1) of row `row`, partial sum into workspace slot `slot`
     int32_t row, slot;
 };
+struct SpRow {  // a row of the gather kernels with at most SP_LONG nonzeros
+    int64_t e0;   // its first nonzero
+    int32_t row, cnt;
+};
 struct SparseRows {
     std::vector<uint8_t> dense_br;
     std::vector<int64_t> host_rp;  // the block row pointers, read back once at build
     DevBuf<int64_t> rptr;  // [M+1]: row r's nonzeros are [rptr[r], rptr[r+1]) (empty if dense)
     DevBuf<int32_t> col;
     DevBuf<uint8_t> val;   // nnz values of the matrix's value type
-    DevBuf<int32_t> brs, short_rows, long_rows;
+    DevBuf<int32_t> brs, long_rows;
+    DevBuf<SpRow> short_rows;
     DevBuf<SparseChunk> chunks;    // long rows cut into chunks
     DevBuf<int32_t> long_first;    // [nlong+1] first chunk of each long row
     int64_t nbrs = 0, nnz = 0, nshort = 0, nlong = 0, nchunks = 0;

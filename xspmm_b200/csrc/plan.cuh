@@ -61,8 +61,9 @@ struct Plan final : PlanBase {
                (int64_t)bv.n * (int64_t)sizeof(VT) +
                (int64_t)(sparse.rptr.n * sizeof(int64_t) + sparse.col.n * sizeof(int32_t) +
                          sparse.val.n +
-                         (sparse.brs.n + sparse.short_rows.n + sparse.long_rows.n +
-                          sparse.long_first.n) * sizeof(int32_t) +
+                         (sparse.brs.n + sparse.long_rows.n + sparse.long_first.n) *
+                             sizeof(int32_t) +
+                         sparse.short_rows.n * sizeof(SpRow) +
                          sparse.chunks.n * sizeof(SparseChunk)) +
                (int64_t)(f32work.pieces.n * sizeof(F32Piece) +
                          (f32work.long_br.n + f32work.long_first.n) * sizeof(int32_t)) +

@@ -30,6 +30,7 @@ constexpr int SP_TN = 128;          // columns per warp (4 per lane)
 constexpr int SP_WARPS = 8;
 constexpr int64_t SP_LONG = 256;    // rows with more nonzeros are cut into chunks
 constexpr int64_t SP_CHUNK = 2048;  // nonzeros per chunk of a long row
+constexpr int SP_UNROLL = 8;        // B rows in flight per warp
 
 // Value-type helpers: 8 consecutive block values of a lane (one 16x16 block row-major: lane l
 // holds row l/2, columns (l&1)*8 .. +7), the nonzero test (the sign bit ignored, so -0 counts as
@@ -49,6 +50,14 @@ template <> struct SpVT<__half> {
         o[0] = f0.x; o[1] = f0.y; o[2] = f1.x; o[3] = f1.y;
     }
     static constexpr int b4_align = 8;
+    using Raw = uint2;  // 4 consecutive elements of a B row, as loaded
+    __device__ static Raw raw4(const __half* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
+    __device__ static Raw zero4() { return make_uint2(0u, 0u); }
+    __device__ static void f4(const Raw& x, float (&o)[4]) {
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&x.x));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&x.y));
+        o[0] = f0.x; o[1] = f0.y; o[2] = f1.x; o[3] = f1.y;
+    }
 };
 template <> struct SpVT<float> {
     __device__ static void load8(const float* p, float (&o)[8]) {
@@ -64,6 +73,12 @@ template <> struct SpVT<float> {
         o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w;
     }
     static constexpr int b4_align = 16;
+    using Raw = float4;
+    __device__ static Raw raw4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+    __device__ static Raw zero4() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+    __device__ static void f4(const Raw& x, float (&o)[4]) {
+        o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w;
+    }
 };
 
 // Per-row nonzero counts (rows of block row br = 16 br .. 16 br + 15), a warp per block row:
@@ -129,50 +144,62 @@ __global__ void sp_extract_kernel(const IT* __restrict__ rp, const IT* __restric
     }
 }
 
-// C[map(r), tile] for rows with at most SP_LONG nonzeros: a warp per (row, 128-column tile).
+// C[map(r), tile] for rows with at most SP_LONG nonzeros: a warp per (row, 128-column tile). The
+// row's descriptor (first nonzero, count, row) is one 16-byte load, so the chain of dependent
+// loads before the B rows is descriptor -> (column, value) pairs -> B rows. The warp loads 32
+// pairs at once (coalesced), broadcasts them and keeps SP_UNROLL B rows in flight (raw fp16 in
+// registers until they are used); nonzeros are still added in column order, in fp64.
 template <typename VT, typename IT, bool VEC>
-__global__ void __launch_bounds__(SP_WARPS * 32)
-sp_gather_short_kernel(const int32_t* __restrict__ rows, int64_t nrows,
-                       const int64_t* __restrict__ rptr, const int32_t* __restrict__ col,
-                       const VT* __restrict__ val, const VT* __restrict__ B,
-                       float* __restrict__ C, const IT* __restrict__ row_map, int64_t M,
-                       int64_t K, int64_t N, unsigned* __restrict__ err) {
+__global__ void __launch_bounds__(SP_WARPS * 32, sizeof(VT) == 2 ? 4 : 2)
+sp_gather_short_kernel(const SpRow* __restrict__ rows, int64_t nrows,
+                       const int32_t* __restrict__ col, const VT* __restrict__ val,
+                       const VT* __restrict__ B, float* __restrict__ C,
+                       const IT* __restrict__ row_map, int64_t M, int64_t K, int64_t N,
+                       unsigned* __restrict__ err) {
     const int lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * SP_WARPS + (threadIdx.x >> 5);
     if (t >= nrows) return;
-    const int64_t r = rows[t];
+    const SpRow ri = rows[t];
+    const int64_t r = ri.row, e0 = ri.e0;
+    const int n_all = ri.cnt;
     const int64_t n0 = (int64_t)blockIdx.y * SP_TN + lane * 4;
     double acc[4] = {0.0, 0.0, 0.0, 0.0};
-    const int64_t e0 = rptr[r], e1 = rptr[r + 1];
-    // the warp loads 32 (column, value) pairs at once (coalesced), then broadcasts them and keeps
-    // four B rows in flight; nonzeros are still added in column order
-    for (int64_t base = e0; base < e1; base += 32) {
-        const int cnt = (int)min((int64_t)32, e1 - base);
-        const int64_t my_c = lane < cnt ? (int64_t)col[base + lane] : 0;
-        const float my_a = lane < cnt ? SpVT<VT>::f(val[base + lane]) : 0.0f;
-        for (int u0 = 0; u0 < cnt; u0 += 4) {
-            float bb[4][4];
-            float a[4];
+    for (int base = 0; base < n_all; base += 32) {
+        const int cnt = min(32, n_all - base);
+        const int64_t my_c = lane < cnt ? (int64_t)col[e0 + base + lane] : 0;
+        const float my_a = lane < cnt ? SpVT<VT>::f(val[e0 + base + lane]) : 0.0f;
+        for (int u0 = 0; u0 < cnt; u0 += SP_UNROLL) {
+            typename SpVT<VT>::Raw raw[SP_UNROLL];
+            float a[SP_UNROLL];
+            bool lv[SP_UNROLL];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < SP_UNROLL; ++u) {
                 const int64_t c = __shfl_sync(0xffffffffu, my_c, (u0 + u) & 31);
                 a[u] = __shfl_sync(0xffffffffu, my_a, (u0 + u) & 31);
-                const bool live = u0 + u < cnt && c < K;
+                lv[u] = u0 + u < cnt && c < K;
                 const VT* src = B + c * N + n0;
-                if (VEC && live && n0 + 4 <= N) {
-                    SpVT<VT>::b4(src, bb[u]);
+                if (VEC && lv[u] && n0 + 4 <= N) {
+                    raw[u] = SpVT<VT>::raw4(src);
                 } else {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        bb[u][q] = (live && n0 + q < N) ? SpVT<VT>::f(src[q]) : 0.0f;
+                    raw[u] = SpVT<VT>::zero4();
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < SP_UNROLL; ++u) {
                 if (u0 + u < cnt) {
+                    float bb[4];
+                    if (VEC) {
+                        SpVT<VT>::f4(raw[u], bb);
+                    } else {
+                        const int64_t c = __shfl_sync(0xffffffffu, my_c, (u0 + u) & 31);
+                        const VT* src = B + c * N + n0;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            bb[q] = (lv[u] && n0 + q < N) ? SpVT<VT>::f(src[q]) : 0.0f;
+                    }
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
-                        acc[q] = fma((double)a[u], (double)bb[u][q], acc[q]);
+                        acc[q] = fma((double)a[u], (double)bb[q], acc[q]);
                 }
             }
         }
@@ -215,28 +242,35 @@ sp_gather_chunk_kernel(const SparseChunk* __restrict__ chunks, const int32_t* __
         const int cnt = (int)min((int64_t)32, w1 - base);
         const int64_t my_c = lane < cnt ? (int64_t)col[base + lane] : 0;
         const float my_a = lane < cnt ? SpVT<VT>::f(val[base + lane]) : 0.0f;
-        for (int u0 = 0; u0 < cnt; u0 += 4) {
-            float bb[4][4];
-            float a[4];
+        for (int u0 = 0; u0 < cnt; u0 += SP_UNROLL) {
+            typename SpVT<VT>::Raw raw[SP_UNROLL];
+            float a[SP_UNROLL];
+            bool lv[SP_UNROLL];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < SP_UNROLL; ++u) {
                 const int64_t c = __shfl_sync(0xffffffffu, my_c, (u0 + u) & 31);
                 a[u] = __shfl_sync(0xffffffffu, my_a, (u0 + u) & 31);
-                const bool live = u0 + u < cnt && c < K;
-                const VT* src = B + c * N + n0;
-                if (VEC && live && n0 + 4 <= N) {
-                    SpVT<VT>::b4(src, bb[u]);
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        bb[u][q] = (live && n0 + q < N) ? SpVT<VT>::f(src[q]) : 0.0f;
-                }
+                lv[u] = u0 + u < cnt && c < K;
+                raw[u] = (VEC && lv[u] && n0 + 4 <= N) ? SpVT<VT>::raw4(B + c * N + n0)
+                                                        : SpVT<VT>::zero4();
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                if (u0 + u < cnt)
+            for (int u = 0; u < SP_UNROLL; ++u) {
+                if (u0 + u < cnt) {
+                    float bb[4];
+                    if (VEC) {
+                        SpVT<VT>::f4(raw[u], bb);
+                    } else {
+                        const int64_t c = __shfl_sync(0xffffffffu, my_c, (u0 + u) & 31);
+                        const VT* src = B + c * N + n0;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) acc[q] = fma((double)a[u], (double)bb[u][q], acc[q]);
+                        for (int q = 0; q < 4; ++q)
+                            bb[q] = (lv[u] && n0 + q < N) ? SpVT<VT>::f(src[q]) : 0.0f;
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc[q] = fma((double)a[u], (double)bb[q], acc[q]);
+                }
+            }
         }
     }
 #pragma unroll
@@ -306,7 +340,7 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
     // Block rows averaging at most dense_nnz nonzeros per block go to the gather kernels
     // (block rows with no block stay: the block kernels write their zeros); rptr is a prefix
     // over all rows, with empty ranges for the rows left on the block kernels.
-    std::vector<int32_t> brs, short_rows, long_rows;
+    std::vector<int32_t> brs, short_ids, long_rows;
     std::vector<int64_t> rptr(M + 1, 0);
     for (int64_t br = 0; br < nbr; ++br) {
         const int64_t nb = (int64_t)hrp[br + 1] - (int64_t)hrp[br];
@@ -318,7 +352,7 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
         if (sparse) {
             brs.push_back((int32_t)br);
             for (int64_t r = r0; r < r1; ++r)
-                (cnt[r] > SP_LONG ? long_rows : short_rows).push_back((int32_t)r);
+                (cnt[r] > SP_LONG ? long_rows : short_ids).push_back((int32_t)r);
         }
         for (int64_t r = r0; r < r1; ++r) rptr[r + 1] = rptr[r] + (sparse ? cnt[r] : 0);
     }
@@ -333,13 +367,18 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
     long_first.push_back((int32_t)chunks.size());
     out.nbrs = (int64_t)brs.size();
     out.nnz = rptr[M];
+    std::vector<SpRow> short_rows(short_ids.size());
+    for (size_t i = 0; i < short_ids.size(); ++i) {
+        const int32_t r = short_ids[i];
+        short_rows[i] = SpRow{rptr[r], r, (int32_t)(rptr[r + 1] - rptr[r])};
+    }
     out.nshort = (int64_t)short_rows.size();
     out.nlong = (int64_t)long_rows.size();
     out.nchunks = (int64_t)chunks.size();
     if (out.nbrs == 0) return;
     out.rptr = DevBuf<int64_t>(M + 1, s);
     out.brs = DevBuf<int32_t>(brs.size(), s);
-    out.short_rows = DevBuf<int32_t>(std::max<size_t>(short_rows.size(), 1), s);
+    out.short_rows = DevBuf<SpRow>(std::max<size_t>(short_rows.size(), 1), s);
     out.long_rows = DevBuf<int32_t>(std::max<size_t>(long_rows.size(), 1), s);
     out.col = DevBuf<int32_t>(std::max<int64_t>(out.nnz, 1), s);
     out.val = DevBuf<uint8_t>(std::max<int64_t>(out.nnz, 1) * sizeof(VT), s);
@@ -349,7 +388,7 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
                                   cudaMemcpyHostToDevice, s));
     if (!short_rows.empty())
         XS_CHECK_CUDA(cudaMemcpyAsync(out.short_rows.get(), short_rows.data(),
-                                      short_rows.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+                                      short_rows.size() * sizeof(SpRow), cudaMemcpyHostToDevice, s));
     if (!long_rows.empty()) {
         XS_CHECK_CUDA(cudaMemcpyAsync(out.long_rows.get(), long_rows.data(),
                                       long_rows.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
@@ -380,12 +419,12 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C,
         dim3 grid((unsigned)ceil_div(sp.nshort, SP_WARPS), (unsigned)ntiles);
         if (vec)
             sp_gather_short_kernel<VT, IT, true><<<grid, SP_WARPS * 32, 0, h.stream>>>(
-                sp.short_rows.get(), sp.nshort, sp.rptr.get(), sp.col.get(), val, B, C,
-                map, M, K, N, h.d_err);
+                sp.short_rows.get(), sp.nshort, sp.col.get(), val, B, C, map, M, K, N,
+                h.d_err);
         else
             sp_gather_short_kernel<VT, IT, false><<<grid, SP_WARPS * 32, 0, h.stream>>>(
-                sp.short_rows.get(), sp.nshort, sp.rptr.get(), sp.col.get(), val, B, C,
-                map, M, K, N, h.d_err);
+                sp.short_rows.get(), sp.nshort, sp.col.get(), val, B, C, map, M, K, N,
+                h.d_err);
         after_launch(h, "sparse_gather_short");
     }
     if (sp.nlong > 0) {
