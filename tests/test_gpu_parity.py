@@ -139,9 +139,9 @@ def test_unpermute_bit_exact(executor, idx):
 # Tier-1 SpMM -- within tolerance of the fp64 restatement
 # ------------------------------------------------------------------------------------------------
 def _tier1_check(executor, M, K, N, rp, ci, v, vdt, idx, seed=0, long_rows=False):
-    """long_rows: also accept up to twice the error of an IEEE fp32 emulation of the reference's
-    block loop. The guarded floor of 1e-3*rms asks for absolute errors below ~1e-6*rms, which
-    fp32 accumulation over thousands of terms cannot give (the reference's WMMA path included)."""
+    """C against the fp64 oracle at the fixed bar (1e-3 fp16, 1e-5 fp32, guarded metric).
+    long_rows: the error of an IEEE fp32 emulation of the reference's block loop is computed for
+    the record (printed), not used as a bound."""
     rng = np.random.default_rng(seed)
     B = rng.standard_normal((K, N)).astype(vdt)
     A = _csr(executor, M, K, rp, ci, v, idx, vdt)
@@ -153,12 +153,11 @@ def _tier1_check(executor, M, K, N, rp, ci, v, vdt, idx, seed=0, long_rows=False
     ref = oracle.bcsr_spmm_f64(M, K, N, brp, bci, bv, B)
     e = errors(ref, _np(C), floor_rel=TOL[np.dtype(vdt)])
     assert np.isfinite(_np(C)).all(), "C not fully written"
-    bound = TOL[np.dtype(vdt)]
-    if long_rows and e["max_rel_guarded"] > bound:
+    if long_rows:
         e32 = errors(ref, fp32_block_emulation(M, N, brp, bci, bv, B), TOL[np.dtype(vdt)])
         e["fp32_emulation_guarded"] = e32["max_rel_guarded"]
-        bound = max(bound, 2.0 * e32["max_rel_guarded"])
-    assert e["max_rel_guarded"] <= bound, e
+        print("long rows:", e)
+    assert e["max_rel_guarded"] <= TOL[np.dtype(vdt)], e
     return e
 
 

@@ -31,9 +31,10 @@ def _oracle_tier2(P, B, clustering):
 
 
 def _close(ref, emu, got):
+    """Fixed bar 1e-3 (guarded); the IEEE fp32 emulation's error is reported, not a bound."""
     e = errors(ref, got, 1e-3)
-    bound = max(1e-3, 2.0 * errors(ref, emu, 1e-3)["max_rel_guarded"])
-    assert e["max_rel_guarded"] <= bound, e
+    e["fp32_emulation_guarded"] = errors(ref, emu, 1e-3)["max_rel_guarded"]
+    assert e["max_rel_guarded"] <= 1e-3, e
 
 
 @pytest.mark.parametrize("index_dtype", [torch.int32, torch.int64])

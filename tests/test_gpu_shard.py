@@ -11,7 +11,7 @@ import torch.multiprocessing as mp
 
 import oracle
 import xspmm_b200 as xs
-from tests.util import errors, fp32_block_emulation
+from tests.util import errors
 from xspmm_b200 import synth
 from xspmm_b200.shard import BlockRowShard, broadcast_b, partition_block_rows
 
@@ -24,9 +24,8 @@ def _problem():
 
 def _check(P, brp, bci, bv, got, perm=None):
     ref = oracle.bcsr_spmm_f64(P.M, P.K, P.N, brp, bci, bv, P.B)
-    emu = fp32_block_emulation(P.M, P.N, brp, bci, bv, P.B)
     e = errors(ref, got, 1e-3)
-    assert e["max_rel_guarded"] <= max(1e-3, 2.0 * errors(ref, emu, 1e-3)["max_rel_guarded"]), e
+    assert e["max_rel_guarded"] <= 1e-3, e
 
 
 @pytest.mark.parametrize("parts", [1, 3, 8])
