@@ -43,6 +43,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "SpMM effective TFLOPS (2*nnz*N/s) at 1/2/4/8 B200; clustering+convert ms"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) of one Tier-1 product, summed over its launches, from a one-pass ncu
+# capture of this bench at full size on one B200 (profiles/tier1_gather_cfg5.md, which gives the
+# command); keyed by (workload, N, ranks). Other workloads report null.
+TRAFFIC = {("cfg5_gnn_rmat_2^20", 128, 1): None}
 
 
 def peaks():
@@ -403,28 +407,52 @@ def run_gpu(args):
     chk_rows = int(rsum(chk["rows"]))
 
     # ---- end to end: B up (rank 0, pinned) + broadcast, product, local C rows down --------------
+    # Every step uploads its B from pinned host memory, runs the product (the library broadcasts
+    # B to the other ranks) and downloads its C rows to pinned host memory. Steps are pipelined
+    # the way a serving loop double-buffers: step i's download (device -> host) overlaps step
+    # i+1's upload (host -> device, the other PCIe direction) and product, on three streams with
+    # two device buffers each for B and C. The interval runs from before the first upload to the
+    # end of the last download; B (K x N fp16) and C are larger than L2, so no flush is needed.
     h_B = torch.from_numpy(P.B).pin_memory() if rank == 0 else None
-    h_C = torch.empty((max(shard.num_rows, 1), N), dtype=torch.float32).pin_memory()
-    es = [ev() for _ in range(args.steps)]
-    ee = [ev() for _ in range(args.steps)]
+    Bs = [B, torch.empty_like(B)]
+    Cs = [C, torch.empty_like(C)]
+    h_Cs = [torch.empty((max(shard.num_rows, 1), N), dtype=torch.float32).pin_memory()
+            for _ in range(2)]
+    s_up, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
-    def e2e_step():
-        if rank == 0:
-            B.copy_(h_B, non_blocking=True)
-        shard.execute(B, C, N, bcast_root=0 if world > 1 else -1)  # B broadcast by the library
-        h_C.copy_(C, non_blocking=True)
+    def e2e_run(nsteps):
+        up = [ev() for _ in range(nsteps)]
+        comp = [ev() for _ in range(nsteps)]
+        dn = [ev() for _ in range(nsteps)]
+        t0, t1 = ev(), ev()
+        t0.record(stream)
+        s_up.wait_event(t0)
+        for i in range(nsteps):
+            b = i % 2
+            with torch.cuda.stream(s_up):
+                if i >= 2:
+                    s_up.wait_event(comp[i - 2])  # step i-2's product has read B[b]
+                if rank == 0:
+                    Bs[b].copy_(h_B, non_blocking=True)
+                up[i].record(s_up)
+            stream.wait_event(up[i])
+            if i >= 2:
+                stream.wait_event(dn[i - 2])  # step i-2's download has read C[b]
+            shard.execute(Bs[b], Cs[b], N, bcast_root=0 if world > 1 else -1)
+            comp[i].record(stream)
+            with torch.cuda.stream(s_dn):
+                s_dn.wait_event(comp[i])
+                h_Cs[b].copy_(Cs[b], non_blocking=True)
+                dn[i].record(s_dn)
+        stream.wait_event(dn[nsteps - 1])
+        t1.record(stream)
+        t1.synchronize()
+        return t0.elapsed_time(t1) / nsteps
 
-    for _ in range(args.warmup):
-        e2e_step()
+    e2e_run(max(args.warmup, 2))
     torch.cuda.synchronize()
     barrier()
-    for i in range(args.steps):
-        flush.fill_(float(i))
-        es[i].record(stream)
-        e2e_step()
-        ee[i].record(stream)
-        ee[i].synchronize()
-    e2e_ms = rmax(sum(s_.elapsed_time(e_) for s_, e_ in zip(es, ee)) / args.steps)
+    e2e_ms = rmax(e2e_run(args.steps))
     e2e_h2d = int(P.K * N * 2)  # B, once per step (rank 0)
     e2e_d2h = int(rsum(shard.num_rows * N * 4))
 
@@ -443,6 +471,19 @@ def run_gpu(args):
             dist.destroy_process_group()
         return
     pk = peaks()
+    if tier2 is not None:
+        # Bandwidth of the two data-movement stages of that Tier-2 call (algorithmic bytes: each
+        # array read once and written once). Permutation: CSR in (row_ptr, 4 B index + 2 B value
+        # per nonzero) and out, plus perm. Conversion: the permuted CSR in, the BCSR out (16 x 16
+        # fp16 blocks, block column indices, block row pointers).
+        perm_b = 2 * (P.nnz * 6 + (P.M + 1) * 4) + P.M * 4
+        conv_b = P.nnz * 6 + (P.M + 1) * 4 + nnzb * (512 + 4) + ((P.M + 15) // 16 + 1) * 4
+        sm = tier2["stages_ms"]
+        tier2["stage_bandwidth"] = {
+            k: {"bytes": int(b), "gbs": round(b / (sm[ms] * 1e-3) / 1e9, 1),
+                "frac_of_hbm": round(b / (sm[ms] * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+            for k, ms, b in (("permutation", "permutation_ms", perm_b),
+                             ("conversion", "conversion_ms", conv_b)) if sm.get(ms, 0) > 0}
     padded = 2.0 * nnzb * 256 * N
     alg_bytes = P.nnz * (4 + 2) + (P.M + 1) * 4 + P.K * N * 2 + P.M * N * 4
     achieved = alg_bytes / (ms * 1e-3) / 1e9
@@ -476,14 +517,18 @@ def run_gpu(args):
         "tier2": tier2,
         "roofline": {"kernel": "Tier-1 product (one plan execute)", "bound": "hbm",
                      "achieved": round(achieved, 2), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 5), "traffic": None,
+                     "frac": round(achieved / pk["hbm_gbs"], 5),
+                     "traffic": TRAFFIC.get((label, N, world)),
                      "alg_bytes": int(alg_bytes),
                      "alg_bytes_def": "A as CSR (4 B index + 2 B value per nonzero, row_ptr), "
                                       "B read once, C written once; B's gathers not counted",
                      "peak_source": pk["source"]},
         "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 5), "unit": "TFLOPS",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": e2e_h2d,
-                "d2h_bytes_per_step": e2e_d2h},
+                "d2h_bytes_per_step": e2e_d2h,
+                "schedule": "per step: B up (pinned), product, C rows down (pinned); steps "
+                            "double-buffered on 3 streams so a step's download overlaps the "
+                            "next step's upload and product; inputs larger than L2, no flush"},
         "b_broadcast_ms": None if b_bcast_ms is None else round(b_bcast_ms, 4),
         "per_rank_blocks": blocks_all,
         "per_rank_plan_device_bytes": bytes_all,
@@ -514,6 +559,9 @@ def run_reference(args):
     """The reference arm: the reference's own CPU path for this workload on the host cores, on a
     bounded sample (see cpu_baseline): its host code clusters, permutes and converts once, then
     each step is one product (oracle fp64 BCSR SpMM on all cores; the reference has none)."""
+    # torchrun sets OMP_NUM_THREADS=1 for its ranks; the arm runs on rank 0 alone and uses every
+    # core of the process (set before the oracle's OpenMP runtime is loaded)
+    os.environ["OMP_NUM_THREADS"] = str(len(os.sched_getaffinity(0)))
     import oracle
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

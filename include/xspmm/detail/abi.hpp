@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <type_traits>
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "../../xspmm_b200.h"
@@ -31,6 +32,8 @@ struct Abi;
     };
 XSPMM_ABI_ROW(__half, int32_t, f16, i32)
 XSPMM_ABI_ROW(__half, int64_t, f16, i64)
+XSPMM_ABI_ROW(__nv_bfloat16, int32_t, bf16, i32)
+XSPMM_ABI_ROW(__nv_bfloat16, int64_t, bf16, i64)
 XSPMM_ABI_ROW(float, int32_t, f32, i32)
 XSPMM_ABI_ROW(float, int64_t, f32, i64)
 #undef XSPMM_ABI_ROW

@@ -8,7 +8,8 @@
 //
 // B is K x N and C is M x N, row-major device arrays (leading dimension N), as in the reference.
 // Instantiations: In = __half or float with Out = float, Idx = int32_t or int64_t (the reference's
-// CUDA backend names the same four, src/cuda/unstructured_mtx_mul.cu:137-148). Work is enqueued on
+// CUDA backend names the same four, src/cuda/unstructured_mtx_mul.cu:137-148), and In =
+// __nv_bfloat16 (tensor-core bf16, fp32 accumulation) as an addition. Work is enqueued on
 // the executor's stream and is asynchronous, like the reference's kernel launches; Tier 2 returns
 // after its last launch and, when timings is given, after the stage events have completed.
 #pragma once
@@ -27,7 +28,8 @@
 
 namespace xspmm {
 
-// Tier 1: C = A * B for A in 16x16 BCSR. Every row of C is written.
+// Tier 1: C = A * B for A in BCSR (16x16 blocks on the tensor cores; other block shapes on a SIMT
+// kernel that computes the product the BCSR describes). Every row of C is written.
 template <typename InputType, typename OutputType, typename IndexType = int64_t>
 void spmm(const BCSRMatrix<InputType, IndexType>& A, const InputType* B, OutputType* C,
           IndexType N) {

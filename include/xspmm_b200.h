@@ -10,7 +10,8 @@
  * Index types: the reference templates every function on IndexType in {int32_t, int64_t}
  * (include/xspmm/matrix/csr.hpp:12, bcsr.hpp:12); each entry point here exists with suffix _i32
  * and _i64. Value types: __half (f16) and float (f32), the instantiations the reference's CUDA
- * backend names (src/cuda/unstructured_mtx_mul.cu:137-148).
+ * backend names (src/cuda/unstructured_mtx_mul.cu:137-148), and __nv_bfloat16 (bf16), which
+ * takes the f16 paths with the bf16 form of the tensor-core instructions (fp32 accumulation).
  *
  * The C++ API mirroring the reference (xspmm::spmm, CudaExecutor, CSRMatrix, BCSRMatrix,
  * SpMMTimings) is header-only on top of this ABI: include/xspmm/xspmm.hpp.
@@ -28,7 +29,7 @@ extern "C" {
 typedef enum xspmm_status {
     XSPMM_STATUS_OK = 0,
     XSPMM_STATUS_INVALID_ARGUMENT = 1, /* bad sizes/pointers, or a malformed CSR/permutation */
-    XSPMM_STATUS_UNSUPPORTED = 2,      /* e.g. a SpMM block size other than 16x16 */
+    XSPMM_STATUS_UNSUPPORTED = 2,      /* e.g. a plan over a BCSR whose blocks are not 16x16 */
     XSPMM_STATUS_CUDA_ERROR = 3,
     XSPMM_STATUS_OUT_OF_MEMORY = 4,
     XSPMM_STATUS_NCCL_ERROR = 5,
@@ -95,16 +96,19 @@ xspmm_status_t xspmm_memcpy_d2d(xspmm_handle_t h, void* dst, const void* src, si
 xspmm_status_t xspmm_synchronize(xspmm_handle_t h);
 
 /* ---------------------------------------------------------------------------------------------
- * Tier-1 BCSR SpMM: C = A * B with A in BCSR (16x16 blocks, row-major inside a block).
+ * Tier-1 BCSR SpMM: C = A * B with A in BCSR (r_block x c_block blocks, row-major inside a block).
  * Replaces xspmm::spmm(const BCSRMatrix&, const In* B, Out* C, N) (include/xspmm/xspmm.hpp:14-18,
  * dispatch src/xspmm.cpp:29-52, launcher src/cuda/unstructured_mtx_mul.cu:31-51, kernel
  * src/common/spmm_math.hpp:20-146).
  *   A: num_block_rows, num_block_cols, num_blocks, row_ptr[num_block_rows+1], col_ind[num_blocks],
- *      values[num_blocks*r_block*c_block]; r_block = c_block = 16 (else UNSUPPORTED -- the
- *      reference kernel hard-codes 16, src/cuda/unstructured_mtx_mul.cu:39).
+ *      values[num_blocks*r_block*c_block]. 16 x 16 blocks take the tensor-core kernels. Any other
+ *      shape (r_block, c_block >= 1) takes a SIMT kernel that sums each row in fp64, column
+ *      order, and rounds once: the reference kernel hard-codes 16 x 16
+ *      (src/cuda/unstructured_mtx_mul.cu:39) and so mis-computes other shapes; this computes the
+ *      product the BCSR describes.
  *   B: K x N row-major (ld = N); C: M x N row-major fp32 (ld = N), every row overwritten.
- *   M, K: true row counts of C and B. Pass num_block_rows*16 / num_block_cols*16 for the
- *      reference's behaviour; smaller values guard the ragged last block row / column, which the
+ *   M, K: true row counts of C and B. Pass num_block_rows*r_block / num_block_cols*c_block for
+ *      the reference's behaviour; smaller values guard the ragged last block row / column, which the
  *      reference kernel reads and writes out of bounds (src/common/spmm_math.hpp:80, :118-122).
  *   out_row_map: NULL, or int array of M entries giving the row of C that row i of A*B goes to
  *      (fuses the Tier-2 unpermute into the store). Same index type as row_ptr.
@@ -114,6 +118,14 @@ xspmm_status_t xspmm_bcsr_spmm_f16f32_i32(xspmm_handle_t h, int32_t num_block_ro
     const int32_t* row_ptr, const int32_t* col_ind, const void* values, const void* B, float* C,
     int32_t M, int32_t K, int32_t N, const int32_t* out_row_map);
 xspmm_status_t xspmm_bcsr_spmm_f16f32_i64(xspmm_handle_t h, int64_t num_block_rows,
+    int64_t num_block_cols, int64_t num_blocks, int64_t r_block, int64_t c_block,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
+    int64_t M, int64_t K, int64_t N, const int64_t* out_row_map);
+xspmm_status_t xspmm_bcsr_spmm_bf16f32_i32(xspmm_handle_t h, int32_t num_block_rows,
+    int32_t num_block_cols, int32_t num_blocks, int32_t r_block, int32_t c_block,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const void* B, float* C,
+    int32_t M, int32_t K, int32_t N, const int32_t* out_row_map);
+xspmm_status_t xspmm_bcsr_spmm_bf16f32_i64(xspmm_handle_t h, int64_t num_block_rows,
     int64_t num_block_cols, int64_t num_blocks, int64_t r_block, int64_t c_block,
     const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
     int64_t M, int64_t K, int64_t N, const int64_t* out_row_map);
@@ -151,6 +163,12 @@ xspmm_status_t xspmm_permute_rows_f16_i32(xspmm_handle_t h, int32_t M, int32_t K
     const int32_t* row_ptr, const int32_t* col_ind, const void* values, const int32_t* perm,
     int32_t* out_row_ptr, int32_t* out_col_ind, void* out_values);
 xspmm_status_t xspmm_permute_rows_f16_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const int64_t* perm,
+    int64_t* out_row_ptr, int64_t* out_col_ind, void* out_values);
+xspmm_status_t xspmm_permute_rows_bf16_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const int32_t* perm,
+    int32_t* out_row_ptr, int32_t* out_col_ind, void* out_values);
+xspmm_status_t xspmm_permute_rows_bf16_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
     const int64_t* row_ptr, const int64_t* col_ind, const void* values, const int64_t* perm,
     int64_t* out_row_ptr, int64_t* out_col_ind, void* out_values);
 xspmm_status_t xspmm_permute_rows_f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
@@ -203,6 +221,12 @@ xspmm_status_t xspmm_csr_to_bcsr_fill_f16_i32(xspmm_handle_t h, int32_t M, int32
 xspmm_status_t xspmm_csr_to_bcsr_fill_f16_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
     const int64_t* row_ptr, const int64_t* col_ind, const void* values, int64_t r_block,
     int64_t c_block, const int64_t* bcsr_row_ptr, int64_t* bcsr_col_ind, void* bcsr_values);
+xspmm_status_t xspmm_csr_to_bcsr_fill_bf16_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t r_block,
+    int32_t c_block, const int32_t* bcsr_row_ptr, int32_t* bcsr_col_ind, void* bcsr_values);
+xspmm_status_t xspmm_csr_to_bcsr_fill_bf16_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, int64_t r_block,
+    int64_t c_block, const int64_t* bcsr_row_ptr, int64_t* bcsr_col_ind, void* bcsr_values);
 xspmm_status_t xspmm_csr_to_bcsr_fill_f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
     const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t r_block,
     int32_t c_block, const int32_t* bcsr_row_ptr, int32_t* bcsr_col_ind, void* bcsr_values);
@@ -223,6 +247,10 @@ xspmm_status_t xspmm_unpermute_dense_f16_i32(xspmm_handle_t h, const void* in, v
     const int32_t* perm, int32_t M, int32_t N);
 xspmm_status_t xspmm_unpermute_dense_f16_i64(xspmm_handle_t h, const void* in, void* out,
     const int64_t* perm, int64_t M, int64_t N);
+xspmm_status_t xspmm_unpermute_dense_bf16_i32(xspmm_handle_t h, const void* in, void* out,
+    const int32_t* perm, int32_t M, int32_t N);
+xspmm_status_t xspmm_unpermute_dense_bf16_i64(xspmm_handle_t h, const void* in, void* out,
+    const int64_t* perm, int64_t M, int64_t N);
 
 /* ---------------------------------------------------------------------------------------------
  * Tier-2 pipeline: C = A * B for A in CSR, with optional clustering. Replaces
@@ -232,7 +260,10 @@ xspmm_status_t xspmm_unpermute_dense_f16_i64(xspmm_handle_t h, const void* in, v
  *   A'' = csr_to_bcsr(A', 16, 16); C[perm[i]] = (A'' * B)[i]  (the unpermute is fused into the
  *   SpMM store, so unpermutation_ms reports 0 and no M x N temporary is allocated).
  *   enable_clustering == 0: C = csr_to_bcsr(A) * B.
- * hw_block_size must be 16 (UNSUPPORTED otherwise). timings may be NULL; when given, the call
+ * hw_block_size (>= 1) is the clustering's column block width, as in the reference; the product
+ * always runs on 16 x 16 blocks, so C = A * B for every width (the reference converts to
+ * hw x hw blocks, :102, and reads them as 16 x 16, so its C is wrong for hw != 16). timings may
+ * be NULL; when given, the call
  * synchronizes at the end of every stage to read its events, like the reference
  * (src/cuda/unstructured_mtx_mul.cu:14-26).
  * ------------------------------------------------------------------------------------------- */
@@ -240,6 +271,12 @@ xspmm_status_t xspmm_spmm_csr_f16f32_i32(xspmm_handle_t h, int32_t M, int32_t K,
     const int32_t* row_ptr, const int32_t* col_ind, const void* values, const void* B, float* C,
     int32_t N, int32_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
 xspmm_status_t xspmm_spmm_csr_f16f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
+    int64_t N, int64_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
+xspmm_status_t xspmm_spmm_csr_bf16f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, const void* B, float* C,
+    int32_t N, int32_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
+xspmm_status_t xspmm_spmm_csr_bf16f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
     const int64_t* row_ptr, const int64_t* col_ind, const void* values, const void* B, float* C,
     int64_t N, int64_t hw_block_size, int enable_clustering, xspmm_timings_t* timings);
 xspmm_status_t xspmm_spmm_csr_f32f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
@@ -258,12 +295,13 @@ xspmm_status_t xspmm_spmm_csr_f32f32_i64(xspmm_handle_t h, int64_t M, int64_t K,
  * matrix and, where the tcgen05 kernel is chosen, A's stacked tensor-core tiles on the device.
  *
  * xspmm_plan_csr_*: the stages of xspmm_spmm_csr_* up to and including CSR->BCSR, with the same
- *   arguments (hw_block_size must be 16). build_timings (may be NULL) receives clustering_ms,
+ *   arguments (any hw_block_size >= 1). build_timings (may be NULL) receives clustering_ms,
  *   permutation_ms and conversion_ms (CSR->BCSR plus the tensor-core tile packing); spmm_ms and
  *   unpermutation_ms are 0. The caller's CSR arrays may be freed once the call returns.
- * xspmm_plan_bcsr_*: adopts a BCSR matrix for Tier-1 products (the arguments of
- *   xspmm_bcsr_spmm_*). The plan READS the caller's arrays at every product: keep them alive and
- *   unchanged until xspmm_plan_destroy.
+ * xspmm_plan_bcsr_*: adopts a BCSR matrix of 16 x 16 blocks (other shapes: UNSUPPORTED; call
+ *   xspmm_bcsr_spmm_* for them) for Tier-1 products (the arguments of xspmm_bcsr_spmm_*). The
+ *   plan READS the caller's arrays at every product: keep them alive and unchanged until
+ *   xspmm_plan_destroy.
  * xspmm_plan_execute: C (M x N, fp32, row-major, rows in the caller's order) = A * B, B (K x N,
  *   row-major) of the plan's value type. Asynchronous on the handle's stream. Results equal
  *   xspmm_spmm_csr_* / xspmm_bcsr_spmm_* on the same inputs and kernel choice.
@@ -276,7 +314,7 @@ typedef struct xspmm_plan_info {
     int64_t rows, cols;                           /* M, K */
     int64_t block_rows, block_cols, nnz_blocks;   /* the 16 x 16 BCSR matrix */
     int32_t clustered;                            /* rows permuted by the clustering */
-    int32_t value_bytes;                          /* 2 (f16) or 4 (f32) */
+    int32_t value_bytes;                          /* 2 (f16, bf16) or 4 (f32) */
     int32_t tcgen05_ready;                        /* stacked tiles for the tcgen05 kernel built */
     int32_t reserved;
     int64_t tcgen05_tiles;                        /* 128 x 16 tiles packed for it */
@@ -289,6 +327,12 @@ xspmm_status_t xspmm_plan_csr_f16f32_i32(xspmm_handle_t h, int32_t M, int32_t K,
 xspmm_status_t xspmm_plan_csr_f16f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
     const int64_t* row_ptr, const int64_t* col_ind, const void* values, int64_t hw_block_size,
     int enable_clustering, xspmm_plan_t* out, xspmm_timings_t* build_timings);
+xspmm_status_t xspmm_plan_csr_bf16f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
+    const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t hw_block_size,
+    int enable_clustering, xspmm_plan_t* out, xspmm_timings_t* build_timings);
+xspmm_status_t xspmm_plan_csr_bf16f32_i64(xspmm_handle_t h, int64_t M, int64_t K, int64_t nnz,
+    const int64_t* row_ptr, const int64_t* col_ind, const void* values, int64_t hw_block_size,
+    int enable_clustering, xspmm_plan_t* out, xspmm_timings_t* build_timings);
 xspmm_status_t xspmm_plan_csr_f32f32_i32(xspmm_handle_t h, int32_t M, int32_t K, int32_t nnz,
     const int32_t* row_ptr, const int32_t* col_ind, const void* values, int32_t hw_block_size,
     int enable_clustering, xspmm_plan_t* out, xspmm_timings_t* build_timings);
@@ -299,6 +343,12 @@ xspmm_status_t xspmm_plan_bcsr_f16f32_i32(xspmm_handle_t h, int32_t nbr, int32_t
     int32_t nnzb, int32_t r_block, int32_t c_block, const int32_t* row_ptr, const int32_t* col_ind,
     const void* values, int32_t M, int32_t K, xspmm_plan_t* out);
 xspmm_status_t xspmm_plan_bcsr_f16f32_i64(xspmm_handle_t h, int64_t nbr, int64_t nbc,
+    int64_t nnzb, int64_t r_block, int64_t c_block, const int64_t* row_ptr, const int64_t* col_ind,
+    const void* values, int64_t M, int64_t K, xspmm_plan_t* out);
+xspmm_status_t xspmm_plan_bcsr_bf16f32_i32(xspmm_handle_t h, int32_t nbr, int32_t nbc,
+    int32_t nnzb, int32_t r_block, int32_t c_block, const int32_t* row_ptr, const int32_t* col_ind,
+    const void* values, int32_t M, int32_t K, xspmm_plan_t* out);
+xspmm_status_t xspmm_plan_bcsr_bf16f32_i64(xspmm_handle_t h, int64_t nbr, int64_t nbc,
     int64_t nnzb, int64_t r_block, int64_t c_block, const int64_t* row_ptr, const int64_t* col_ind,
     const void* values, int64_t M, int64_t K, xspmm_plan_t* out);
 xspmm_status_t xspmm_plan_bcsr_f32f32_i32(xspmm_handle_t h, int32_t nbr, int32_t nbc,
@@ -340,7 +390,7 @@ xspmm_status_t xspmm_plan_destroy(xspmm_plan_t plan);
  *   timeout_ms. Every rank of the communicator must make the same execute / gather calls in the
  *   same order.
  * A timeout aborts the communicator (TIMEOUT); any NCCL error too (NCCL_ERROR); after that every
- * call on it or its plans returns NCCL_ERROR. hw_block_size must be 16.
+ * call on it or its plans returns NCCL_ERROR. hw_block_size: as for xspmm_spmm_csr_*.
  * ------------------------------------------------------------------------------------------- */
 typedef struct xspmm_dist_comm_s* xspmm_dist_comm_t;
 typedef struct xspmm_dist_plan_s* xspmm_dist_plan_t;
@@ -368,6 +418,12 @@ xspmm_status_t xspmm_dist_plan_csr_f16f32_i32(xspmm_handle_t h, xspmm_dist_comm_
     int32_t K, int32_t nnz, const int32_t* row_ptr, const int32_t* col_ind, const void* values,
     int32_t hw_block_size, int enable_clustering, double row_weight, xspmm_dist_plan_t* out);
 xspmm_status_t xspmm_dist_plan_csr_f16f32_i64(xspmm_handle_t h, xspmm_dist_comm_t comm, int64_t M,
+    int64_t K, int64_t nnz, const int64_t* row_ptr, const int64_t* col_ind, const void* values,
+    int64_t hw_block_size, int enable_clustering, double row_weight, xspmm_dist_plan_t* out);
+xspmm_status_t xspmm_dist_plan_csr_bf16f32_i32(xspmm_handle_t h, xspmm_dist_comm_t comm, int32_t M,
+    int32_t K, int32_t nnz, const int32_t* row_ptr, const int32_t* col_ind, const void* values,
+    int32_t hw_block_size, int enable_clustering, double row_weight, xspmm_dist_plan_t* out);
+xspmm_status_t xspmm_dist_plan_csr_bf16f32_i64(xspmm_handle_t h, xspmm_dist_comm_t comm, int64_t M,
     int64_t K, int64_t nnz, const int64_t* row_ptr, const int64_t* col_ind, const void* values,
     int64_t hw_block_size, int enable_clustering, double row_weight, xspmm_dist_plan_t* out);
 xspmm_status_t xspmm_dist_plan_csr_f32f32_i32(xspmm_handle_t h, xspmm_dist_comm_t comm, int32_t M,

@@ -76,3 +76,42 @@ def test_cpp_api_header_compiles_against_the_abi():
     r = subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-I" + os.path.join(ROOT, "include"),
                         "-I" + cuda_inc, src], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+_ALL_TYPES_SRC = r"""
+#include "xspmm/xspmm.hpp"
+#include "xspmm/clustering.hpp"
+#include "xspmm/plan.hpp"
+#include "xspmm/dist.hpp"
+template <typename V, typename I>
+void use(std::shared_ptr<const xspmm::Executor> exec, const xspmm::DistComm& comm, V* B, float* C) {
+    xspmm::CSRMatrix<V, I> A(exec, 4, 4, 1);
+    xspmm::SpMMTimings t;
+    xspmm::spmm(exec, A, B, C, I(8), I(8), true, &t);
+    auto Ab = xspmm::csr_to_bcsr(exec, A, I(3), I(5));
+    xspmm::spmm(Ab, B, C, I(8));
+    I* perm = nullptr;
+    xspmm::compute_1d_jaccard_clustering(exec, A, 0.5f, I(16), perm);
+    auto Ap = xspmm::apply_permutation(exec, A, perm);
+    xspmm::unpermute_dense_matrix(exec, B, B, perm, I(4), I(8));
+    xspmm::SpMMPlan<V, I> plan(exec, A, I(16), true, &t);
+    xspmm::DistPlan<V, I> dp(comm, exec, A, I(16), true);
+}
+template void use<__half, int32_t>(std::shared_ptr<const xspmm::Executor>, const xspmm::DistComm&, __half*, float*);
+template void use<__half, int64_t>(std::shared_ptr<const xspmm::Executor>, const xspmm::DistComm&, __half*, float*);
+template void use<__nv_bfloat16, int32_t>(std::shared_ptr<const xspmm::Executor>, const xspmm::DistComm&, __nv_bfloat16*, float*);
+template void use<__nv_bfloat16, int64_t>(std::shared_ptr<const xspmm::Executor>, const xspmm::DistComm&, __nv_bfloat16*, float*);
+template void use<float, int32_t>(std::shared_ptr<const xspmm::Executor>, const xspmm::DistComm&, float*, float*);
+template void use<float, int64_t>(std::shared_ptr<const xspmm::Executor>, const xspmm::DistComm&, float*, float*);
+"""
+
+
+def test_cpp_api_instantiates_every_value_and_index_type(tmp_path):
+    """Every C++ entry (Tier 1 on any block shape, Tier 2, clustering, permutation, unpermute,
+    plans, distributed plans) compiles for fp16, bf16 and fp32 values with int32 and int64
+    indices, i.e. each maps onto a declared C entry point."""
+    src = tmp_path / "all_types.cpp"
+    src.write_text(_ALL_TYPES_SRC)
+    r = subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-I" + os.path.join(ROOT, "include"),
+                        "-I/usr/local/cuda/include", str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr

@@ -281,8 +281,8 @@ def test_errors(executor):
     A = _csr(executor, 32, 32, rp, ci, v, torch.int64)
     B = torch.zeros((32, 8), dtype=torch.float16, device=executor.device)
     C = torch.zeros((32, 8), dtype=torch.float32, device=executor.device)
-    with pytest.raises(xs.XSpMMError, match="UNSUPPORTED"):
-        xs.spmm(executor, A, B, C, 8, 8, True)
+    with pytest.raises(xs.XSpMMError, match="INVALID_ARGUMENT"):
+        xs.spmm(executor, A, B, C, 8, 0, True)  # hw_block_size 0
     bad = torch.as_tensor(np.arange(32)[::-1].copy()).to(executor.device)
     bad[3] = 40
     with pytest.raises(xs.XSpMMError, match="INVALID_ARGUMENT"):

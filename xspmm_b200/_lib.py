@@ -98,14 +98,14 @@ def lib():
     L.xspmm_synchronize.argtypes = [_P]
     for suf, IT in (("i32", _I32), ("i64", _I64)):
         s = _sig(IT)
-        for vt in ("f16f32", "f32f32"):
+        for vt in ("f16f32", "bf16f32", "f32f32"):
             getattr(L, f"xspmm_bcsr_spmm_{vt}_{suf}").argtypes = s["bcsr_spmm"]
             getattr(L, f"xspmm_spmm_csr_{vt}_{suf}").argtypes = s["pipeline"]
             getattr(L, f"xspmm_plan_csr_{vt}_{suf}").argtypes = s["plan_csr"]
             getattr(L, f"xspmm_plan_bcsr_{vt}_{suf}").argtypes = s["plan_bcsr"]
         getattr(L, f"xspmm_cluster_jaccard_{suf}").argtypes = s["cluster"]
         getattr(L, f"xspmm_csr_to_bcsr_count_{suf}").argtypes = s["count"]
-        for v in ("f16", "f32"):
+        for v in ("f16", "bf16", "f32"):
             getattr(L, f"xspmm_permute_rows_{v}_{suf}").argtypes = s["permute"]
             getattr(L, f"xspmm_csr_to_bcsr_fill_{v}_{suf}").argtypes = s["fill"]
             getattr(L, f"xspmm_unpermute_dense_{v}_{suf}").argtypes = s["unpermute"]
@@ -120,7 +120,7 @@ def lib():
     L.xspmm_dist_comm_wrap.argtypes = [_P, _I32, ctypes.POINTER(_P)]
     L.xspmm_dist_comm_destroy.argtypes = [_P]
     for suf, IT in (("i32", _I32), ("i64", _I64)):
-        for vt in ("f16f32", "f32f32"):
+        for vt in ("f16f32", "bf16f32", "f32f32"):
             getattr(L, f"xspmm_dist_plan_csr_{vt}_{suf}").argtypes = [
                 _P, _P, IT, IT, IT, _P, _P, _P, IT, ctypes.c_int, ctypes.c_double,
                 ctypes.POINTER(_P)]

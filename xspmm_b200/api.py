@@ -18,7 +18,7 @@ import torch
 from . import _lib
 from ._lib import XSpMMError, check, lib
 
-_VAL = {torch.float16: "f16", torch.float32: "f32"}
+_VAL = {torch.float16: "f16", torch.float32: "f32", torch.bfloat16: "bf16"}
 _IDX = {torch.int32: "i32", torch.int64: "i64"}
 _IT_C = {torch.int32: ctypes.c_int32, torch.int64: ctypes.c_int64}
 
@@ -34,6 +34,17 @@ def _torch_dtype(x, default):
         return x
     return {np.dtype(np.float16): torch.float16, np.dtype(np.float32): torch.float32,
             np.dtype(np.int32): torch.int32, np.dtype(np.int64): torch.int64}[np.dtype(x)]
+
+
+def _host_values(values, value_dtype, n):
+    """The first n values as a CPU tensor of value_dtype. numpy has no bf16: bf16 values come as
+    a torch tensor, or as float32/float16 numbers rounded to bf16 (round to nearest even)."""
+    if isinstance(values, torch.Tensor):
+        return values[:n].detach().to("cpu", value_dtype).contiguous()
+    if value_dtype == torch.bfloat16:
+        return torch.from_numpy(np.ascontiguousarray(values[:n], dtype=np.float32)).to(torch.bfloat16)
+    vt = {torch.float16: np.float16, torch.float32: np.float32}[value_dtype]
+    return torch.from_numpy(np.ascontiguousarray(values[:n], dtype=vt))
 
 
 @dataclass
@@ -118,20 +129,23 @@ class CSRMatrix:
 
     @classmethod
     def from_host(cls, exec, num_rows, num_cols, row_ptr, col_ind, values,
-                  index_dtype=torch.int64):
-        values = np.asarray(values)
+                  index_dtype=torch.int64, value_dtype=None):
+        """values: numpy (fp16/fp32) or a torch tensor (also bf16); value_dtype overrides the
+        values' own type (float numbers are rounded to it)."""
+        if value_dtype is None:
+            value_dtype = (values.dtype if isinstance(values, torch.Tensor)
+                           else _torch_dtype(np.asarray(values).dtype, torch.float16))
         m = cls(exec, num_rows, num_cols, int(row_ptr[-1]) if len(row_ptr) else 0,
-                value_dtype=_torch_dtype(values.dtype, torch.float16), index_dtype=index_dtype)
+                value_dtype=value_dtype, index_dtype=index_dtype)
         m.copy_from_host(row_ptr, col_ind, values)
         return m
 
     def copy_from_host(self, row_ptr, col_ind, values) -> None:
         it = {torch.int32: np.int32, torch.int64: np.int64}[self.index_dtype]
-        vt = {torch.float16: np.float16, torch.float32: np.float32}[self.value_dtype]
         self.row_ptr.copy_(torch.from_numpy(np.ascontiguousarray(row_ptr, dtype=it)))
         if self.nnz > 0:
             self.col_ind.copy_(torch.from_numpy(np.ascontiguousarray(col_ind[: self.nnz], dtype=it)))
-            self.values.copy_(torch.from_numpy(np.ascontiguousarray(values[: self.nnz], dtype=vt)))
+            self.values.copy_(_host_values(values, self.value_dtype, self.nnz))
 
     def get_num_rows(self): return self.num_rows
     def get_num_cols(self): return self.num_cols
@@ -168,12 +182,11 @@ class BCSRMatrix:
 
     def copy_from_host(self, row_ptr, col_ind, values) -> None:
         it = {torch.int32: np.int32, torch.int64: np.int64}[self.index_dtype]
-        vt = {torch.float16: np.float16, torch.float32: np.float32}[self.value_dtype]
         self.row_ptr.copy_(torch.from_numpy(np.ascontiguousarray(row_ptr, dtype=it)))
         if self.num_blocks > 0:
             self.col_ind.copy_(torch.from_numpy(np.ascontiguousarray(col_ind, dtype=it)))
-            self.values.copy_(torch.from_numpy(
-                np.ascontiguousarray(np.asarray(values, dtype=vt).reshape(-1))))
+            flat = values.reshape(-1) if isinstance(values, torch.Tensor) else np.asarray(values).reshape(-1)
+            self.values.copy_(_host_values(flat, self.value_dtype, self.values.numel()))
 
     def get_num_block_rows(self): return self.num_block_rows
     def get_num_block_cols(self): return self.num_block_cols
@@ -366,7 +379,7 @@ def unpermute_dense_matrix(exec: CudaExecutor, in_matrix: torch.Tensor, out_matr
                            perm: torch.Tensor, M: int, N: int) -> None:
     """include/xspmm/xspmm.hpp:35-40."""
     _check_dev(exec, in_matrix, out_matrix, perm)
-    v = {torch.float32: "f32", torch.float16: "f16"}[in_matrix.dtype]
+    v = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}[in_matrix.dtype]
     IT = _it(perm.dtype)
     check(getattr(lib(), f"xspmm_unpermute_dense_{v}_{_IDX[perm.dtype]}")(
         exec.handle, _p(in_matrix), _p(out_matrix), _p(perm), IT(M), IT(N)))

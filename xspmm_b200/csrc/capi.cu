@@ -162,23 +162,28 @@ XS_API xspmm_status_t xspmm_synchronize(xspmm_handle_t hh) {
         const void* vals, const void* B, float* C, IT M, IT K, IT N, const IT* map) {             \
         return guarded([&] {                                                                      \
             Handle& h = H(hh);                                                                    \
-            XS_REQUIRE(rb == 16 && cb == 16, XSPMM_STATUS_UNSUPPORTED,                            \
-                       "Tier-1 SpMM supports 16x16 blocks only");                                 \
+            need(rb >= 1 && cb >= 1, "block shape must be at least 1 x 1");                       \
             need(nbr >= 0 && nbc >= 0 && nnzb >= 0 && M >= 0 && K >= 0 && N >= 0,                 \
                  "negative dimension");                                                           \
-            need((int64_t)M <= (int64_t)nbr * 16 && (int64_t)K <= (int64_t)nbc * 16,              \
+            need((int64_t)M <= (int64_t)nbr * rb && (int64_t)K <= (int64_t)nbc * cb,              \
                  "M or K larger than the block grid");                                            \
-            need((int64_t)M > ((int64_t)nbr - 1) * 16, "M smaller than the block rows cover");    \
+            need((int64_t)M > ((int64_t)nbr - 1) * rb, "M smaller than the block rows cover");    \
             if (nbr == 0 || N == 0) return;                                                       \
             need(rp && C, "null row_ptr or C");                                                   \
             need(nnzb == 0 || (ci && vals && B), "null col_ind, values or B");                    \
             DeviceGuard g(h.device);                                                              \
-            bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, rp, ci, static_cast<const VT*>(vals),            \
-                              static_cast<const VT*>(B), C, M, K, N, map);                        \
+            if (rb == 16 && cb == 16)                                                             \
+                bcsr_spmm<VT, IT>(h, nbr, nbc, nnzb, rp, ci, static_cast<const VT*>(vals),        \
+                                  static_cast<const VT*>(B), C, M, K, N, map);                    \
+            else                                                                                  \
+                bcsr_spmm_blocks<VT, IT>(h, nbr, rb, cb, rp, ci, static_cast<const VT*>(vals),    \
+                                         static_cast<const VT*>(B), C, M, K, N, map);             \
         });                                                                                       \
     }
 XS_SPMM(f16f32_i32, __half, int32_t)
 XS_SPMM(f16f32_i64, __half, int64_t)
+XS_SPMM(bf16f32_i32, __nv_bfloat16, int32_t)
+XS_SPMM(bf16f32_i64, __nv_bfloat16, int64_t)
 XS_SPMM(f32f32_i32, float, int32_t)
 XS_SPMM(f32f32_i64, float, int64_t)
 
@@ -216,6 +221,8 @@ XS_CLUSTER(i64, int64_t)
     }
 XS_PERMUTE(f16_i32, __half, int32_t)
 XS_PERMUTE(f16_i64, __half, int64_t)
+XS_PERMUTE(bf16_i32, __nv_bfloat16, int32_t)
+XS_PERMUTE(bf16_i64, __nv_bfloat16, int64_t)
 XS_PERMUTE(f32_i32, float, int32_t)
 XS_PERMUTE(f32_i64, float, int64_t)
 
@@ -250,6 +257,8 @@ XS_COUNT(i64, int64_t)
     }
 XS_FILL(f16_i32, __half, int32_t)
 XS_FILL(f16_i64, __half, int64_t)
+XS_FILL(bf16_i32, __nv_bfloat16, int32_t)
+XS_FILL(bf16_i64, __nv_bfloat16, int64_t)
 XS_FILL(f32_i32, float, int32_t)
 XS_FILL(f32_i64, float, int64_t)
 
@@ -270,6 +279,8 @@ XS_UNPERM(f32_i32, float, int32_t)
 XS_UNPERM(f32_i64, float, int64_t)
 XS_UNPERM(f16_i32, __half, int32_t)
 XS_UNPERM(f16_i64, __half, int64_t)
+XS_UNPERM(bf16_i32, __nv_bfloat16, int32_t)
+XS_UNPERM(bf16_i64, __nv_bfloat16, int64_t)
 
 #define XS_PIPE(SUF, VT, IT)                                                                      \
     XS_API xspmm_status_t xspmm_spmm_csr_##SUF(                                                   \
@@ -278,7 +289,7 @@ XS_UNPERM(f16_i64, __half, int64_t)
         return guarded([&] {                                                                      \
             Handle& h = H(hh);                                                                    \
             need(M >= 0 && K >= 0 && nnz >= 0 && N >= 0, "negative dimension");                   \
-            XS_REQUIRE(hw == 16, XSPMM_STATUS_UNSUPPORTED, "hw_block_size must be 16");           \
+            need(hw >= 1, "hw_block_size must be at least 1");                                    \
             if (t) *t = xspmm_timings_t{0, 0, 0, 0, 0, 0};                                        \
             if (M == 0 || N == 0) return;                                                         \
             need(rp && C && (nnz == 0 || (ci && v && B)), "null pointer");                        \
@@ -289,5 +300,7 @@ XS_UNPERM(f16_i64, __half, int64_t)
     }
 XS_PIPE(f16f32_i32, __half, int32_t)
 XS_PIPE(f16f32_i64, __half, int64_t)
+XS_PIPE(bf16f32_i32, __nv_bfloat16, int32_t)
+XS_PIPE(bf16f32_i64, __nv_bfloat16, int64_t)
 XS_PIPE(f32f32_i32, float, int32_t)
 XS_PIPE(f32f32_i64, float, int64_t)

@@ -33,7 +33,7 @@ void adopt(xspmm_handle_t hh, std::unique_ptr<Plan<VT, IT>> plan, xspmm_plan_t* 
             *out = nullptr;                                                                       \
             Handle& h = H(hh);                                                                    \
             need(M >= 0 && K >= 0 && nnz >= 0, "negative dimension");                             \
-            XS_REQUIRE(hw == 16, XSPMM_STATUS_UNSUPPORTED, "hw_block_size must be 16");           \
+            need(hw >= 1, "hw_block_size must be at least 1");                                    \
             need(M == 0 || rp, "null row_ptr");                                                   \
             need(nnz == 0 || (ci && v), "null col_ind or values");                                \
             if (t) *t = xspmm_timings_t{0, 0, 0, 0, 0, 0};                                        \
@@ -60,6 +60,8 @@ void adopt(xspmm_handle_t hh, std::unique_ptr<Plan<VT, IT>> plan, xspmm_plan_t* 
     }
 XS_PLAN_CSR(f16f32_i32, __half, int32_t)
 XS_PLAN_CSR(f16f32_i64, __half, int64_t)
+XS_PLAN_CSR(bf16f32_i32, __nv_bfloat16, int32_t)
+XS_PLAN_CSR(bf16f32_i64, __nv_bfloat16, int64_t)
 XS_PLAN_CSR(f32f32_i32, float, int32_t)
 XS_PLAN_CSR(f32f32_i64, float, int64_t)
 
@@ -91,6 +93,8 @@ XS_PLAN_CSR(f32f32_i64, float, int64_t)
     }
 XS_PLAN_BCSR(f16f32_i32, __half, int32_t)
 XS_PLAN_BCSR(f16f32_i64, __half, int64_t)
+XS_PLAN_BCSR(bf16f32_i32, __nv_bfloat16, int32_t)
+XS_PLAN_BCSR(bf16f32_i64, __nv_bfloat16, int64_t)
 XS_PLAN_BCSR(f32f32_i32, float, int32_t)
 XS_PLAN_BCSR(f32f32_i64, float, int64_t)
 

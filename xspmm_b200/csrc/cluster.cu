@@ -1220,6 +1220,19 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                             }
                         }
                     }
+                    // The candidate at smax was accepted and adds columns: grow p, in the same
+                    // barrier interval as the appends above (they touch neither p nor U, and the
+                    // grower's position is settled, so U[smax] is its row).
+                    if (smax >= 0) {
+                        const int grow_row = st.u(smax);
+                        const int64_t g0 = a.qptr[grow_row], g1 = a.qptr[grow_row + 1];
+                        for (int64_t j = g0 + tid; j < g1; j += CL_THREADS) {
+                            const int b = a.qcol[j];
+                            const uint32_t bit = 1u << (b & 31);
+                            if (!(atomicOr(&a.pbits[b >> 5], bit) & bit))
+                                a.plist[atomicAdd(&sh.pcount, 1)] = b;
+                        }
+                    }
                     __syncthreads();
                     if (tid == 0) {
                         sh.out += nr;
@@ -1229,28 +1242,16 @@ __global__ void __launch_bounds__(CL_THREADS, 1) cluster_kernel(ClusterArgs a) {
                         sh.smax = -1;
                         sh.nr = 0;
                         sh.nkeep = 0;
-                    }
-                    if (smax < 0) {  // nothing grew p: every candidate is settled
-                        __syncthreads();
-                        break;
-                    }
-                    // The candidate at smax was accepted and adds columns: grow p.
-                    const int grow_row = st.u(smax);
-                    const int64_t g0 = a.qptr[grow_row], g1 = a.qptr[grow_row + 1];
-                    for (int64_t j = g0 + tid; j < g1; j += CL_THREADS) {
-                        const int b = a.qcol[j];
-                        const uint32_t bit = 1u << (b & 31);
-                        if (!(atomicOr(&a.pbits[b >> 5], bit) & bit)) a.plist[atomicAdd(&sh.pcount, 1)] = b;
+                        if (smax >= 0) {
+                            sh.limit = smax;
+                            sh.grown = 1;
+                            sh.m = min_inter(a.t_lo, sh.pcount);
+                            sh.ub = max_len(a.t_lo, sh.pcount);
+                            sh.need = (int)(sh.pcount - sh.m + 1);
+                        }
                     }
                     __syncthreads();
-                    if (tid == 0) {
-                        sh.limit = smax;
-                        sh.grown = 1;
-                        sh.m = min_inter(a.t_lo, sh.pcount);
-                        sh.ub = max_len(a.t_lo, sh.pcount);
-                        sh.need = (int)(sh.pcount - sh.m + 1);
-                    }
-                    __syncthreads();
+                    if (smax < 0) break;  // nothing grew p: every candidate is settled
                 }
                 for (int t = tid; t < sh.pcount; t += CL_THREADS) a.pbits[a.plist[t] >> 5] = 0u;
             }

@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
+#include <cuda_bf16.h>
 #include <cstdint>
 #include <cstdio>
 #include <algorithm>
@@ -145,6 +146,25 @@ T read_scalar(Handle& h, const T* dptr);
 // Small device helpers
 // ------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void flag_error(unsigned* err, unsigned bit) { atomicOr(err, bit); }
+
+// A stored value as float (exact for every value type of the library).
+__device__ __forceinline__ float to_float(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_float(float x) { return x; }
+
+// 16-bit value types share every data-movement kernel (the bits are copied, never converted);
+// only the arithmetic differs. half_like<VT> selects the 16-bit paths, as_half() views the bits.
+template <typename VT> struct half_like { static constexpr bool value = false; };
+template <> struct half_like<__half> { static constexpr bool value = true; };
+template <> struct half_like<__nv_bfloat16> { static constexpr bool value = true; };
+template <typename VT> inline const __half* as_half(const VT* p) {
+    static_assert(sizeof(VT) == 2, "16-bit value type");
+    return reinterpret_cast<const __half*>(p);
+}
+template <typename VT> inline __half* as_half(VT* p) {
+    static_assert(sizeof(VT) == 2, "16-bit value type");
+    return reinterpret_cast<__half*>(p);
+}
 
 __device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
 

@@ -445,6 +445,8 @@ template int64_t csr_to_bcsr_count<int64_t>(Handle&, int64_t, int64_t, int64_t, 
                                            VT*);
 XS_INST_FILL(__half, int32_t)
 XS_INST_FILL(__half, int64_t)
+XS_INST_FILL(__nv_bfloat16, int32_t)
+XS_INST_FILL(__nv_bfloat16, int64_t)
 XS_INST_FILL(float, int32_t)
 XS_INST_FILL(float, int64_t)
 

@@ -277,7 +277,8 @@ struct DistPlan final : DistPlanBase {
 template <typename VT, typename IT>
 std::unique_ptr<DistPlanBase> dist_plan_build(Handle& h, xspmm_dist_comm_s* c, int64_t M,
                                               int64_t K, int64_t nnz, const IT* rp, const IT* ci,
-                                              const VT* v, bool clustering, double row_weight) {
+                                              const VT* v, int64_t hw, bool clustering,
+                                              double row_weight) {
     auto dp = std::make_unique<DistPlan<VT, IT>>();
     cudaStream_t s = h.stream;
     dp->M = M;
@@ -287,7 +288,7 @@ std::unique_ptr<DistPlanBase> dist_plan_build(Handle& h, xspmm_dist_comm_s* c, i
     dp->perm = DevBuf<IT>(std::max<int64_t>(M, 1), s);
     if (M > 0) {
         if (clustering) {
-            cluster_jaccard<IT>(h, M, K, nnz, rp, ci, 0.5f, 16, dp->perm.get());
+            cluster_jaccard<IT>(h, M, K, nnz, rp, ci, 0.5f, hw, dp->perm.get());
         } else {
             iota_kernel<IT><<<grid_for(h, M), 256, 0, s>>>(dp->perm.get(), M);
             after_launch(h, "dist_iota");
@@ -468,7 +469,7 @@ XS_API xspmm_status_t xspmm_dist_comm_destroy(xspmm_dist_comm_t c) {
             Handle& h = H(hh);                                                                     \
             xspmm_dist_comm_s* c = CM(cc);                                                         \
             need(M >= 0 && K >= 0 && nnz >= 0 && row_weight >= 0.0, "negative argument");          \
-            XS_REQUIRE(hw == 16, XSPMM_STATUS_UNSUPPORTED, "hw_block_size must be 16");            \
+            need(hw >= 1, "hw_block_size must be at least 1");                                     \
             need(c->device == h.device, "communicator and handle on different devices");           \
             need(M == 0 || rp, "null row_ptr");                                                    \
             need(nnz == 0 || (ci && v), "null col_ind or values");                                 \
@@ -477,7 +478,7 @@ XS_API xspmm_status_t xspmm_dist_comm_destroy(xspmm_dist_comm_t c) {
             ps->owner = hh;                                                                        \
             ps->comm = c;                                                                          \
             ps->p = dist_plan_build<VT, IT>(h, c, M, K, nnz, rp, ci, static_cast<const VT*>(v),    \
-                                            clustering != 0, row_weight);                          \
+                                            hw, clustering != 0, row_weight);                      \
             ps->p->value_bytes = (int)sizeof(VT);                                                  \
             hh->live_plans += 1;                                                                   \
             *out = ps.release();                                                                   \
@@ -485,6 +486,8 @@ XS_API xspmm_status_t xspmm_dist_comm_destroy(xspmm_dist_comm_t c) {
     }
 XS_DIST_PLAN(f16f32_i32, __half, int32_t)
 XS_DIST_PLAN(f16f32_i64, __half, int64_t)
+XS_DIST_PLAN(bf16f32_i32, __nv_bfloat16, int32_t)
+XS_DIST_PLAN(bf16f32_i64, __nv_bfloat16, int64_t)
 XS_DIST_PLAN(f32f32_i32, float, int32_t)
 XS_DIST_PLAN(f32f32_i64, float, int64_t)
 

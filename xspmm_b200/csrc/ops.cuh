@@ -20,10 +20,16 @@ void bcsr_spmm(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* row_
 // shapes and alignments allow it.
 bool tc_supported(int64_t nbr, int64_t nbc, int64_t nnzb, const void* vals, const void* B,
                   const void* C, int64_t N);
+// Tier-1 for BCSR block shapes other than 16x16 (spmm_blocks.cu): rb x cb blocks.
+template <typename VT, typename IT>
+void bcsr_spmm_blocks(Handle& h, int64_t nbr, int64_t rb, int64_t cb, const IT* rp, const IT* ci,
+                      const VT* v, const VT* B, float* C, int64_t M, int64_t K, int64_t N,
+                      const IT* map);
+// 16-bit values: fp16, or bf16 when bf16 is set (the bits are read through __half pointers).
 template <typename IT>
 void bcsr_spmm_tc(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
                   const __half* vals, const __half* B, float* C, int64_t M, int64_t K, int64_t N,
-                  const IT* map);
+                  const IT* map, bool bf16);
 
 // What the tcgen05 kernel derives from A once: per group of 8 block rows the union of block
 // columns (gptr/gcol) and the stacked A tiles packed 128 x 16 per union entry, with their TMA map.
@@ -38,7 +44,7 @@ void tc_prepare(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,
                 const __half* vals, TcPrep& out);
 template <typename IT>
 void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M, int64_t K,
-                int64_t N, const IT* map);
+                int64_t N, const IT* map, bool bf16);
 bool tc_preferred(int64_t nbr, int64_t nbc, int64_t nnzb);
 
 // The mma.sync Tier-1 kernel, without the automatic choice of tcgen05.
@@ -65,7 +71,7 @@ void mma_work_build(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT*
 template <typename IT>
 void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
                        const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map,
-                       const MmaWork* work);
+                       const MmaWork* work, bool bf16);
 // Execution order of block rows for the mma.sync kernel: sorted by first block column.
 template <typename IT>
 void block_row_order(Handle& h, int64_t nbr, int64_t nbc, const IT* rp, const IT* ci,
@@ -87,6 +93,9 @@ struct SpRow {  // a row of the gather kernels with at most SP_LONG nonzeros
     int64_t e0;   // its first nonzero
     int32_t row, cnt;
 };
+struct SpTask {  // consecutive short rows [first, first + nrows) taken by one warp (nrows <= 32)
+    int32_t first, nrows;
+};
 struct SparseRows {
     std::vector<uint8_t> dense_br;
     std::vector<int64_t> host_rp;  // the block row pointers, read back once at build
@@ -95,9 +104,11 @@ struct SparseRows {
     DevBuf<uint8_t> val;   // nnz values of the matrix's value type
     DevBuf<int32_t> brs, long_rows;
     DevBuf<SpRow> short_rows;
+    DevBuf<SpTask> tasks;          // short rows packed into warp tasks
     DevBuf<SparseChunk> chunks;    // long rows cut into chunks
     DevBuf<int32_t> long_first;    // [nlong+1] first chunk of each long row
-    int64_t nbrs = 0, nnz = 0, nshort = 0, nlong = 0, nchunks = 0;
+    int64_t nbrs = 0, nnz = 0, nshort = 0, ntasks = 0, nlong = 0, nchunks = 0;
+    int64_t nplain_tasks = 0;      // tasks [0, nplain_tasks) hold rows of <= SP_PLAIN nonzeros
 };
 template <typename VT, typename IT>
 void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT* ci,

@@ -26,8 +26,10 @@ template <typename VT, typename IT>
 void plan_from_csr(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* row_ptr,
                    const IT* col_ind, const VT* values, int64_t hw, bool clustering, bool mark,
                    Plan<VT, IT>& out) {
-    XS_REQUIRE(hw == 16, XSPMM_STATUS_UNSUPPORTED,
-               "hw_block_size must be 16 (the tensor-core block size)");
+    // hw_block_size is the clustering's column block width, as in the reference (:83). The
+    // product always runs on 16 x 16 blocks: the reference converts to hw x hw blocks (:102) but
+    // its kernel reads them as 16 x 16 (:39), so for hw != 16 its C is wrong; C here is A * B.
+    XS_REQUIRE(hw >= 1, XSPMM_STATUS_INVALID_ARGUMENT, "hw_block_size must be at least 1");
     cudaStream_t s = h.stream;
     auto ev = [&](int i) {
         if (mark) XS_CHECK_CUDA(cudaEventRecord(h.ev[i], s));
@@ -91,12 +93,12 @@ void plan_from_bcsr(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT*
 
 template <typename VT, typename IT>
 void Plan<VT, IT>::prepare_tc(Handle& h) {
-    if constexpr (std::is_same<VT, __half>::value) {
+    if constexpr (half_like<VT>::value) {
         if (tc_built || nbr == 0 || nbc == 0 || nnzb == 0) return;
         XS_REQUIRE(nnzb * 16 < (int64_t(1) << 31) && nbc * 16 < (int64_t(1) << 31) &&
                        reinterpret_cast<uintptr_t>(v) % 16 == 0,
                    XSPMM_STATUS_UNSUPPORTED, "matrix not supported by the tcgen05 kernel");
-        tc_prepare<IT>(h, nbr, nbc, nnzb, rp, ci, v, tc);
+        tc_prepare<IT>(h, nbr, nbc, nnzb, rp, ci, as_half(v), tc);
         tc_built = true;
     } else {
         (void)h;
@@ -108,15 +110,16 @@ void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
     if (M == 0 || N == 0) return;
     const VT* B = static_cast<const VT*>(Bv);
     const IT* map = clustered ? perm.get() : nullptr;
-    if constexpr (std::is_same<VT, __half>::value) {
+    if constexpr (half_like<VT>::value) {
+        constexpr bool bf16 = std::is_same<VT, __nv_bfloat16>::value;
         if (plan_wants_tc(h, nbr, nbc, nnzb) && tc_supported(nbr, nbc, nnzb, v, B, C, N)) {
             prepare_tc(h);
-            tc_execute<IT>(h, tc, B, C, M, K, N, map);
+            tc_execute<IT>(h, tc, as_half(B), C, M, K, N, map, bf16);
             return;
         }
         // When B is well beyond what L2 holds, run the block rows in order of their first
         // block column so that CTAs in flight together gather nearby rows of B.
-        const bool big_b = (double)K * (double)N * sizeof(__half) > 48.0 * (1 << 20);
+        const bool big_b = (double)K * (double)N * sizeof(VT) > 48.0 * (1 << 20);
         // A single product of a small matrix does not repay building the list (one host
         // round trip); a large one does (long rows would serialize on one CTA).
         const bool want_work = !one_shot || nnzb >= (int64_t(1) << 18);
@@ -137,8 +140,8 @@ void Plan<VT, IT>::execute(Handle& h, const void* Bv, float* C, int64_t N) {
             work_sorted = big_b;
         }
         if (!(split && work.empty))
-            bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map,
-                                  work_built ? &work : nullptr);
+            bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, as_half(v), as_half(B), C, M, K, N, map,
+                                  work_built ? &work : nullptr, bf16);
         if (split) sparse_rows_execute<VT, IT>(h, sparse, B, C, M, K, N, map);
     } else {
         // fp32: the same split, at a higher fill (the SIMT block kernel pays per nonzero column
@@ -200,6 +203,8 @@ void spmm_csr_pipeline(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* r
                                             int64_t, bool, xspmm_timings_t*);
 XS_INST_PIPE(__half, int32_t)
 XS_INST_PIPE(__half, int64_t)
+XS_INST_PIPE(__nv_bfloat16, int32_t)
+XS_INST_PIPE(__nv_bfloat16, int64_t)
 XS_INST_PIPE(float, int32_t)
 XS_INST_PIPE(float, int64_t)
 

@@ -64,6 +64,7 @@ struct Plan final : PlanBase {
                          (sparse.brs.n + sparse.long_rows.n + sparse.long_first.n) *
                              sizeof(int32_t) +
                          sparse.short_rows.n * sizeof(SpRow) +
+                         sparse.tasks.n * sizeof(SpTask) +
                          sparse.chunks.n * sizeof(SparseChunk)) +
                (int64_t)(f32work.pieces.n * sizeof(F32Piece) +
                          (f32work.long_br.n + f32work.long_first.n) * sizeof(int32_t)) +
@@ -78,7 +79,7 @@ struct Plan final : PlanBase {
         bv.s = s;
         sparse.rptr.s = sparse.col.s = sparse.val.s = s;
         sparse.brs.s = sparse.short_rows.s = sparse.long_rows.s = sparse.long_first.s = s;
-        sparse.chunks.s = s;
+        sparse.chunks.s = sparse.tasks.s = s;
         f32work.pieces.s = f32work.long_br.s = f32work.long_first.s = s;
         tc.gptr.s = s;
         tc.gcol.s = s;

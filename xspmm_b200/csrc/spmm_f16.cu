@@ -1,5 +1,6 @@
-// spmm_f16.cu -- Tier-1 BCSR SpMM, fp16 blocks x fp16 B -> fp32 C, on the warp-level tensor-core
-// path (mma.sync m16n8k16 with fp32 accumulation).
+// spmm_f16.cu -- Tier-1 BCSR SpMM, 16-bit blocks x 16-bit B -> fp32 C (fp16, or bf16 with the bf16
+// form of the instruction), on the warp-level tensor-core path (mma.sync m16n8k16 with fp32
+// accumulation).
 //
 // Semantics follow the reference kernel (src/common/spmm_math.hpp:59-122): for block row br,
 // C[16br+i, n] = sum over its blocks j (in col_ind order) of A_j[i, :] . B[16 col_j + :, n], every
@@ -55,16 +56,28 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* 
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(smem_u32(p)));
 }
+// D += A x B, fp32 accumulators; A and B both fp16 (BF16 = false) or both bf16.
+template <bool BF16>
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                           uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    if constexpr (BF16) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
 }
 
-template <typename IT, int WARPS, bool ALIGNED>
+// The values and B are 16-bit (fp16, or bf16 when BF16); only the MMA instruction differs, so
+// both are read through __half pointers.
+template <typename IT, int WARPS, bool ALIGNED, bool BF16>
 __global__ void __launch_bounds__(WARPS * 32, WARPS == 1 ? 24 : 1)
 bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ col_ind,
                          const __half* __restrict__ vals, const __half* __restrict__ B,
@@ -192,8 +205,8 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
                 const int chunk = (warp * 64 + j * 16) / 8 + (mi >> 1);
                 uint32_t b[4];
                 ldmatrix_x4_trans(b, sB + b_kk * ROW_BYTES + ((chunk ^ (b_kk & 7)) * 16));
-                mma_16816(p[2 * j], a, b[0], b[1]);
-                mma_16816(p[2 * j + 1], a, b[2], b[3]);
+                mma_16816<BF16>(p[2 * j], a, b[0], b[1]);
+                mma_16816<BF16>(p[2 * j + 1], a, b[2], b[3]);
             }
             if ((i + 1) % GROUP == 0 || i + 1 == nblk) {
 #pragma unroll
@@ -250,11 +263,12 @@ bcsr_spmm_f16_mma_kernel(const IT* __restrict__ row_ptr, const IT* __restrict__ 
 template <typename IT, int WARPS, bool ALIGNED>
 void launch(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v, const __half* B,
             float* C, int64_t M, int64_t K, int64_t N, const IT* map, const MmaItem* items,
-            float* ws) {
+            float* ws, bool bf16) {
     constexpr int TN = 64 * WARPS;
     constexpr int smem = STAGES * (512 + 16 * TN * 2);
     static_assert(smem <= 48 * 1024, "stage ring must fit the default dynamic smem limit");
-    auto kern = bcsr_spmm_f16_mma_kernel<IT, WARPS, ALIGNED>;
+    auto kern = bf16 ? bcsr_spmm_f16_mma_kernel<IT, WARPS, ALIGNED, true>
+                     : bcsr_spmm_f16_mma_kernel<IT, WARPS, ALIGNED, false>;
     dim3 grid((unsigned)nbr, (unsigned)ceil_div(N, TN));  // nbr = number of work items
     kern<<<grid, WARPS * 32, smem, h.stream>>>(rp, ci, v, B, C, map, M, K, N, items, ws, h.d_err);
     after_launch(h, "bcsr_spmm_f16_mma");
@@ -284,15 +298,15 @@ bool tc_preferred(int64_t nbr, int64_t nbc, int64_t nnzb) {
 template <typename IT>
 static void bcsr_spmm_f16_impl(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,
                                const IT* ci, const __half* v, const __half* B, float* C,
-                               int64_t M, int64_t K, int64_t N, const IT* map) {
+                               int64_t M, int64_t K, int64_t N, const IT* map, bool bf16) {
     if (nbr == 0 || N == 0 || M == 0) return;
     const Tier1Kernel choice = tier1_kernel_choice(h);
     if (choice != Tier1Kernel::Mma && tc_supported(nbr, nbc, nnzb, v, B, C, N) &&
         (choice == Tier1Kernel::Tc || tc_preferred(nbr, nbc, nnzb))) {
-        bcsr_spmm_tc<IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
+        bcsr_spmm_tc<IT>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map, bf16);
         return;
     }
-    bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map, nullptr);
+    bcsr_spmm_mma_f16<IT>(h, nbr, rp, ci, v, B, C, M, K, N, map, nullptr, bf16);
 }
 
 // C[map(16 br + i), n] = sum over the slots of split block row br, in slot order.
@@ -325,7 +339,7 @@ __global__ void mma_split_reduce_kernel(const float* __restrict__ ws,
 template <typename IT>
 void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const __half* v,
                        const __half* B, float* C, int64_t M, int64_t K, int64_t N, const IT* map,
-                       const MmaWork* work) {
+                       const MmaWork* work, bool bf16) {
     if (nbr == 0 || N == 0 || M == 0) return;
     const bool listed = work && work->nitems > 0;
     const int64_t nwork = listed ? work->nitems : nbr;
@@ -338,13 +352,13 @@ void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const
                          (reinterpret_cast<uintptr_t>(C) % 8 == 0);
     const int warps = N <= 64 ? 1 : (N <= 128 ? 2 : 4);
     if (aligned) {
-        if (warps == 1) launch<IT, 1, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
-        else if (warps == 2) launch<IT, 2, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
-        else launch<IT, 4, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
+        if (warps == 1) launch<IT, 1, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws, bf16);
+        else if (warps == 2) launch<IT, 2, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws, bf16);
+        else launch<IT, 4, true>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws, bf16);
     } else {
-        if (warps == 1) launch<IT, 1, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
-        else if (warps == 2) launch<IT, 2, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
-        else launch<IT, 4, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws);
+        if (warps == 1) launch<IT, 1, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws, bf16);
+        else if (warps == 2) launch<IT, 2, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws, bf16);
+        else launch<IT, 4, false>(h, nwork, rp, ci, v, B, C, M, K, N, map, items, ws, bf16);
     }
     if (listed && work->nlong > 0) {
         const int64_t total = work->nlong * 16 * N;
@@ -358,10 +372,10 @@ void bcsr_spmm_mma_f16(Handle& h, int64_t nbr, const IT* rp, const IT* ci, const
 
 template void bcsr_spmm_mma_f16<int32_t>(Handle&, int64_t, const int32_t*, const int32_t*,
                                          const __half*, const __half*, float*, int64_t, int64_t,
-                                         int64_t, const int32_t*, const MmaWork*);
+                                         int64_t, const int32_t*, const MmaWork*, bool);
 template void bcsr_spmm_mma_f16<int64_t>(Handle&, int64_t, const int64_t*, const int64_t*,
                                          const __half*, const __half*, float*, int64_t, int64_t,
-                                         int64_t, const int64_t*, const MmaWork*);
+                                         int64_t, const int64_t*, const MmaWork*, bool);
 
 // Block rows sorted by their first block column (empty rows last): the execution order a plan
 // gives the mma.sync kernel, so that CTAs running together gather nearby rows of B and the gather
@@ -476,19 +490,17 @@ template void mma_work_build<int64_t>(Handle&, int64_t, int64_t, int64_t, const 
 template void block_row_order<int64_t>(Handle&, int64_t, int64_t, const int64_t*, const int64_t*,
                                        DevBuf<int32_t>&);
 
-template <>
-void bcsr_spmm<__half, int32_t>(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb,
-                                const int32_t* rp, const int32_t* ci, const __half* v,
-                                const __half* B, float* C, int64_t M, int64_t K, int64_t N,
-                                const int32_t* map) {
-    bcsr_spmm_f16_impl<int32_t>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
-}
-template <>
-void bcsr_spmm<__half, int64_t>(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb,
-                                const int64_t* rp, const int64_t* ci, const __half* v,
-                                const __half* B, float* C, int64_t M, int64_t K, int64_t N,
-                                const int64_t* map) {
-    bcsr_spmm_f16_impl<int64_t>(h, nbr, nbc, nnzb, rp, ci, v, B, C, M, K, N, map);
-}
+#define XS_BCSR_SPMM_16(VT, IT, BF)                                                               \
+    template <>                                                                                   \
+    void bcsr_spmm<VT, IT>(Handle & h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,      \
+                           const IT* ci, const VT* v, const VT* B, float* C, int64_t M,           \
+                           int64_t K, int64_t N, const IT* map) {                                 \
+        bcsr_spmm_f16_impl<IT>(h, nbr, nbc, nnzb, rp, ci, as_half(v), as_half(B), C, M, K, N, map, \
+                               BF);                                                               \
+    }
+XS_BCSR_SPMM_16(__half, int32_t, false)
+XS_BCSR_SPMM_16(__half, int64_t, false)
+XS_BCSR_SPMM_16(__nv_bfloat16, int32_t, true)
+XS_BCSR_SPMM_16(__nv_bfloat16, int64_t, true)
 
 }  // namespace xspmm_b200

@@ -10,17 +10,23 @@
 //     (blocks ascending, then the column inside the block) -- the nonzeros of the BCSR values,
 //     read once -- and each product then gathers one B row per nonzero: 6 + 2N bytes per
 //     nonzero instead of 512 + 32N per block in fp16 (8 + 4N against 1024 + 64N in fp32).
-// The result is the same sum, C[16br+i, n] = sum over the row's nonzeros a * B[col, n],
-// accumulated in fp64 in column order and rounded once to fp32 (the tensor-core kernels
-// accumulate in fp32; the fp32 SIMT kernel also in fp64, in the same column order). A row of a
-// split block row with no nonzero is written as zeros, as the block product writes it.
+// The result is the same sum, C[16br+i, n] = sum over the row's nonzeros a * B[col, n], added in
+// column order. For 16-bit values every product is exact in fp32; a row of up to SP_PLAIN
+// nonzeros is summed in fp32 (as the tensor-core kernels and the reference's WMMA accumulate), a
+// longer one in fp32 groups of SP_UNROLL products whose sums are added in fp64, so that hub rows
+// lose no accuracy to their large partial sums. fp32 values are multiplied and summed in fp64 and
+// rounded once (as the fp32 SIMT block kernel does). A row of a split block row with no nonzero
+// is written as zeros, as the block product writes it.
 //
-// Kernels: a warp per row and 128-column tile (4 columns per lane) for rows of up to SP_LONG
-// nonzeros; longer rows (hub rows) are cut into chunks of SP_CHUNK nonzeros, a CTA each, whose
-// fp64 partials are added in chunk order afterwards -- results do not depend on timing.
+// Kernels: a warp per task of consecutive short rows (up to SP_LONG nonzeros each) and 128-column
+// tile (4 columns per lane); longer rows (hub rows) are cut into chunks of SP_CHUNK nonzeros, a
+// CTA each, whose partials (each warp's share in column order, its SP_UNROLL-nonzero groups added
+// in fp64, then the warps' sums in warp order) are added in fp64 in chunk order afterwards -- results
+// do not depend on timing.
 #include "ops.cuh"
 
 #include <algorithm>
+#include <type_traits>
 #include <vector>
 
 namespace xspmm_b200 {
@@ -31,6 +37,12 @@ constexpr int SP_WARPS = 8;
 constexpr int64_t SP_LONG = 256;    // rows with more nonzeros are cut into chunks
 constexpr int64_t SP_CHUNK = 2048;  // nonzeros per chunk of a long row
 constexpr int SP_UNROLL = 8;        // B rows in flight per warp
+constexpr int SP_TASK_NNZ = 128;    // nonzeros a warp task of several short rows may hold
+// 16-bit values: rows of at most SP_PLAIN nonzeros are summed in fp32; in longer rows each group of
+// SP_UNROLL products is summed in fp32 and the groups are added in fp64, so that a long row's
+// rounding error stays at fp64 level relative to its partial sums.
+constexpr int SP_PLAIN = 128;
+constexpr int SP_CHUNK_MINB = 2;    // CTAs per SM the chunk kernel is compiled for
 
 // Value-type helpers: 8 consecutive block values of a lane (one 16x16 block row-major: lane l
 // holds row l/2, columns (l&1)*8 .. +7), the nonzero test (the sign bit ignored, so -0 counts as
@@ -50,12 +62,35 @@ template <> struct SpVT<__half> {
         o[0] = f0.x; o[1] = f0.y; o[2] = f1.x; o[3] = f1.y;
     }
     static constexpr int b4_align = 8;
+    using Acc = float;  // fp16 x fp16 products are exact in fp32; summed in fp32, column order
     using Raw = uint2;  // 4 consecutive elements of a B row, as loaded
     __device__ static Raw raw4(const __half* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
     __device__ static Raw zero4() { return make_uint2(0u, 0u); }
     __device__ static void f4(const Raw& x, float (&o)[4]) {
         const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&x.x));
         const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&x.y));
+        o[0] = f0.x; o[1] = f0.y; o[2] = f1.x; o[3] = f1.y;
+    }
+};
+template <> struct SpVT<__nv_bfloat16> {  // as fp16: same bits moved, bf16 -> fp32 conversions
+    __device__ static void load8(const __nv_bfloat16* p, __nv_bfloat16 (&o)[8]) {
+        const uint4 x = *reinterpret_cast<const uint4*>(p);
+        *reinterpret_cast<uint4*>(o) = x;
+    }
+    __device__ static bool nz(__nv_bfloat16 x) {
+        return (__bfloat16_as_ushort(x) & 0x7FFFu) != 0;
+    }
+    __device__ static float f(__nv_bfloat16 x) { return __bfloat162float(x); }
+    static constexpr int b4_align = 8;
+    using Acc = float;  // bf16 x bf16 products are exact in fp32 (8 + 8 significant bits)
+    using Raw = uint2;
+    __device__ static Raw raw4(const __nv_bfloat16* p) {
+        return __ldg(reinterpret_cast<const uint2*>(p));
+    }
+    __device__ static Raw zero4() { return make_uint2(0u, 0u); }
+    __device__ static void f4(const Raw& x, float (&o)[4]) {
+        const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.x));
+        const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.y));
         o[0] = f0.x; o[1] = f0.y; o[2] = f1.x; o[3] = f1.y;
     }
 };
@@ -73,6 +108,7 @@ template <> struct SpVT<float> {
         o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w;
     }
     static constexpr int b4_align = 16;
+    using Acc = double;  // fp32 products and sums in fp64, rounded once
     using Raw = float4;
     __device__ static Raw raw4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
     __device__ static Raw zero4() { return make_float4(0.f, 0.f, 0.f, 0.f); }
@@ -144,81 +180,146 @@ __global__ void sp_extract_kernel(const IT* __restrict__ rp, const IT* __restric
     }
 }
 
-// C[map(r), tile] for rows with at most SP_LONG nonzeros: a warp per (row, 128-column tile). The
-// row's descriptor (first nonzero, count, row) is one 16-byte load, so the chain of dependent
-// loads before the B rows is descriptor -> (column, value) pairs -> B rows. The warp loads 32
-// pairs at once (coalesced), broadcasts them and keeps SP_UNROLL B rows in flight (raw fp16 in
-// registers until they are used); nonzeros are still added in column order, in fp64.
-template <typename VT, typename IT, bool VEC>
-__global__ void __launch_bounds__(SP_WARPS * 32, sizeof(VT) == 2 ? 4 : 2)
-sp_gather_short_kernel(const SpRow* __restrict__ rows, int64_t nrows,
-                       const int32_t* __restrict__ col, const VT* __restrict__ val,
-                       const VT* __restrict__ B, float* __restrict__ C,
-                       const IT* __restrict__ row_map, int64_t M, int64_t K, int64_t N,
-                       unsigned* __restrict__ err) {
+// C[map(r), tile] for rows with at most SP_LONG nonzeros, a warp per (task, 128-column tile). A
+// task is up to 32 consecutive short rows holding at most SP_TASK_NNZ nonzeros (or one row of up
+// to SP_LONG). The warp walks the task's nonzeros as one stream, row after row: lane i holds row
+// i's descriptor and the inclusive prefix of the counts, each lane finds the row of stream
+// position base + lane by a 5-step search over that prefix and loads the (column, value) pair,
+// and the warp keeps SP_UNROLL B rows in flight across row ends, so that rows of one to three
+// nonzeros do not leave it waiting on a chain of loads per row. A row's nonzeros are still added
+// in column order, in fp64, and its sum is rounded once to fp32 when the stream leaves the row;
+// rows without nonzeros are written as zeros.
+template <typename VT, typename IT, bool VEC, bool FLUSH>
+__global__ void __launch_bounds__(SP_WARPS * 32, sizeof(VT) == 2 ? (FLUSH ? 3 : 4) : 2)
+sp_gather_rows_kernel(const SpTask* __restrict__ tasks, int64_t ntasks,
+                      const SpRow* __restrict__ rows, const int32_t* __restrict__ col,
+                      const VT* __restrict__ val, const VT* __restrict__ B, float* __restrict__ C,
+                      const IT* __restrict__ row_map, int64_t M, int64_t K, int64_t N,
+                      unsigned* __restrict__ err) {
+    const unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * SP_WARPS + (threadIdx.x >> 5);
-    if (t >= nrows) return;
-    const SpRow ri = rows[t];
-    const int64_t r = ri.row, e0 = ri.e0;
-    const int n_all = ri.cnt;
+    if (t >= ntasks) return;
+    const SpTask tk = tasks[t];
+    SpRow ri{0, -1, 0};
+    if (lane < tk.nrows) ri = rows[tk.first + lane];
+    // where the lane's row is stored (-1: no row, or a bad map entry)
+    int64_t orow = -1;
+    if (ri.row >= 0 && ri.row < M) {
+        orow = row_map ? (int64_t)row_map[ri.row] : (int64_t)ri.row;
+        if (orow < 0 || orow >= M) {
+            flag_error(err, DERR_PERM_OUT_OF_RANGE);
+            orow = -1;
+        }
+    }
+    int incl = ri.cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += v;
+    }
+    const int total = __shfl_sync(FULL, incl, 31);
+    const int64_t e_rel = ri.e0 - (int64_t)(incl - ri.cnt);  // stream position k -> k + e_rel
     const int64_t n0 = (int64_t)blockIdx.y * SP_TN + lane * 4;
-    double acc[4] = {0.0, 0.0, 0.0, 0.0};
-    for (int base = 0; base < n_all; base += 32) {
-        const int cnt = min(32, n_all - base);
-        const int64_t my_c = lane < cnt ? (int64_t)col[e0 + base + lane] : 0;
-        const float my_a = lane < cnt ? SpVT<VT>::f(val[e0 + base + lane]) : 0.0f;
+    const bool full4 = VEC && n0 + 4 <= N;
+
+    // A row's sum: products added into acc in column order; with FLUSH (tasks holding a row of
+    // more than SP_PLAIN nonzeros, 16-bit values) each group of SP_UNROLL products is then moved
+    // into the fp64 tot.
+    using Acc = typename SpVT<VT>::Acc;
+    constexpr bool flush = FLUSH && sizeof(Acc) == 4;
+    auto store = [&](int j, const double (&tot)[4], const Acc (&acc)[4]) {  // j warp-uniform
+        const int64_t o = __shfl_sync(FULL, orow, j);
+        if (o < 0) return;
+        float* dst = C + o * N + n0;
+        float r[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) r[q] = flush ? (float)(tot[q] + (double)acc[q]) : (float)acc[q];
+        if (full4) {
+            *reinterpret_cast<float4*>(dst) = make_float4(r[0], r[1], r[2], r[3]);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (n0 + q < N) dst[q] = r[q];
+        }
+    };
+    Acc acc[4] = {0, 0, 0, 0};
+    double tot[4] = {0.0, 0.0, 0.0, 0.0};
+    // rows without nonzeros
+    {
+        unsigned zm = __ballot_sync(FULL, ri.cnt == 0 && orow >= 0);
+        while (zm) {
+            const int j = __ffs(zm) - 1;
+            zm &= zm - 1;
+            store(j, tot, acc);
+        }
+    }
+    int cur = -1;  // the row being summed
+    for (int base = 0; base < total; base += 32) {
+        const int cnt = min(32, total - base);
+        const int k = base + lane;
+        int j = 0;  // the row of stream position k: the number of rows whose prefix is <= k
+#pragma unroll
+        for (int step = 16; step >= 1; step >>= 1) {
+            if (__shfl_sync(FULL, incl, j + step - 1) <= k) j += step;
+        }
+        const int64_t rel = __shfl_sync(FULL, e_rel, j);
+        int my_c = 0;
+        float my_a = 0.0f;
+        if (lane < cnt) {
+            my_c = col[rel + k];
+            my_a = SpVT<VT>::f(val[rel + k]);
+        }
         for (int u0 = 0; u0 < cnt; u0 += SP_UNROLL) {
             typename SpVT<VT>::Raw raw[SP_UNROLL];
             float a[SP_UNROLL];
+            int ju[SP_UNROLL];
             bool lv[SP_UNROLL];
 #pragma unroll
             for (int u = 0; u < SP_UNROLL; ++u) {
-                const int64_t c = __shfl_sync(0xffffffffu, my_c, (u0 + u) & 31);
-                a[u] = __shfl_sync(0xffffffffu, my_a, (u0 + u) & 31);
+                const int src_lane = (u0 + u) & 31;
+                const int64_t c = __shfl_sync(FULL, my_c, src_lane);
+                a[u] = __shfl_sync(FULL, my_a, src_lane);
+                ju[u] = __shfl_sync(FULL, j, src_lane);
                 lv[u] = u0 + u < cnt && c < K;
-                const VT* src = B + c * N + n0;
-                if (VEC && lv[u] && n0 + 4 <= N) {
-                    raw[u] = SpVT<VT>::raw4(src);
-                } else {
-                    raw[u] = SpVT<VT>::zero4();
-                }
+                raw[u] = (full4 && lv[u]) ? SpVT<VT>::raw4(B + c * N + n0) : SpVT<VT>::zero4();
             }
 #pragma unroll
             for (int u = 0; u < SP_UNROLL; ++u) {
                 if (u0 + u < cnt) {
+                    if (ju[u] != cur) {
+                        if (cur >= 0) store(cur, tot, acc);
+                        cur = ju[u];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            acc[q] = 0;
+                            tot[q] = 0.0;
+                        }
+                    }
                     float bb[4];
-                    if (VEC) {
+                    if (VEC) {  // N % 4 == 0: a lane's 4 columns are all inside N or all past it
                         SpVT<VT>::f4(raw[u], bb);
                     } else {
-                        const int64_t c = __shfl_sync(0xffffffffu, my_c, (u0 + u) & 31);
+                        const int64_t c = __shfl_sync(FULL, my_c, (u0 + u) & 31);
                         const VT* src = B + c * N + n0;
 #pragma unroll
                         for (int q = 0; q < 4; ++q)
                             bb[q] = (lv[u] && n0 + q < N) ? SpVT<VT>::f(src[q]) : 0.0f;
                     }
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        acc[q] = fma((double)a[u], (double)bb[q], acc[q]);
+                    for (int q = 0; q < 4; ++q) acc[q] = fma((Acc)a[u], (Acc)bb[q], acc[q]);
+                }
+            }
+            if (flush) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    tot[q] += (double)acc[q];
+                    acc[q] = 0;
                 }
             }
         }
     }
-    if (r >= M) return;
-    const int64_t orow = row_map ? (int64_t)row_map[r] : r;
-    if (orow < 0 || orow >= M) {
-        if (lane == 0) flag_error(err, DERR_PERM_OUT_OF_RANGE);
-        return;
-    }
-    float* dst = C + orow * N + n0;
-    if (VEC && n0 + 4 <= N) {
-        *reinterpret_cast<float4*>(dst) =
-            make_float4((float)acc[0], (float)acc[1], (float)acc[2], (float)acc[3]);
-    } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (n0 + q < N) dst[q] = (float)acc[q];
-    }
+    if (cur >= 0) store(cur, tot, acc);
 }
 
 // Rows with more than SP_LONG nonzeros are cut into chunks of at most SP_CHUNK nonzeros: a CTA
@@ -227,7 +328,7 @@ sp_gather_short_kernel(const SpRow* __restrict__ rows, int64_t nrows,
 // chunk order and rounds once. (One CTA per hub row of ~40K nonzeros set the time of the whole
 // product.)
 template <typename VT, bool VEC>
-__global__ void __launch_bounds__(SP_WARPS * 32)
+__global__ void __launch_bounds__(SP_WARPS * 32, SP_CHUNK_MINB)
 sp_gather_chunk_kernel(const SparseChunk* __restrict__ chunks, const int32_t* __restrict__ col,
                        const VT* __restrict__ val, const VT* __restrict__ B,
                        double* __restrict__ ws, int64_t K, int64_t N) {
@@ -237,7 +338,9 @@ sp_gather_chunk_kernel(const SparseChunk* __restrict__ chunks, const int32_t* __
     const int64_t n0 = (int64_t)blockIdx.y * SP_TN + lane * 4;
     const int64_t len = ck.e1 - ck.e0, per = (len + SP_WARPS - 1) / SP_WARPS;
     const int64_t w0 = ck.e0 + min(len, per * warp), w1 = ck.e0 + min(len, per * (warp + 1));
-    double acc[4] = {0.0, 0.0, 0.0, 0.0};
+    using Acc = typename SpVT<VT>::Acc;
+    Acc acc[4] = {0, 0, 0, 0};
+    double tot[4] = {0.0, 0.0, 0.0, 0.0};  // fp64 sum of the SP_UNROLL-nonzero groups
     for (int64_t base = w0; base < w1; base += 32) {
         const int cnt = (int)min((int64_t)32, w1 - base);
         const int64_t my_c = lane < cnt ? (int64_t)col[base + lane] : 0;
@@ -268,13 +371,18 @@ sp_gather_chunk_kernel(const SparseChunk* __restrict__ chunks, const int32_t* __
                             bb[q] = (lv[u] && n0 + q < N) ? SpVT<VT>::f(src[q]) : 0.0f;
                     }
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) acc[q] = fma((double)a[u], (double)bb[q], acc[q]);
+                    for (int q = 0; q < 4; ++q) acc[q] = fma((Acc)a[u], (Acc)bb[q], acc[q]);
                 }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                tot[q] += (double)acc[q];
+                acc[q] = 0;
             }
         }
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) red[warp][lane * 4 + q] = acc[q];
+    for (int q = 0; q < 4; ++q) red[warp][lane * 4 + q] = tot[q];
     __syncthreads();
     if (warp != 0) return;
 #pragma unroll
@@ -372,7 +480,29 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
         const int32_t r = short_ids[i];
         short_rows[i] = SpRow{rptr[r], r, (int32_t)(rptr[r + 1] - rptr[r])};
     }
+    // warp tasks: consecutive short rows, at most 32 of them and SP_TASK_NNZ nonzeros (a row
+    // with more nonzeros is a task of its own)
+    // with a 16-bit value type, tasks of rows above SP_PLAIN nonzeros (the fp64-flush kernel) are
+    // kept apart from the others and listed after them
+    const bool two_kinds = sizeof(VT) == 2;
+    auto heavy = [&](size_t i) { return two_kinds && short_rows[i].cnt > SP_PLAIN; };
+    std::vector<SpTask> tasks, heavy_tasks;
+    for (size_t i = 0; i < short_rows.size();) {
+        SpTask tk{(int32_t)i, 0};
+        const bool hv = heavy(i);
+        int64_t nz = 0;
+        while (i < short_rows.size() && tk.nrows < 32 && heavy(i) == hv &&
+               (tk.nrows == 0 || nz + short_rows[i].cnt <= SP_TASK_NNZ)) {
+            nz += short_rows[i].cnt;
+            ++tk.nrows;
+            ++i;
+        }
+        (hv ? heavy_tasks : tasks).push_back(tk);
+    }
+    out.nplain_tasks = (int64_t)tasks.size();
+    tasks.insert(tasks.end(), heavy_tasks.begin(), heavy_tasks.end());
     out.nshort = (int64_t)short_rows.size();
+    out.ntasks = (int64_t)tasks.size();
     out.nlong = (int64_t)long_rows.size();
     out.nchunks = (int64_t)chunks.size();
     if (out.nbrs == 0) return;
@@ -386,9 +516,13 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
                                   cudaMemcpyHostToDevice, s));
     XS_CHECK_CUDA(cudaMemcpyAsync(out.brs.get(), brs.data(), brs.size() * sizeof(int32_t),
                                   cudaMemcpyHostToDevice, s));
-    if (!short_rows.empty())
+    out.tasks = DevBuf<SpTask>(std::max<size_t>(tasks.size(), 1), s);
+    if (!short_rows.empty()) {
         XS_CHECK_CUDA(cudaMemcpyAsync(out.short_rows.get(), short_rows.data(),
                                       short_rows.size() * sizeof(SpRow), cudaMemcpyHostToDevice, s));
+        XS_CHECK_CUDA(cudaMemcpyAsync(out.tasks.get(), tasks.data(), tasks.size() * sizeof(SpTask),
+                                      cudaMemcpyHostToDevice, s));
+    }
     if (!long_rows.empty()) {
         XS_CHECK_CUDA(cudaMemcpyAsync(out.long_rows.get(), long_rows.data(),
                                       long_rows.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
@@ -415,18 +549,21 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C,
     XS_REQUIRE(ntiles <= 65535, XSPMM_STATUS_UNSUPPORTED, "N too large for the gather kernels");
     const bool vec = N % 4 == 0 && reinterpret_cast<uintptr_t>(B) % SpVT<VT>::b4_align == 0 &&
                      reinterpret_cast<uintptr_t>(C) % 16 == 0;
-    if (sp.nshort > 0) {
-        dim3 grid((unsigned)ceil_div(sp.nshort, SP_WARPS), (unsigned)ntiles);
+    auto rows_launch = [&](auto flush, int64_t t0, int64_t t1) {
+        constexpr bool F = decltype(flush)::value;
+        if (t1 <= t0) return;
+        dim3 grid((unsigned)ceil_div(t1 - t0, SP_WARPS), (unsigned)ntiles);
+        const SpTask* tk = sp.tasks.get() + t0;
         if (vec)
-            sp_gather_short_kernel<VT, IT, true><<<grid, SP_WARPS * 32, 0, h.stream>>>(
-                sp.short_rows.get(), sp.nshort, sp.col.get(), val, B, C, map, M, K, N,
-                h.d_err);
+            sp_gather_rows_kernel<VT, IT, true, F><<<grid, SP_WARPS * 32, 0, h.stream>>>(
+                tk, t1 - t0, sp.short_rows.get(), sp.col.get(), val, B, C, map, M, K, N, h.d_err);
         else
-            sp_gather_short_kernel<VT, IT, false><<<grid, SP_WARPS * 32, 0, h.stream>>>(
-                sp.short_rows.get(), sp.nshort, sp.col.get(), val, B, C, map, M, K, N,
-                h.d_err);
-        after_launch(h, "sparse_gather_short");
-    }
+            sp_gather_rows_kernel<VT, IT, false, F><<<grid, SP_WARPS * 32, 0, h.stream>>>(
+                tk, t1 - t0, sp.short_rows.get(), sp.col.get(), val, B, C, map, M, K, N, h.d_err);
+        after_launch(h, "sparse_gather_rows");
+    };
+    rows_launch(std::false_type(), 0, sp.nplain_tasks);
+    rows_launch(std::true_type(), sp.nplain_tasks, sp.ntasks);
     if (sp.nlong > 0) {
         DevBuf<double> ws((size_t)sp.nchunks * (size_t)N, h.stream);
         dim3 grid((unsigned)sp.nchunks, (unsigned)ntiles);
@@ -455,6 +592,8 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C,
                                               int64_t, int64_t, int64_t, const IT*);
 XS_INST_SP(__half, int32_t)
 XS_INST_SP(__half, int64_t)
+XS_INST_SP(__nv_bfloat16, int32_t)
+XS_INST_SP(__nv_bfloat16, int64_t)
 XS_INST_SP(float, int32_t)
 XS_INST_SP(float, int64_t)
 

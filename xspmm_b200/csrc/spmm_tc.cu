@@ -206,9 +206,11 @@ __device__ __forceinline__ uint64_t desc_b(uint32_t saddr) {
 // MN-major (bit 16 = 1), N >> 3 at [17,23), M >> 4 at [24,29).
 constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 16) | ((uint32_t)(TC_BN >> 3) << 17) |
                               ((uint32_t)(128 >> 4) << 24);
+// The same with A and B in bf16 (A format at [7,10) and B format at [10,13): 1 = bf16).
+constexpr uint32_t TC_IDESC_BF16 = TC_IDESC | (1u << 7) | (1u << 10);
 
 // ---- the kernel -----------------------------------------------------------------------------------
-template <typename IT>
+template <typename IT, bool BF16>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUtensorMap tmB,
                     const int64_t* __restrict__ gptr, const int32_t* __restrict__ gcol,
@@ -293,7 +295,8 @@ bcsr_spmm_tc_kernel(const __half* __restrict__ apk, const __grid_constant__ CUte
                         tc_fence_after();
                     }
                     tc_mma(tmem + (uint32_t)(b * TC_ACC_COLS), desc_a(sa + kk * A_TILE),
-                           desc_b(sa + A_STAGE + kk * B_SLAB), TC_IDESC, first ? 0u : 1u);
+                           desc_b(sa + A_STAGE + kk * B_SLAB), BF16 ? TC_IDESC_BF16 : TC_IDESC,
+                           first ? 0u : 1u);
                     ++mmas;
                     if ((e % TC_FLUSH_G) == TC_FLUSH_G - 1 || e == nk - 1)
                         tc_commit(&acc_full[b]);
@@ -804,11 +807,11 @@ void tc_prepare(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp,
 
 template <typename IT>
 void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M, int64_t K,
-                int64_t N, const IT* map) {
+                int64_t N, const IT* map, bool bf16) {
     cudaStream_t s = h.stream;
     const int ntiles = (int)ceil_div(N, TC_BN);
     const int64_t tiles = p.ngroups * ntiles;
-    auto kern = bcsr_spmm_tc_kernel<IT>;
+    auto kern = bf16 ? bcsr_spmm_tc_kernel<IT, true> : bcsr_spmm_tc_kernel<IT, false>;
     XS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
     const int64_t avg_union = std::max<int64_t>(1, p.bound / p.ngroups);
     // Split-K factor: the CTAs of a tile form one cluster, and clusters are placed whole inside
@@ -861,20 +864,20 @@ void tc_execute(Handle& h, const TcPrep& p, const __half* B, float* C, int64_t M
 template <typename IT>
 void bcsr_spmm_tc(Handle& h, int64_t nbr, int64_t nbc, int64_t nnzb, const IT* rp, const IT* ci,
                   const __half* vals, const __half* B, float* C, int64_t M, int64_t K, int64_t N,
-                  const IT* map) {
+                  const IT* map, bool bf16) {
     TcPrep p;
     tc_prepare<IT>(h, nbr, nbc, nnzb, rp, ci, vals, p);
-    tc_execute<IT>(h, p, B, C, M, K, N, map);
+    tc_execute<IT>(h, p, B, C, M, K, N, map, bf16);
 }
 
 #define XS_INST_TC(IT)                                                                            \
     template void tc_prepare<IT>(Handle&, int64_t, int64_t, int64_t, const IT*, const IT*,        \
                                  const __half*, TcPrep&);                                         \
     template void tc_execute<IT>(Handle&, const TcPrep&, const __half*, float*, int64_t, int64_t, \
-                                 int64_t, const IT*);                                             \
+                                 int64_t, const IT*, bool);                                       \
     template void bcsr_spmm_tc<IT>(Handle&, int64_t, int64_t, int64_t, const IT*, const IT*,      \
                                    const __half*, const __half*, float*, int64_t, int64_t,        \
-                                   int64_t, const IT*);
+                                   int64_t, const IT*, bool);
 XS_INST_TC(int32_t)
 XS_INST_TC(int64_t)
 
