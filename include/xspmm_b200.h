@@ -62,6 +62,9 @@ typedef struct xspmm_timings {
  *       (every pass walks the index; read at every clustering call).
  *   XSPMM_TIER1_KERNEL = mma | tc                  default fp16 Tier-1 kernel of every handle
  *       whose xspmm_set_tier1_kernel is automatic (read once per process).
+ *   XSPMM_GATHER_KERNEL = simt                     16-bit plans multiply their nearly empty
+ *       block rows on the SIMT gather kernels instead of the tensor-core gather (read once per
+ *       process).
  * ------------------------------------------------------------------------------------------- */
 
 /* ---------------------------------------------------------------------------------------------

@@ -268,11 +268,13 @@ def _ragged_rows_problem(seed, M=3000, K=60000):
     return synth.Problem("ragged", M, K, 8, rp, cols.astype(np.int64), v, None)
 
 
-@pytest.mark.parametrize("N,clustering", [(128, False), (256, True), (36, False), (7, True)])
+@pytest.mark.parametrize("N,clustering", [(128, False), (256, True), (36, False), (7, True),
+                                          (24, True), (200, False)])
 def test_plan_gather_row_tasks(executor, N, clustering):
-    """Every row of a ragged, nearly empty matrix goes through the gather kernels: C is within
-    the fp16 bar (1e-3 guarded) of the fp64 oracle, empty rows are exact zeros, and repeated
-    products are the same bits."""
+    """Every row of a ragged, nearly empty matrix goes through the gather kernels (the
+    tensor-core gather when N is a multiple of 8 -- 24 and 200 end in a partial 64-column tile --
+    the SIMT one otherwise): C is within the fp16 bar (1e-3 guarded) of the fp64 oracle, empty
+    rows are exact zeros, and repeated products are the same bits."""
     P = _ragged_rows_problem(N)
     B = np.random.default_rng(N + 1).standard_normal((P.K, N)).astype(np.float16)
     A = xs.CSRMatrix.from_host(executor, P.M, P.K, P.row_ptr, P.col_ind, P.values,

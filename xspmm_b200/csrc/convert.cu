@@ -188,6 +188,128 @@ bcsr_fill_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const VT*
     }
 }
 
+// The same fill with the blocks assembled in shared memory (block rows of at most 32 rows): the
+// kernel above zeroes a block row's blocks in global memory and then scatters 2- or 4-byte values
+// into them, one row at a time (a chain of dependent loads per row, and partial sector writes
+// that reach L2 after the zero fill). Here a warp takes all entries of the block row at once
+// (lane-strided over the contiguous range; an entry's row is found by a search over the row ends
+// the lanes hold), assembles up to CV_ASM_BYTES of blocks in shared memory (zeroed, values
+// scattered, the last duplicate of a row whose columns are not strictly increasing winning as
+// in the reference) and writes them once with 16-byte stores.
+constexpr int CV_ASM_BYTES = 4096;  // per warp
+
+template <typename VT, typename IT>
+__global__ void __launch_bounds__(CV_WARPS * 32)
+bcsr_fill_asm_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const VT* __restrict__ v,
+                     int64_t M, int64_t K, int64_t nbr, int64_t rb, int64_t cb, BlockDiv bd,
+                     const IT* __restrict__ brp, IT* __restrict__ bci, VT* __restrict__ bvals,
+                     int64_t* __restrict__ long_list, unsigned* __restrict__ long_n,
+                     unsigned long_cap) {
+    __shared__ uint32_t win_all[CV_WARPS][WIN_WORDS];
+    __shared__ uint32_t pre_all[CV_WARPS][WIN_WORDS];
+    __shared__ __align__(16) uint8_t asm_all[CV_WARPS][CV_ASM_BYTES];
+    const unsigned FULL = 0xffffffffu;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t* win = win_all[warp];
+    uint32_t* pre = pre_all[warp];
+    VT* sv = reinterpret_cast<VT*>(asm_all[warp]);
+    const int64_t bsz = rb * cb;
+    const int sb = (int)(CV_ASM_BYTES / (bsz * (int64_t)sizeof(VT)));  // blocks per round (>= 1)
+    for (int64_t br = (int64_t)blockIdx.x * CV_WARPS + warp; br < nbr;
+         br += (int64_t)gridDim.x * CV_WARPS) {
+        const int64_t base = brp[br], nb = (int64_t)brp[br + 1] - base;
+        if (nb <= 0) continue;
+        const int64_t r0 = br * rb, r1 = min(M, r0 + rb);
+        const int nrows = (int)(r1 - r0);  // <= 32
+        const int64_t e0 = rp[r0], e1 = rp[r1];
+        if (long_list && e1 - e0 > CV_LONG) {  // filled by bcsr_fill_long_kernel
+            if (lane == 0) {
+                const unsigned k = atomicAdd(long_n, 1u);
+                if (k < long_cap) long_list[k] = br;
+            }
+            continue;
+        }
+        // lane j holds the end of row r0 + j (past the block row: no end)
+        const int64_t rend = lane < nrows ? (int64_t)rp[r0 + lane + 1] : INT64_MAX;
+        auto row_of = [&](int64_t e) {  // rows whose end is <= e, i.e. the row holding e
+            int j = 0;
+#pragma unroll
+            for (int step = 16; step >= 1; step >>= 1)
+                if (__shfl_sync(FULL, rend, j + step - 1) <= e) j += step;
+            return j;
+        };
+        // rows whose columns are not strictly increasing
+        uint32_t unsorted = 0;
+        for (int64_t b0 = e0; b0 < e1; b0 += 32) {
+            const int64_t e = b0 + lane;
+            const int j = row_of(e < e1 ? e : e1 - 1);
+            const int64_t end = __shfl_sync(FULL, rend, j);
+            if (e < e1 && e + 1 < end && ci[e] >= ci[e + 1]) unsorted |= 1u << j;
+        }
+        unsorted = __reduce_or_sync(FULL, unsorted);
+        int64_t lo, hi;
+        block_col_range(ci, e0, e1, K, bd, lo, hi, nullptr);
+        int64_t rank_base = 0;
+        for (int64_t wb = lo; wb <= hi; wb += WIN_BITS) {
+            const int nwords = (int)min((int64_t)WIN_WORDS, (hi - wb) / 32 + 1);
+            mark_window(win, nwords, ci, e0, e1, K, bd, wb);
+            const uint32_t wtotal = window_prefix(win, pre, nwords);
+            for (int w = lane; w < nwords; w += 32) {  // column indices of the window's blocks
+                uint32_t x = win[w];
+                int64_t o = base + rank_base + pre[w];
+                while (x) {
+                    const int b = __ffs(x) - 1;
+                    bci[o++] = (IT)(wb + (int64_t)w * 32 + b);
+                    x &= x - 1;
+                }
+            }
+            for (int k0 = 0; k0 < (int)wtotal; k0 += sb) {
+                const int kn = min(sb, (int)wtotal - k0);
+                const int64_t bytes = (int64_t)kn * bsz * (int64_t)sizeof(VT);
+                uint4* s4 = reinterpret_cast<uint4*>(asm_all[warp]);
+                for (int64_t q = lane; q < (bytes + 15) / 16; q += 32) s4[q] = make_uint4(0, 0, 0, 0);
+                __syncwarp();
+                auto put = [&](int64_t e, int j) {
+                    const int64_t c = (int64_t)ci[e];
+                    if (c < 0 || c >= K) return;
+                    const int64_t b = bd(c);
+                    const int64_t d = b - wb;
+                    if (d < 0 || d >= (int64_t)nwords * 32) return;
+                    const int rank = (int)(pre[d >> 5] + __popc(win[d >> 5] & ((1u << (d & 31)) - 1u)));
+                    if (rank < k0 || rank >= k0 + kn) return;
+                    sv[(int64_t)(rank - k0) * bsz + (int64_t)j * cb + (c - b * cb)] = v[e];
+                };
+                for (int64_t b0 = e0; b0 < e1; b0 += 32) {
+                    const int64_t e = b0 + lane;
+                    const int j = row_of(e < e1 ? e : e1 - 1);
+                    if (e < e1 && !((unsorted >> j) & 1u)) put(e, j);
+                }
+                if (unsorted) {  // those rows by one lane, in CSR order: the last duplicate wins
+                    for (int j = 0; j < nrows; ++j) {
+                        if (!((unsorted >> j) & 1u)) continue;
+                        const int64_t prev = __shfl_sync(FULL, rend, j > 0 ? j - 1 : 0);
+                        const int64_t s = j == 0 ? e0 : prev;
+                        const int64_t t = __shfl_sync(FULL, rend, j);
+                        if (lane == 0)
+                            for (int64_t e = s; e < t; ++e) put(e, j);
+                    }
+                }
+                __syncwarp();
+                VT* dst = bvals + (base + rank_base + k0) * bsz;
+                if (reinterpret_cast<uintptr_t>(dst) % 16 == 0 && bytes % 16 == 0) {
+                    uint4* d4 = reinterpret_cast<uint4*>(dst);
+                    for (int64_t q = lane; q < bytes / 16; q += 32) d4[q] = s4[q];
+                } else {
+                    for (int64_t q = lane; q < (int64_t)kn * bsz; q += 32) dst[q] = sv[q];
+                }
+                __syncwarp();
+            }
+            rank_base += wtotal;
+            __syncwarp();
+        }
+    }
+}
+
 // ---- block rows with more than CV_LONG entries: one CTA each ---------------------------------
 // A warp walking tens of thousands of entries (a dense row, the hub rows of a power-law graph,
 // the 16 x 688-block rows of the pruned-LLM config) would serialize the launch; these rows are
@@ -423,9 +545,17 @@ void csr_to_bcsr_fill(Handle& h, int64_t M, int64_t K, int64_t nnz, const IT* ro
     DevBuf<int64_t> long_list(may_be_long ? cap : 0, h.stream);
     DevBuf<unsigned> long_n(may_be_long ? 1 : 0, h.stream);
     if (may_be_long) XS_CHECK_CUDA(cudaMemsetAsync(long_n.get(), 0, sizeof(unsigned), h.stream));
-    bcsr_fill_kernel<VT, IT><<<cv_grid(h, nbr), CV_WARPS * 32, 0, h.stream>>>(
-        row_ptr, col_ind, values, M, K, nbr, rb, cb, make_div(cb), brp, bci, bvals,
-        long_list.get(), long_n.get(), (unsigned)cap);
+    // blocks assembled in shared memory when a block row has at most 32 rows and at least four
+    // blocks fit a warp's buffer; otherwise zero-fill and scatter in global memory
+    if (bvals && rb <= 32 && rb * cb * (int64_t)sizeof(VT) * 4 <= CV_ASM_BYTES) {
+        bcsr_fill_asm_kernel<VT, IT><<<cv_grid(h, nbr), CV_WARPS * 32, 0, h.stream>>>(
+            row_ptr, col_ind, values, M, K, nbr, rb, cb, make_div(cb), brp, bci, bvals,
+            long_list.get(), long_n.get(), (unsigned)cap);
+    } else {
+        bcsr_fill_kernel<VT, IT><<<cv_grid(h, nbr), CV_WARPS * 32, 0, h.stream>>>(
+            row_ptr, col_ind, values, M, K, nbr, rb, cb, make_div(cb), brp, bci, bvals,
+            long_list.get(), long_n.get(), (unsigned)cap);
+    }
     after_launch(h, "bcsr_fill");
     if (may_be_long) {
         bcsr_fill_long_kernel<VT, IT><<<cl_grid(h, cap), CL_T, 0, h.stream>>>(

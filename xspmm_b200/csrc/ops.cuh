@@ -96,6 +96,23 @@ struct SpRow {  // a row of the gather kernels with at most SP_LONG nonzeros
 struct SpTask {  // consecutive short rows [first, first + nrows) taken by one warp (nrows <= 32)
     int32_t first, nrows;
 };
+// Tensor-core gather (16-bit values): the nonzeros of a task as k-steps of 16 stream positions.
+// col[i] is the B row of position i (-1: padding). Positions 2p and 2p+1 share two words:
+// pair[2p] = value(2p) | value(2p+1) << 16 (their 16 bits), pair[2p+1] = onehot(2p) |
+// onehot(2p+1) << 16 with onehot = 1 << (row offset in the task's block row, 0..15), 0 for padding.
+struct SpKStep {
+    int32_t col[16];
+    uint32_t pair[16];
+};
+struct SpMmaTask {
+    int64_t ks0;    // first k-step record
+    int64_t e0;     // chunk tasks: first nonzero of the chunk
+    int32_t nks;    // k-steps
+    int32_t out;    // >= 0: block row, rows 16*out + i for the bits i of mask; < 0: chunk of a long
+                    // row whose fp64 partial goes to workspace slot -(out + 1)
+    uint32_t mask;  // block-row tasks: the rows the task owns (and writes, zeros included)
+    int32_t nnz;    // chunk tasks: nonzeros in the chunk
+};
 struct SparseRows {
     std::vector<uint8_t> dense_br;
     std::vector<int64_t> host_rp;  // the block row pointers, read back once at build
@@ -109,6 +126,12 @@ struct SparseRows {
     DevBuf<int32_t> long_first;    // [nlong+1] first chunk of each long row
     int64_t nbrs = 0, nnz = 0, nshort = 0, ntasks = 0, nlong = 0, nchunks = 0;
     int64_t nplain_tasks = 0;      // tasks [0, nplain_tasks) hold rows of <= SP_PLAIN nonzeros
+    // tensor-core gather (16-bit values only)
+    DevBuf<SpKStep> ksteps;
+    DevBuf<SpMmaTask> mtasks;      // chunk tasks of the long rows first, then block-row tasks
+    DevBuf<int32_t> mlong_first;   // [nlong+1] first workspace slot of each long row
+    int64_t nksteps = 0, nmtasks = 0, nmslots = 0;
+    bool mma_built = false;
 };
 template <typename VT, typename IT>
 void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT* ci,

@@ -112,19 +112,32 @@ __global__ void permute_copy_kernel(const IT* __restrict__ rp, const IT* __restr
         const int total = __shfl_sync(FULL, incl, 31);  // <= 32 * PERM_LONG
         const int64_t dsrc = os - (int64_t)(incl - slen);  // stream position k of this row:
         const int64_t ddst = ns - (int64_t)(incl - slen);  // source k + dsrc, destination k + ddst
-        for (int k0 = 0; k0 < total; k0 += 128) {
+        // 8 entries per lane per round: every load of the round is issued before its stores
+        constexpr int U = 8;
+        for (int k0 = 0; k0 < total; k0 += 32 * U) {
+            int64_t dst[U];
+            IT cv[U];
+            VT vv[U];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < U; ++u) {
                 const int k = k0 + u * 32 + lane;
                 int j = 0;
 #pragma unroll
                 for (int step = 16; step >= 1; step >>= 1)
                     if (__shfl_sync(FULL, incl, j + step - 1) <= k) j += step;
                 const int64_t src = __shfl_sync(FULL, dsrc, j) + k;
-                const int64_t dst = __shfl_sync(FULL, ddst, j) + k;
-                if (k < total) {
-                    nci[dst] = ci[src];
-                    if (v) nv[dst] = v[src];
+                const int64_t d = __shfl_sync(FULL, ddst, j) + k;  // every lane shuffles
+                dst[u] = k < total ? d : -1;
+                if (dst[u] >= 0) {
+                    cv[u] = ci[src];
+                    if (v) vv[u] = v[src];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (dst[u] >= 0) {
+                    nci[dst[u]] = cv[u];
+                    if (v) nv[dst[u]] = vv[u];
                 }
             }
         }

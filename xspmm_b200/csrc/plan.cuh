@@ -65,7 +65,9 @@ struct Plan final : PlanBase {
                              sizeof(int32_t) +
                          sparse.short_rows.n * sizeof(SpRow) +
                          sparse.tasks.n * sizeof(SpTask) +
-                         sparse.chunks.n * sizeof(SparseChunk)) +
+                         sparse.chunks.n * sizeof(SparseChunk) +
+                         sparse.ksteps.n * sizeof(SpKStep) + sparse.mtasks.n * sizeof(SpMmaTask) +
+                         sparse.mlong_first.n * sizeof(int32_t)) +
                (int64_t)(f32work.pieces.n * sizeof(F32Piece) +
                          (f32work.long_br.n + f32work.long_first.n) * sizeof(int32_t)) +
                (int64_t)(tc.gptr.n * sizeof(int64_t) + tc.gcol.n * sizeof(int32_t) +
@@ -80,6 +82,9 @@ struct Plan final : PlanBase {
         sparse.rptr.s = sparse.col.s = sparse.val.s = s;
         sparse.brs.s = sparse.short_rows.s = sparse.long_rows.s = sparse.long_first.s = s;
         sparse.chunks.s = sparse.tasks.s = s;
+        sparse.ksteps.s = s;
+        sparse.mtasks.s = s;
+        sparse.mlong_first.s = s;
         f32work.pieces.s = f32work.long_br.s = f32work.long_first.s = s;
         tc.gptr.s = s;
         tc.gcol.s = s;

@@ -18,14 +18,20 @@
 // rounded once (as the fp32 SIMT block kernel does). A row of a split block row with no nonzero
 // is written as zeros, as the block product writes it.
 //
-// Kernels: a warp per task of consecutive short rows (up to SP_LONG nonzeros each) and 128-column
+// Kernels. 16-bit values with N % 8 == 0 (the common case) take the tensor-core gather
+// (sp_mma_kernel, below): 16 nonzeros at a time as one mma.sync per 8 columns. Otherwise the SIMT
+// gather: a warp per task of consecutive short rows (up to SP_LONG nonzeros each) and 128-column
 // tile (4 columns per lane); longer rows (hub rows) are cut into chunks of SP_CHUNK nonzeros, a
 // CTA each, whose partials (each warp's share in column order, its SP_UNROLL-nonzero groups added
-// in fp64, then the warps' sums in warp order) are added in fp64 in chunk order afterwards -- results
-// do not depend on timing.
+// in fp64, then the warps' sums in warp order) are added in fp64 afterwards. Both give results
+// that do not depend on timing.
 #include "ops.cuh"
+#include "mma_sync.cuh"
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <type_traits>
 #include <vector>
 
@@ -395,7 +401,10 @@ sp_gather_chunk_kernel(const SparseChunk* __restrict__ chunks, const int32_t* __
     }
 }
 
-// C[map(r), n] = sum of row r's chunk partials in chunk order, rounded once to fp32.
+// C[map(r), n] = sum of row r's chunk partials, rounded once to fp32. The partials are added in
+// fp64 in four interleaved running sums (slots s = 0, 1, 2, 3 mod 4, each in chunk order), then
+// (s0 + s1) + (s2 + s3): the loads of a hub row's tens of partials overlap instead of forming one
+// chain, and the order stays fixed.
 template <typename IT>
 __global__ void sp_reduce_kernel(const int32_t* __restrict__ rows, const int32_t* __restrict__ first,
                                  int64_t nrows, const double* __restrict__ ws, float* __restrict__ C,
@@ -407,8 +416,19 @@ __global__ void sp_reduce_kernel(const int32_t* __restrict__ rows, const int32_t
         const int64_t i = t / N, n = t - i * N;
         const int64_t r = rows[i];
         if (r >= M) continue;
-        double acc = 0.0;
-        for (int s = first[i]; s < first[i + 1]; ++s) acc += ws[(int64_t)s * N + n];
+        double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+        const int s1 = first[i + 1];
+        int s = first[i];
+        for (; s + 4 <= s1; s += 4) {
+            a0 += ws[(int64_t)s * N + n];
+            a1 += ws[(int64_t)(s + 1) * N + n];
+            a2 += ws[(int64_t)(s + 2) * N + n];
+            a3 += ws[(int64_t)(s + 3) * N + n];
+        }
+        if (s < s1) a0 += ws[(int64_t)s * N + n];
+        if (s + 1 < s1) a1 += ws[(int64_t)(s + 1) * N + n];
+        if (s + 2 < s1) a2 += ws[(int64_t)(s + 2) * N + n];
+        const double acc = (a0 + a1) + (a2 + a3);
         const int64_t orow = row_map ? (int64_t)row_map[r] : r;
         if (orow < 0 || orow >= M) {
             flag_error(err, DERR_PERM_OUT_OF_RANGE);
@@ -416,6 +436,298 @@ __global__ void sp_reduce_kernel(const int32_t* __restrict__ rows, const int32_t
         }
         C[orow * N + n] = (float)acc;
     }
+}
+
+// ---- tensor-core gather (16-bit values) ------------------------------------------------------
+// The SIMT kernels above spend ~48 warp instructions per nonzero (shuffles, conversions, FMAs per
+// column). Here a warp takes a task of up to SPM_TASK_KS k-steps, each k-step 16 consecutive
+// positions of the task's nonzero stream, and multiplies them on the tensor core as one
+// mma.sync m16n8k16 per 8 columns: A (16 x 16) holds position k's value in row (its row offset
+// in the block row) and column k, zeros elsewhere; B (16 x 8) holds the 16 gathered B rows.
+// Sixteen times the useful multiplies, but the tensor pipe has them to spare, and the warp issues
+// ~4 instructions per nonzero instead of ~48. The stream comes pre-arranged in 128-byte k-step
+// records (built once per plan), so one coalesced load gives a k-step's columns (lanes 0-15) and
+// packed (row, value) words (lanes 16-31). B rows are staged by 16-byte cp.async in an
+// SPM_STAGES-deep per-warp ring of 16 x 64-column slabs (chunks XOR-swizzled by k & 7, so that
+// ldmatrix.trans reads them without bank conflicts); the columns of a k-step are loaded two
+// k-steps before its copies are issued. Accumulation: the products of SPM_GROUP k-steps
+// accumulate in the tensor core from zero, and each group's result is added to fp32 running sums
+// with round-to-nearest adds (as the block kernel does), so a row collects at most three
+// truncating tensor-core accumulations. Rows stay whole inside a task (each has at most SP_LONG
+// nonzeros); longer rows are cut into SPM_CHUNK-nonzero chunks whose fp32 partials are added in
+// fp64, in chunk order, by sp_reduce_kernel.
+// Columns per warp: 128 (a whole B row of 256 bytes per nonzero when N = 128) or 64.
+constexpr int SPM_TN = 128;
+constexpr int SPM_STAGES = 4;       // B slabs in flight per warp (a power of two)
+constexpr int SPM_WARPS = 4;        // warps per CTA (independent; no CTA barrier)
+constexpr int SPM_TASK_KS = 32;     // k-steps a block-row task may hold
+constexpr int64_t SPM_CHUNK = 512;  // nonzeros per chunk of a long row (32 k-steps)
+constexpr int SPM_MRING = 2 * SPM_STAGES;  // k-step records in flight per warp (128 B each)
+// A task's products accumulate in the tensor core from its first k-step to its last, with no
+// round-to-nearest flush in between (the block kernels flush every 8 blocks): a row's nonzeros
+// span at most SP_LONG / 16 + 1 = 17 k-steps of a block-row task (the k-steps without its
+// nonzeros add exact zeros), a chunk's SPM_CHUNK / 16 = 32, against the hundreds of
+// accumulations that made the unflushed tcgen05 kernel miss the 1e-3 bar.
+static_assert(SPM_TASK_KS * 16 >= 2 * SP_LONG, "a block-row task must hold any short row");
+
+// Fills the k-step records of every task, a warp per task: lane i (< 16) holds row i of the
+// block row (or lane 0 the chunk), each lane finds the row of stream position p by a 4-step
+// search over the inclusive prefix of the counts, and padding positions get column -1, value 0.
+template <typename VT>
+__global__ void sp_kstep_fill_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks,
+                                     const int64_t* __restrict__ rptr,
+                                     const int32_t* __restrict__ col, const VT* __restrict__ val,
+                                     SpKStep* __restrict__ ks) {
+    const unsigned FULL = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < ntasks;
+         t += warps) {
+        const SpMmaTask tk = tasks[t];
+        int cnt = 0;
+        int64_t e0 = 0;
+        if (tk.out >= 0) {
+            if (lane < 16 && ((tk.mask >> lane) & 1u)) {
+                const int64_t r = (int64_t)tk.out * 16 + lane;
+                e0 = rptr[r];
+                cnt = (int)(rptr[r + 1] - e0);
+            }
+        } else if (lane == 0) {
+            e0 = tk.e0;
+            cnt = tk.nnz;
+        }
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const int total = __shfl_sync(FULL, incl, 31);
+        const int64_t erel = e0 - (int64_t)(incl - cnt);  // position p of this lane's row -> p + erel
+        const int npos = tk.nks * 16;
+        SpKStep* rec = ks + tk.ks0;
+        for (int p0 = 0; p0 < npos; p0 += 32) {
+            const int p = p0 + lane;
+            int j = 0;  // the row of position p: the number of rows whose prefix is <= p
+#pragma unroll
+            for (int step = 8; step >= 1; step >>= 1)
+                if (__shfl_sync(FULL, incl, j + step - 1) <= p) j += step;
+            const int64_t er = __shfl_sync(FULL, erel, j);
+            int32_t c = -1;
+            uint32_t vb = 0u, oh = 0u;  // value bits, one-hot row
+            if (p < total) {
+                c = col[er + p];
+                vb = (uint32_t)(*reinterpret_cast<const uint16_t*>(val + er + p));
+                oh = 1u << j;
+            }
+            const uint32_t vb1 = __shfl_down_sync(FULL, vb, 1);  // position p + 1 (p even)
+            const uint32_t oh1 = __shfl_down_sync(FULL, oh, 1);
+            if (p < npos) {
+                rec[p >> 4].col[p & 15] = c;
+                if ((p & 1) == 0) {
+                    rec[p >> 4].pair[(p & 15)] = vb | (vb1 << 16);
+                    rec[p >> 4].pair[(p & 15) + 1] = oh | (oh1 << 16);
+                }
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void cp_async16_sa(uint32_t dst, uint64_t src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+                 "r"(src_bytes));
+}
+__device__ __forceinline__ int4 lds128(uint32_t a) {
+    int4 v;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(a)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t a) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a)
+                 : "memory");
+}
+// The A fragment register of positions 2p, 2p+1 for C row `row`: the pair's value bits where its
+// one-hot row word has bit `row` (low half) or bit `row` + 16 (high half), zeros elsewhere.
+__device__ __forceinline__ uint32_t spm_afrag(uint2 w, int row) {
+    return w.x & (((w.y >> row) & 0x00010001u) * 0xFFFFu);
+}
+
+// Slab geometry for TN columns per warp (64 or 128): CH 16-byte chunks per slab row, each lane
+// copying RPL rows of one chunk; NT n8 tiles.
+template <int TN>
+struct SpmGeom {
+    static constexpr int CH = TN / 8;
+    static constexpr int RPL = 16 * CH / 32;
+    static constexpr int ROWB = TN * 2;
+    static constexpr int SLAB = 16 * ROWB;
+    static constexpr int NT = TN / 8;
+    static constexpr int WSMEM = SPM_STAGES * SLAB + SPM_MRING * 128;
+    static constexpr int MINB = TN == 64 ? 6 : 3;  // CTAs per SM (shared memory allows)
+};
+
+template <bool BF16, typename IT, int TN>
+__global__ void __launch_bounds__(SPM_WARPS * 32, SpmGeom<TN>::MINB)
+sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
+              const SpKStep* __restrict__ ks, const __half* __restrict__ B, float* __restrict__ C,
+              double* __restrict__ ws, const IT* __restrict__ row_map, int64_t M, int64_t K,
+              int64_t N, unsigned* __restrict__ err) {
+    using namespace warpmma;
+    using G = SpmGeom<TN>;
+    extern __shared__ __align__(128) uint8_t spm_smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t = (int64_t)(blockIdx.x / ntn) * SPM_WARPS + warp;
+    if (t >= ntasks) return;  // warp-uniform; the warps of a CTA never wait on one another
+    const int64_t n0 = (int64_t)(blockIdx.x % ntn) * TN;
+    const uint32_t slab0 = smem_u32(spm_smem + warp * G::WSMEM);
+    const uint32_t ring0 = slab0 + SPM_STAGES * G::SLAB;  // SPM_MRING k-step records
+    const SpMmaTask tk = tasks[t];
+    const int nks = tk.nks;
+    const uint64_t rec = reinterpret_cast<uint64_t>(ks + tk.ks0);
+    // copies: lane l takes the 16-byte chunk l % CH (8 columns) of slab rows kr .. kr + RPL - 1
+    const int ch = lane % G::CH, kr = (lane / G::CH) * G::RPL;
+    const uint32_t klim = (n0 + ch * 8 < N) ? (uint32_t)K : 0u;  // column c copied iff c < klim
+    const uint64_t bl = reinterpret_cast<uint64_t>(B) + (uint64_t)(n0 + ch * 8) * 2u;
+    const uint32_t rowb = (uint32_t)N * 2u;
+    uint32_t doff[G::RPL];
+#pragma unroll
+    for (int i = 0; i < G::RPL; ++i) {
+        const int k = kr + i;
+        doff[i] = (uint32_t)(k * G::ROWB + ((ch ^ (k & 7)) << 4));
+    }
+    // ldmatrix: lane l addresses row (mi & 1) * 8 + mr of matrix mi = l >> 3; matrices 0/1 are
+    // n8 tile 2jp (k rows 0-7 / 8-15), 2/3 are n8 tile 2jp + 1
+    const int mi = lane >> 3, mr = lane & 7, kk = (mi & 1) * 8 + mr;
+    uint32_t loff[G::NT / 2];
+#pragma unroll
+    for (int jp = 0; jp < G::NT / 2; ++jp)
+        loff[jp] = (uint32_t)(kk * G::ROWB + (((2 * jp + (mi >> 1)) ^ mr) << 4));
+    const int g = lane >> 2, tq = lane & 3;
+    // record q into its ring slot (lanes 0-7, 16 bytes each)
+    const uint64_t rec_l = rec + lane * 16;
+    const uint32_t ring_l = ring0 + lane * 16;
+    auto meta_copy = [&](int q) {
+        if (lane < 8 && q < nks)
+            cp_async16_sa(ring_l + (uint32_t)(q & (SPM_MRING - 1)) * 128u, rec_l + (uint64_t)q * 128u,
+                          16);
+    };
+    // k-step q's B rows, their columns read from the record in the ring; a column outside
+    // [0, klim) copies nothing and zero-fills (the source given is B's first row, a valid address)
+    const uint32_t ring_c = ring0 + kr * 4;
+    auto issue = [&](int q) {
+        if (q < nks) {
+            const uint32_t st = slab0 + (uint32_t)(q & (SPM_STAGES - 1)) * G::SLAB;
+            uint32_t c[G::RPL];
+#pragma unroll
+            for (int i = 0; i < G::RPL; i += 4) {
+                const int4 c4 = lds128(ring_c + (uint32_t)(q & (SPM_MRING - 1)) * 128u + i * 4);
+                c[i] = (uint32_t)c4.x;
+                c[i + 1] = (uint32_t)c4.y;
+                c[i + 2] = (uint32_t)c4.z;
+                c[i + 3] = (uint32_t)c4.w;
+            }
+#pragma unroll
+            for (int i = 0; i < G::RPL; ++i) {
+                const bool ok = c[i] < klim;
+                cp_async16_sa(st + doff[i], bl + (uint64_t)(ok ? c[i] : 0u) * rowb, ok ? 16 : 0);
+            }
+        }
+    };
+    // Group order: the records of k-steps 0 .. SPM_STAGES-1 first (waited for), then group g
+    // holds k-step g's B rows and k-step (g + SPM_STAGES)'s record, so a record has landed one
+    // iteration before the copies that read its columns are issued.
+#pragma unroll
+    for (int q = 0; q < SPM_STAGES; ++q) meta_copy(q);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < SPM_STAGES - 1; ++q) {
+        issue(q);
+        meta_copy(q + SPM_STAGES);
+        cp_async_commit();
+    }
+    // The task's products accumulate in the tensor core from its first k-step to its last.
+    float acc[G::NT][4];
+#pragma unroll
+    for (int j = 0; j < G::NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[j][q] = 0.0f;
+    for (int s = 0; s < nks; ++s) {
+        issue(s + SPM_STAGES - 1);
+        meta_copy(s + 2 * SPM_STAGES - 1);
+        cp_async_commit();
+        cp_async_wait<SPM_STAGES - 1>();
+        __syncwarp();
+        const uint32_t rs = ring0 + (uint32_t)(s & (SPM_MRING - 1)) * 128u + 64u;
+        const uint2 w0 = lds64(rs + 8 * tq), w1 = lds64(rs + 8 * (tq + 4));
+        uint32_t a[4];
+        a[0] = spm_afrag(w0, g);
+        a[1] = spm_afrag(w0, g + 8);
+        a[2] = spm_afrag(w1, g);
+        a[3] = spm_afrag(w1, g + 8);
+        const uint32_t st = slab0 + (uint32_t)(s & (SPM_STAGES - 1)) * G::SLAB;
+#pragma unroll
+        for (int jp = 0; jp < G::NT / 2; ++jp) {
+            uint32_t b[4];
+            ldsm_x4_trans(b, st + loff[jp]);
+            mma_16816<BF16>(acc[2 * jp], a, b[0], b[1]);
+            mma_16816<BF16>(acc[2 * jp + 1], a, b[2], b[3]);
+        }
+        __syncwarp();  // every lane is done with this slot before it is refilled
+    }
+    cp_async_wait<0>();
+    if (tk.out >= 0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int i = g + 8 * h;
+            if (!((tk.mask >> i) & 1u)) continue;
+            const int64_t r = (int64_t)tk.out * 16 + i;
+            if (r >= M) continue;
+            const int64_t o = row_map ? (int64_t)row_map[r] : r;
+            if (o < 0 || o >= M) {
+                flag_error(err, DERR_PERM_OUT_OF_RANGE);
+                continue;
+            }
+            float* dst = C + o * N + n0;
+#pragma unroll
+            for (int j = 0; j < G::NT; ++j) {
+                const int n = j * 8 + 2 * tq;
+                if (n0 + n < N)
+                    *reinterpret_cast<float2*>(dst + n) = make_float2(acc[j][2 * h], acc[j][2 * h + 1]);
+            }
+        }
+    } else if (g == 0) {  // a chunk: row 0 holds its partial
+        double* dst = ws + (int64_t)(-(tk.out + 1)) * N + n0;
+#pragma unroll
+        for (int j = 0; j < G::NT; ++j) {
+            const int n = j * 8 + 2 * tq;
+            if (n0 + n < N) {
+                dst[n] = (double)acc[j][0];
+                dst[n + 1] = (double)acc[j][1];
+            }
+        }
+    }
+}
+
+// XSPMM_GATHER_KERNEL = simt keeps 16-bit products on the SIMT gather kernels (comparisons);
+// read once per process.
+enum class GatherKernel { Auto, Simt };
+GatherKernel gather_kernel_choice() {
+    static const GatherKernel k = [] {
+        const char* e = std::getenv("XSPMM_GATHER_KERNEL");
+        return (e && std::strcmp(e, "simt") == 0) ? GatherKernel::Simt : GatherKernel::Auto;
+    }();
+    return k;
 }
 
 unsigned sp_grid(Handle& h, int64_t warps_wanted) {
@@ -445,9 +757,9 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
     XS_CHECK_CUDA(cudaMemcpyAsync(hrp.data(), rp, (nbr + 1) * sizeof(IT), cudaMemcpyDeviceToHost, s));
     XS_CHECK_CUDA(cudaStreamSynchronize(s));
     out.host_rp.assign(hrp.begin(), hrp.end());
-    // Block rows averaging at most dense_nnz nonzeros per block go to the gather kernels
-    // (block rows with no block stay: the block kernels write their zeros); rptr is a prefix
-    // over all rows, with empty ranges for the rows left on the block kernels.
+    // Block rows averaging at most dense_nnz nonzeros per block, and block rows without blocks,
+    // go to the gather kernels; rptr is a prefix over all rows, with empty ranges for the rows
+    // left on the block kernels.
     std::vector<int32_t> brs, short_ids, long_rows;
     std::vector<int64_t> rptr(M + 1, 0);
     for (int64_t br = 0; br < nbr; ++br) {
@@ -455,7 +767,9 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
         const int64_t r0 = br * 16, r1 = std::min<int64_t>(M, r0 + 16);
         int64_t nz = 0;
         for (int64_t r = r0; r < r1; ++r) nz += cnt[r];
-        const bool sparse = nb > 0 && nz <= dense_nnz * nb;
+        // (a block row without blocks is sparse too: its rows are written as zeros by the gather
+        // kernels, alongside the other tasks, instead of by a launch of the block kernel)
+        const bool sparse = nz <= dense_nnz * nb;
         out.dense_br[br] = sparse ? 0 : 1;
         if (sparse) {
             brs.push_back((int32_t)br);
@@ -537,7 +851,65 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
         rp, ci, v, out.brs.get(), out.nbrs, M, out.rptr.get(), out.col.get(),
         reinterpret_cast<VT*>(out.val.get()));
     after_launch(h, "sparse_extract");
-    XS_CHECK_CUDA(cudaStreamSynchronize(s));  // the host vectors go out of scope
+    if constexpr (sizeof(VT) == 2) {
+        // Tensor-core gather tasks: the chunks of the long rows (SPM_CHUNK nonzeros each), then,
+        // per sparse block row, its short rows packed in order into tasks of at most
+        // SPM_TASK_KS k-steps.
+        std::vector<SpMmaTask> mt;
+        std::vector<int32_t> mfirst;
+        int64_t nks = 0, slots = 0;
+        for (const int32_t r : long_rows) {
+            mfirst.push_back((int32_t)slots);
+            for (int64_t e = rptr[r]; e < rptr[r + 1]; e += SPM_CHUNK) {
+                const int64_t n = std::min<int64_t>(SPM_CHUNK, rptr[r + 1] - e);
+                const int32_t k = (int32_t)((n + 15) / 16);
+                mt.push_back(SpMmaTask{nks, e, k, (int32_t)(-(slots + 1)), 0u, (int32_t)n});
+                nks += k;
+                ++slots;
+            }
+        }
+        mfirst.push_back((int32_t)slots);
+        for (const int32_t br : brs) {
+            const int64_t r0 = (int64_t)br * 16, r1 = std::min<int64_t>(M, r0 + 16);
+            uint32_t mask = 0;
+            int64_t pos = 0;
+            auto emit = [&]() {
+                const int32_t k = (int32_t)((pos + 15) / 16);
+                mt.push_back(SpMmaTask{nks, 0, k, br, mask, 0});
+                nks += k;
+                mask = 0;
+                pos = 0;
+            };
+            for (int64_t r = r0; r < r1; ++r) {
+                if (cnt[r] > SP_LONG) continue;
+                if (mask != 0 && (pos + cnt[r] + 15) / 16 > SPM_TASK_KS) emit();
+                mask |= 1u << (r - r0);
+                pos += cnt[r];
+            }
+            if (mask != 0) emit();
+        }
+        XS_REQUIRE(slots < (int64_t(1) << 31) - 1, XSPMM_STATUS_UNSUPPORTED, "too many chunks");
+        out.nksteps = nks;
+        out.nmtasks = (int64_t)mt.size();
+        out.nmslots = slots;
+        if (!mt.empty()) {
+            out.mtasks = DevBuf<SpMmaTask>(mt.size(), s);
+            out.ksteps = DevBuf<SpKStep>(std::max<int64_t>(nks, 1), s);
+            out.mlong_first = DevBuf<int32_t>(mfirst.size(), s);
+            XS_CHECK_CUDA(cudaMemcpyAsync(out.mtasks.get(), mt.data(), mt.size() * sizeof(SpMmaTask),
+                                          cudaMemcpyHostToDevice, s));
+            XS_CHECK_CUDA(cudaMemcpyAsync(out.mlong_first.get(), mfirst.data(),
+                                          mfirst.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+            sp_kstep_fill_kernel<VT><<<sp_grid(h, out.nmtasks), 256, 0, s>>>(
+                out.mtasks.get(), out.nmtasks, out.rptr.get(), out.col.get(),
+                reinterpret_cast<const VT*>(out.val.get()), out.ksteps.get());
+            after_launch(h, "sparse_kstep_fill");
+            out.mma_built = true;
+        }
+        XS_CHECK_CUDA(cudaStreamSynchronize(s));  // the host vectors go out of scope
+    } else {
+        XS_CHECK_CUDA(cudaStreamSynchronize(s));  // the host vectors go out of scope
+    }
 }
 
 template <typename VT, typename IT>
@@ -547,6 +919,51 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C,
     const VT* val = reinterpret_cast<const VT*>(sp.val.get());
     const int64_t ntiles = ceil_div(N, SP_TN);
     XS_REQUIRE(ntiles <= 65535, XSPMM_STATUS_UNSUPPORTED, "N too large for the gather kernels");
+    if constexpr (sizeof(VT) == 2) {
+        // tensor-core gather: 16-byte copies of B rows need N % 8 == 0 and an aligned B
+        if (sp.mma_built && gather_kernel_choice() != GatherKernel::Simt && N % 8 == 0 &&
+            reinterpret_cast<uintptr_t>(B) % 16 == 0 && reinterpret_cast<uintptr_t>(C) % 8 == 0) {
+            constexpr bool BF = std::is_same<VT, __nv_bfloat16>::value;
+            DevBuf<double> ws((size_t)std::max<int64_t>(sp.nmslots, 1) * (size_t)N, h.stream);
+            auto launch = [&](auto tn_const) {
+                constexpr int TN = decltype(tn_const)::value;
+                const int ntn = (int)ceil_div(N, TN);
+                const int64_t blocks = ceil_div(sp.nmtasks, SPM_WARPS) * ntn;
+                XS_REQUIRE(blocks < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED,
+                           "too many tasks for the tensor-core gather");
+                const int smem = SPM_WARPS * SpmGeom<TN>::WSMEM;
+                // the shared-memory limit is a per-device attribute: set once per device (devices
+                // past 63 every time; a repeated set is harmless)
+                static std::atomic<uint64_t> attr_set{0};
+                auto kern = sp_mma_kernel<BF, IT, TN>;
+                const uint64_t bit = h.device < 64 ? (uint64_t(1) << h.device) : 0;
+                if (bit == 0 || !(attr_set.load(std::memory_order_relaxed) & bit)) {
+                    XS_CHECK_CUDA(cudaFuncSetAttribute(
+                        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+                    attr_set.fetch_or(bit, std::memory_order_relaxed);
+                }
+                kern<<<(unsigned)blocks, SPM_WARPS * 32, smem, h.stream>>>(
+                    sp.mtasks.get(), sp.nmtasks, ntn, sp.ksteps.get(),
+                    reinterpret_cast<const __half*>(B), C, ws.get(), map, M, K, N, h.d_err);
+            };
+            // 128 columns per warp when N fills them, else 64
+            if (SPM_TN == 128 && N > 64)
+                launch(std::integral_constant<int, 128>());
+            else
+                launch(std::integral_constant<int, 64>());
+            after_launch(h, "sparse_mma");
+            if (sp.nlong > 0) {
+                const int64_t total = sp.nlong * N;
+                const unsigned rgrid = (unsigned)std::max<int64_t>(
+                    1, std::min(ceil_div(total, 256), (int64_t)sm_count(h.device) * 16));
+                sp_reduce_kernel<IT><<<rgrid, 256, 0, h.stream>>>(
+                    sp.long_rows.get(), sp.mlong_first.get(), sp.nlong, ws.get(), C, map, M, N,
+                    h.d_err);
+                after_launch(h, "sparse_reduce");
+            }
+            return;
+        }
+    }
     const bool vec = N % 4 == 0 && reinterpret_cast<uintptr_t>(B) % SpVT<VT>::b4_align == 0 &&
                      reinterpret_cast<uintptr_t>(C) % 16 == 0;
     auto rows_launch = [&](auto flush, int64_t t0, int64_t t1) {
