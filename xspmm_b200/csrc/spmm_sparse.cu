@@ -445,30 +445,31 @@ __global__ void sp_reduce_kernel(const int32_t* __restrict__ rows, const int32_t
 // mma.sync m16n8k16 per 8 columns: A (16 x 16) holds position k's value in row (its row offset
 // in the block row) and column k, zeros elsewhere; B (16 x 8) holds the 16 gathered B rows.
 // Sixteen times the useful multiplies, but the tensor pipe has them to spare, and the warp issues
-// ~4 instructions per nonzero instead of ~48. The stream comes pre-arranged in 128-byte k-step
-// records (built once per plan), so one coalesced load gives a k-step's columns (lanes 0-15) and
-// packed (row, value) words (lanes 16-31). B rows are staged by 16-byte cp.async in an
-// SPM_STAGES-deep per-warp ring of 16 x 64-column slabs (chunks XOR-swizzled by k & 7, so that
-// ldmatrix.trans reads them without bank conflicts); the columns of a k-step are loaded two
-// k-steps before its copies are issued. Accumulation: the products of SPM_GROUP k-steps
-// accumulate in the tensor core from zero, and each group's result is added to fp32 running sums
-// with round-to-nearest adds (as the block kernel does), so a row collects at most three
-// truncating tensor-core accumulations. Rows stay whole inside a task (each has at most SP_LONG
-// nonzeros); longer rows are cut into SPM_CHUNK-nonzero chunks whose fp32 partials are added in
-// fp64, in chunk order, by sp_reduce_kernel.
-// Columns per warp: 128 (a whole B row of 256 bytes per nonzero when N = 128) or 64.
-constexpr int SPM_TN = 128;
+// a few instructions per nonzero instead of ~48. The stream comes pre-arranged in 128-byte k-step
+// records (built once per plan): the 16 columns, then per pair of positions their two values and
+// their two one-hot rows, from which each A fragment register takes 4 ALU operations. B rows are
+// staged by 16-byte cp.async in an SPM_STAGES-deep per-warp ring of 16 x TN slabs (chunks
+// XOR-swizzled by k & 7, so that ldmatrix.trans reads them without bank conflicts); the records
+// stream into a ring of their own by cp.async, a k-step's record landing one iteration before
+// the copies that read its columns are issued. A block-row task holds the rows of one block row
+// up to SPM_ROW_MAX nonzeros each; longer rows are cut into SPM_CHUNK-nonzero chunks whose fp32
+// partials are added in fp64 by sp_reduce_kernel.
+// Columns per warp: 64 (measured faster than 128, whose registers allow half the warps per SM).
+constexpr int SPM_TN = 64;
 constexpr int SPM_STAGES = 4;       // B slabs in flight per warp (a power of two)
 constexpr int SPM_WARPS = 4;        // warps per CTA (independent; no CTA barrier)
 constexpr int SPM_TASK_KS = 32;     // k-steps a block-row task may hold
-constexpr int64_t SPM_CHUNK = 512;  // nonzeros per chunk of a long row (32 k-steps)
+constexpr int64_t SPM_ROW_MAX = 128;  // rows with more nonzeros are cut into chunks
+constexpr int64_t SPM_CHUNK = 128;  // nonzeros per chunk (8 k-steps)
 constexpr int SPM_MRING = 2 * SPM_STAGES;  // k-step records in flight per warp (128 B each)
 // A task's products accumulate in the tensor core from its first k-step to its last, with no
-// round-to-nearest flush in between (the block kernels flush every 8 blocks): a row's nonzeros
-// span at most SP_LONG / 16 + 1 = 17 k-steps of a block-row task (the k-steps without its
-// nonzeros add exact zeros), a chunk's SPM_CHUNK / 16 = 32, against the hundreds of
-// accumulations that made the unflushed tcgen05 kernel miss the 1e-3 bar.
-static_assert(SPM_TASK_KS * 16 >= 2 * SP_LONG, "a block-row task must hold any short row");
+// round-to-nearest flush in between (the block kernels flush every 8 blocks, and a flush here
+// costs the registers of a second set of sums): a row of a block-row task has at most
+// SPM_ROW_MAX nonzeros, so its own products enter at most 9 of the accumulations (the k-steps
+// without its nonzeros add exact zeros), and a chunk of a longer row is 8 k-steps, its fp32
+// partial added to the row's others in fp64. Measured on rows of 200-3,000 nonzeros, chunks of
+// 512 without a flush reached a guarded error of 2e-3; the grouped flush kept it below 1e-3.
+static_assert(SPM_TASK_KS * 16 >= 2 * SPM_ROW_MAX, "a block-row task must hold any of its rows");
 
 // Fills the k-step records of every task, a warp per task: lane i (< 16) holds row i of the
 // block row (or lane 0 the chunk), each lane finds the row of stream position p by a 4-step
@@ -852,13 +853,18 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
         reinterpret_cast<VT*>(out.val.get()));
     after_launch(h, "sparse_extract");
     if constexpr (sizeof(VT) == 2) {
-        // Tensor-core gather tasks: the chunks of the long rows (SPM_CHUNK nonzeros each), then,
-        // per sparse block row, its short rows packed in order into tasks of at most
-        // SPM_TASK_KS k-steps.
+        // Tensor-core gather tasks: the rows of the sparse block rows above SPM_ROW_MAX nonzeros
+        // cut into chunks of SPM_CHUNK, then, per sparse block row, its other rows packed in
+        // order into tasks of at most SPM_TASK_KS k-steps.
         std::vector<SpMmaTask> mt;
-        std::vector<int32_t> mfirst;
+        std::vector<int32_t> mfirst, mlong;
+        for (const int32_t br : brs) {
+            const int64_t r0 = (int64_t)br * 16, r1 = std::min<int64_t>(M, r0 + 16);
+            for (int64_t r = r0; r < r1; ++r)
+                if (cnt[r] > SPM_ROW_MAX) mlong.push_back((int32_t)r);
+        }
         int64_t nks = 0, slots = 0;
-        for (const int32_t r : long_rows) {
+        for (const int32_t r : mlong) {
             mfirst.push_back((int32_t)slots);
             for (int64_t e = rptr[r]; e < rptr[r + 1]; e += SPM_CHUNK) {
                 const int64_t n = std::min<int64_t>(SPM_CHUNK, rptr[r + 1] - e);
@@ -881,7 +887,7 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
                 pos = 0;
             };
             for (int64_t r = r0; r < r1; ++r) {
-                if (cnt[r] > SP_LONG) continue;
+                if (cnt[r] > SPM_ROW_MAX) continue;
                 if (mask != 0 && (pos + cnt[r] + 15) / 16 > SPM_TASK_KS) emit();
                 mask |= 1u << (r - r0);
                 pos += cnt[r];
@@ -892,10 +898,16 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
         out.nksteps = nks;
         out.nmtasks = (int64_t)mt.size();
         out.nmslots = slots;
+        out.nmlong = (int64_t)mlong.size();
         if (!mt.empty()) {
             out.mtasks = DevBuf<SpMmaTask>(mt.size(), s);
             out.ksteps = DevBuf<SpKStep>(std::max<int64_t>(nks, 1), s);
             out.mlong_first = DevBuf<int32_t>(mfirst.size(), s);
+            out.mlong_rows = DevBuf<int32_t>(std::max<size_t>(mlong.size(), 1), s);
+            if (!mlong.empty())
+                XS_CHECK_CUDA(cudaMemcpyAsync(out.mlong_rows.get(), mlong.data(),
+                                              mlong.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                              s));
             XS_CHECK_CUDA(cudaMemcpyAsync(out.mtasks.get(), mt.data(), mt.size() * sizeof(SpMmaTask),
                                           cudaMemcpyHostToDevice, s));
             XS_CHECK_CUDA(cudaMemcpyAsync(out.mlong_first.get(), mfirst.data(),
@@ -952,12 +964,12 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C,
             else
                 launch(std::integral_constant<int, 64>());
             after_launch(h, "sparse_mma");
-            if (sp.nlong > 0) {
-                const int64_t total = sp.nlong * N;
+            if (sp.nmlong > 0) {
+                const int64_t total = sp.nmlong * N;
                 const unsigned rgrid = (unsigned)std::max<int64_t>(
                     1, std::min(ceil_div(total, 256), (int64_t)sm_count(h.device) * 16));
                 sp_reduce_kernel<IT><<<rgrid, 256, 0, h.stream>>>(
-                    sp.long_rows.get(), sp.mlong_first.get(), sp.nlong, ws.get(), C, map, M, N,
+                    sp.mlong_rows.get(), sp.mlong_first.get(), sp.nmlong, ws.get(), C, map, M, N,
                     h.d_err);
                 after_launch(h, "sparse_reduce");
             }
