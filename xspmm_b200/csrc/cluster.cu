@@ -1643,6 +1643,10 @@ seed_sets_heavy_kernel(const int64_t* __restrict__ qptr, const int32_t* __restri
     const int nh = *nheavy;
     auto h1 = [](uint32_t x) { return (x * 2654435761u) >> (32 - SSH_SKETCH_LOG); };
     auto h2 = [](uint32_t x) { return ((x ^ 0x9e3779b9u) * 2246822519u) >> (32 - SSH_SKETCH_LOG); };
+    // Dynamic shared memory starts with whatever the SM's previous kernel left there: the two
+    // bitmaps start empty here, and each row clears its own bits when it is done.
+    for (int i = tid; i < 2 * nbcw; i += CL_THREADS) hs_dyn[i] = 0u;
+    __syncthreads();
     for (int hi = blockIdx.x; hi < nh; hi += gridDim.x) {
         const int r = hlist[hi];
         int32_t* out = sets + (int64_t)r * SS_REC;

@@ -263,11 +263,26 @@ bcsr_fill_asm_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const
                     x &= x - 1;
                 }
             }
-            for (int k0 = 0; k0 < (int)wtotal; k0 += sb) {
-                const int kn = min(sb, (int)wtotal - k0);
+            // Windows of more than two buffers of blocks (block rows of scattered columns, e.g.
+            // R-MAT's) are zero-filled and scattered in global memory in one pass instead of being
+            // assembled a buffer at a time (a pass over the entries per buffer).
+            const bool direct = (int)wtotal > 2 * sb;
+            const int step = direct ? (int)wtotal : sb;
+            for (int k0 = 0; k0 < (int)wtotal; k0 += step) {
+                const int kn = min(step, (int)wtotal - k0);
                 const int64_t bytes = (int64_t)kn * bsz * (int64_t)sizeof(VT);
+                VT* gdst = bvals + (base + rank_base + k0) * bsz;
+                VT* tgt = direct ? gdst : sv;
+                const bool vec = reinterpret_cast<uintptr_t>(gdst) % 16 == 0 && bytes % 16 == 0;
                 uint4* s4 = reinterpret_cast<uint4*>(asm_all[warp]);
-                for (int64_t q = lane; q < (bytes + 15) / 16; q += 32) s4[q] = make_uint4(0, 0, 0, 0);
+                if (!direct) {
+                    for (int64_t q = lane; q < (bytes + 15) / 16; q += 32) s4[q] = make_uint4(0, 0, 0, 0);
+                } else if (vec) {
+                    uint4* d4 = reinterpret_cast<uint4*>(gdst);
+                    for (int64_t q = lane; q < bytes / 16; q += 32) d4[q] = make_uint4(0, 0, 0, 0);
+                } else {
+                    for (int64_t q = lane; q < (int64_t)kn * bsz; q += 32) gdst[q] = VT(0.0f);
+                }
                 __syncwarp();
                 auto put = [&](int64_t e, int j) {
                     const int64_t c = (int64_t)ci[e];
@@ -277,7 +292,7 @@ bcsr_fill_asm_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const
                     if (d < 0 || d >= (int64_t)nwords * 32) return;
                     const int rank = (int)(pre[d >> 5] + __popc(win[d >> 5] & ((1u << (d & 31)) - 1u)));
                     if (rank < k0 || rank >= k0 + kn) return;
-                    sv[(int64_t)(rank - k0) * bsz + (int64_t)j * cb + (c - b * cb)] = v[e];
+                    tgt[(int64_t)(rank - k0) * bsz + (int64_t)j * cb + (c - b * cb)] = v[e];
                 };
                 for (int64_t b0 = e0; b0 < e1; b0 += 32) {
                     const int64_t e = b0 + lane;
@@ -295,12 +310,13 @@ bcsr_fill_asm_kernel(const IT* __restrict__ rp, const IT* __restrict__ ci, const
                     }
                 }
                 __syncwarp();
-                VT* dst = bvals + (base + rank_base + k0) * bsz;
-                if (reinterpret_cast<uintptr_t>(dst) % 16 == 0 && bytes % 16 == 0) {
-                    uint4* d4 = reinterpret_cast<uint4*>(dst);
-                    for (int64_t q = lane; q < bytes / 16; q += 32) d4[q] = s4[q];
-                } else {
-                    for (int64_t q = lane; q < (int64_t)kn * bsz; q += 32) dst[q] = sv[q];
+                if (!direct) {
+                    if (vec) {
+                        uint4* d4 = reinterpret_cast<uint4*>(gdst);
+                        for (int64_t q = lane; q < bytes / 16; q += 32) d4[q] = s4[q];
+                    } else {
+                        for (int64_t q = lane; q < (int64_t)kn * bsz; q += 32) gdst[q] = sv[q];
+                    }
                 }
                 __syncwarp();
             }

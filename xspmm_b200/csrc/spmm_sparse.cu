@@ -454,21 +454,21 @@ __global__ void sp_reduce_kernel(const int32_t* __restrict__ rows, const int32_t
 // the copies that read its columns are issued. A block-row task holds the rows of one block row
 // up to SPM_ROW_MAX nonzeros each; longer rows are cut into SPM_CHUNK-nonzero chunks whose fp32
 // partials are added in fp64 by sp_reduce_kernel.
-// Columns per warp: 64 (measured faster than 128, whose registers allow half the warps per SM).
+// Columns per warp: 64. With the grouped flush a thread holds two sets of sums per 8 columns
+// (118 registers at 64 columns, 12 warps per SM); 32 columns per warp (74 registers, 24 warps)
+// measured slower on cfg5 (0.78 against 0.67 ms), the per-k-step work being paid per 32 columns.
 constexpr int SPM_TN = 64;
 constexpr int SPM_STAGES = 4;       // B slabs in flight per warp (a power of two)
 constexpr int SPM_WARPS = 4;        // warps per CTA (independent; no CTA barrier)
 constexpr int SPM_TASK_KS = 32;     // k-steps a block-row task may hold
-constexpr int64_t SPM_ROW_MAX = 128;  // rows with more nonzeros are cut into chunks
-constexpr int64_t SPM_CHUNK = 128;  // nonzeros per chunk (8 k-steps)
+constexpr int64_t SPM_ROW_MAX = 256;  // rows with more nonzeros are cut into chunks
+constexpr int64_t SPM_CHUNK = 512;  // nonzeros per chunk (32 k-steps)
+constexpr int SPM_GROUP = 8;        // k-steps per tensor-core accumulation group
 constexpr int SPM_MRING = 2 * SPM_STAGES;  // k-step records in flight per warp (128 B each)
-// A task's products accumulate in the tensor core from its first k-step to its last, with no
-// round-to-nearest flush in between (the block kernels flush every 8 blocks, and a flush here
-// costs the registers of a second set of sums): a row of a block-row task has at most
-// SPM_ROW_MAX nonzeros, so its own products enter at most 9 of the accumulations (the k-steps
-// without its nonzeros add exact zeros), and a chunk of a longer row is 8 k-steps, its fp32
-// partial added to the row's others in fp64. Measured on rows of 200-3,000 nonzeros, chunks of
-// 512 without a flush reached a guarded error of 2e-3; the grouped flush kept it below 1e-3.
+// Accumulation: the products of SPM_GROUP k-steps accumulate in the tensor core from zero and
+// each group's result is added to fp32 running sums with round-to-nearest adds, as the block
+// kernels do every 8 blocks. Without it (one accumulation per task) the ragged-rows test reached
+// a guarded error of 1.2-2e-3 even with every chain cut to 8 k-steps; with it, below 1e-3.
 static_assert(SPM_TASK_KS * 16 >= 2 * SPM_ROW_MAX, "a block-row task must hold any of its rows");
 
 // Fills the k-step records of every task, a warp per task: lane i (< 16) holds row i of the
@@ -573,7 +573,11 @@ struct SpmGeom {
     static constexpr int SLAB = 16 * ROWB;
     static constexpr int NT = TN / 8;
     static constexpr int WSMEM = SPM_STAGES * SLAB + SPM_MRING * 128;
-    static constexpr int MINB = TN == 64 ? 6 : 3;  // CTAs per SM (shared memory allows)
+    static constexpr int MINB = TN == 32 ? 4 : TN == 64 ? 3 : 2;  // CTAs of SPM_WARPS per SM
+    // 16-byte chunk c of slab row k is stored at chunk c ^ swz(k): the 8 rows an ldmatrix matrix
+    // reads then fall on 8 different 16-byte bank groups (rows of 128 bytes or more: k & 7; rows
+    // of 64 bytes, two per 128-byte line: (k >> 1) & 3)
+    __device__ static int swz(int k) { return TN >= 64 ? (k & 7) : ((k >> 1) & 3); }
 };
 
 template <bool BF16, typename IT, int TN>
@@ -603,7 +607,7 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
 #pragma unroll
     for (int i = 0; i < G::RPL; ++i) {
         const int k = kr + i;
-        doff[i] = (uint32_t)(k * G::ROWB + ((ch ^ (k & 7)) << 4));
+        doff[i] = (uint32_t)(k * G::ROWB + ((ch ^ G::swz(k)) << 4));
     }
     // ldmatrix: lane l addresses row (mi & 1) * 8 + mr of matrix mi = l >> 3; matrices 0/1 are
     // n8 tile 2jp (k rows 0-7 / 8-15), 2/3 are n8 tile 2jp + 1
@@ -611,7 +615,7 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
     uint32_t loff[G::NT / 2];
 #pragma unroll
     for (int jp = 0; jp < G::NT / 2; ++jp)
-        loff[jp] = (uint32_t)(kk * G::ROWB + (((2 * jp + (mi >> 1)) ^ mr) << 4));
+        loff[jp] = (uint32_t)(kk * G::ROWB + (((2 * jp + (mi >> 1)) ^ G::swz(kk)) << 4));
     const int g = lane >> 2, tq = lane & 3;
     // record q into its ring slot (lanes 0-7, 16 bytes each)
     const uint64_t rec_l = rec + lane * 16;
@@ -628,13 +632,20 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
         if (q < nks) {
             const uint32_t st = slab0 + (uint32_t)(q & (SPM_STAGES - 1)) * G::SLAB;
             uint32_t c[G::RPL];
+            const uint32_t ca = ring_c + (uint32_t)(q & (SPM_MRING - 1)) * 128u;
+            if constexpr (G::RPL == 2) {
+                const uint2 c2 = lds64(ca);
+                c[0] = c2.x;
+                c[1] = c2.y;
+            } else {
 #pragma unroll
-            for (int i = 0; i < G::RPL; i += 4) {
-                const int4 c4 = lds128(ring_c + (uint32_t)(q & (SPM_MRING - 1)) * 128u + i * 4);
-                c[i] = (uint32_t)c4.x;
-                c[i + 1] = (uint32_t)c4.y;
-                c[i + 2] = (uint32_t)c4.z;
-                c[i + 3] = (uint32_t)c4.w;
+                for (int i = 0; i < G::RPL; i += 4) {
+                    const int4 c4 = lds128(ca + i * 4);
+                    c[i] = (uint32_t)c4.x;
+                    c[i + 1] = (uint32_t)c4.y;
+                    c[i + 2] = (uint32_t)c4.z;
+                    c[i + 3] = (uint32_t)c4.w;
+                }
             }
 #pragma unroll
             for (int i = 0; i < G::RPL; ++i) {
@@ -657,12 +668,13 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
         meta_copy(q + SPM_STAGES);
         cp_async_commit();
     }
-    // The task's products accumulate in the tensor core from its first k-step to its last.
-    float acc[G::NT][4];
+    // Each group of SPM_GROUP k-steps accumulates in the tensor core from zero (acc); the group
+    // sums are added to sum with round-to-nearest fp32 adds.
+    float acc[G::NT][4], sum[G::NT][4];
 #pragma unroll
     for (int j = 0; j < G::NT; ++j)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) acc[j][q] = 0.0f;
+        for (int q = 0; q < 4; ++q) sum[j][q] = 0.0f;
     for (int s = 0; s < nks; ++s) {
         issue(s + SPM_STAGES - 1);
         meta_copy(s + 2 * SPM_STAGES - 1);
@@ -677,12 +689,28 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
         a[2] = spm_afrag(w1, g);
         a[3] = spm_afrag(w1, g + 8);
         const uint32_t st = slab0 + (uint32_t)(s & (SPM_STAGES - 1)) * G::SLAB;
+        if ((s & (SPM_GROUP - 1)) == 0) {
 #pragma unroll
-        for (int jp = 0; jp < G::NT / 2; ++jp) {
-            uint32_t b[4];
-            ldsm_x4_trans(b, st + loff[jp]);
-            mma_16816<BF16>(acc[2 * jp], a, b[0], b[1]);
-            mma_16816<BF16>(acc[2 * jp + 1], a, b[2], b[3]);
+            for (int jp = 0; jp < G::NT / 2; ++jp) {
+                uint32_t b[4];
+                ldsm_x4_trans(b, st + loff[jp]);
+                mma_16816_first<BF16>(acc[2 * jp], a, b[0], b[1]);
+                mma_16816_first<BF16>(acc[2 * jp + 1], a, b[2], b[3]);
+            }
+        } else {
+#pragma unroll
+            for (int jp = 0; jp < G::NT / 2; ++jp) {
+                uint32_t b[4];
+                ldsm_x4_trans(b, st + loff[jp]);
+                mma_16816<BF16>(acc[2 * jp], a, b[0], b[1]);
+                mma_16816<BF16>(acc[2 * jp + 1], a, b[2], b[3]);
+            }
+        }
+        if ((s & (SPM_GROUP - 1)) == SPM_GROUP - 1 || s == nks - 1) {
+#pragma unroll
+            for (int j = 0; j < G::NT; ++j)
+#pragma unroll
+                for (int q2 = 0; q2 < 4; ++q2) sum[j][q2] = __fadd_rn(sum[j][q2], acc[j][q2]);
         }
         __syncwarp();  // every lane is done with this slot before it is refilled
     }
@@ -704,7 +732,7 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
             for (int j = 0; j < G::NT; ++j) {
                 const int n = j * 8 + 2 * tq;
                 if (n0 + n < N)
-                    *reinterpret_cast<float2*>(dst + n) = make_float2(acc[j][2 * h], acc[j][2 * h + 1]);
+                    *reinterpret_cast<float2*>(dst + n) = make_float2(sum[j][2 * h], sum[j][2 * h + 1]);
             }
         }
     } else if (g == 0) {  // a chunk: row 0 holds its partial
@@ -713,8 +741,8 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
         for (int j = 0; j < G::NT; ++j) {
             const int n = j * 8 + 2 * tq;
             if (n0 + n < N) {
-                dst[n] = (double)acc[j][0];
-                dst[n + 1] = (double)acc[j][1];
+                dst[n] = (double)sum[j][0];
+                dst[n + 1] = (double)sum[j][1];
             }
         }
     }
@@ -958,11 +986,7 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C,
                     sp.mtasks.get(), sp.nmtasks, ntn, sp.ksteps.get(),
                     reinterpret_cast<const __half*>(B), C, ws.get(), map, M, K, N, h.d_err);
             };
-            // 128 columns per warp when N fills them, else 64
-            if (SPM_TN == 128 && N > 64)
-                launch(std::integral_constant<int, 128>());
-            else
-                launch(std::integral_constant<int, 64>());
+            launch(std::integral_constant<int, SPM_TN>());
             after_launch(h, "sparse_mma");
             if (sp.nmlong > 0) {
                 const int64_t total = sp.nmlong * N;
