@@ -131,7 +131,8 @@ struct SparseRows {
     DevBuf<SpMmaTask> mtasks;      // chunk tasks of the long rows first, then block-row tasks
     DevBuf<int32_t> mlong_rows;    // its rows cut into chunks (more than SPM_ROW_MAX nonzeros)
     DevBuf<int32_t> mlong_first;   // [nmlong+1] first workspace slot of each of them
-    int64_t nksteps = 0, nmtasks = 0, nmslots = 0, nmlong = 0;
+    DevBuf<int32_t> mranges;       // [nmranges+1]: warp ranges of consecutive tasks
+    int64_t nksteps = 0, nmtasks = 0, nmslots = 0, nmlong = 0, nmranges = 0;
     bool mma_built = false;
 };
 template <typename VT, typename IT>

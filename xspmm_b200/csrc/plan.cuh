@@ -67,7 +67,7 @@ struct Plan final : PlanBase {
                          sparse.tasks.n * sizeof(SpTask) +
                          sparse.chunks.n * sizeof(SparseChunk) +
                          sparse.ksteps.n * sizeof(SpKStep) + sparse.mtasks.n * sizeof(SpMmaTask) +
-                         (sparse.mlong_first.n + sparse.mlong_rows.n) * sizeof(int32_t)) +
+                         (sparse.mlong_first.n + sparse.mlong_rows.n + sparse.mranges.n) * sizeof(int32_t)) +
                (int64_t)(f32work.pieces.n * sizeof(F32Piece) +
                          (f32work.long_br.n + f32work.long_first.n) * sizeof(int32_t)) +
                (int64_t)(tc.gptr.n * sizeof(int64_t) + tc.gcol.n * sizeof(int32_t) +
@@ -86,6 +86,7 @@ struct Plan final : PlanBase {
         sparse.mtasks.s = s;
         sparse.mlong_first.s = s;
         sparse.mlong_rows.s = s;
+        sparse.mranges.s = s;
         f32work.pieces.s = f32work.long_br.s = f32work.long_first.s = s;
         tc.gptr.s = s;
         tc.gcol.s = s;

@@ -465,6 +465,7 @@ constexpr int64_t SPM_ROW_MAX = 256;  // rows with more nonzeros are cut into ch
 constexpr int64_t SPM_CHUNK = 512;  // nonzeros per chunk (32 k-steps)
 constexpr int SPM_GROUP = 8;        // k-steps per tensor-core accumulation group
 constexpr int SPM_MRING = 2 * SPM_STAGES;  // k-step records in flight per warp (128 B each)
+constexpr int SPM_RANGES_PER_SM = 16;  // warp ranges of tasks per SM (per 64-column tile)
 // Accumulation: the products of SPM_GROUP k-steps accumulate in the tensor core from zero and
 // each group's result is added to fp32 running sums with round-to-nearest adds, as the block
 // kernels do every 8 blocks. Without it (one accumulation per task) the ragged-rows test reached
@@ -573,31 +574,41 @@ struct SpmGeom {
     static constexpr int SLAB = 16 * ROWB;
     static constexpr int NT = TN / 8;
     static constexpr int WSMEM = SPM_STAGES * SLAB + SPM_MRING * 128;
-    static constexpr int MINB = TN == 32 ? 4 : TN == 64 ? 3 : 2;  // CTAs of SPM_WARPS per SM
+    static constexpr int MINB = TN == 32 ? 4 : TN == 64 ? 4 : 2;  // CTAs of SPM_WARPS per SM
     // 16-byte chunk c of slab row k is stored at chunk c ^ swz(k): the 8 rows an ldmatrix matrix
     // reads then fall on 8 different 16-byte bank groups (rows of 128 bytes or more: k & 7; rows
     // of 64 bytes, two per 128-byte line: (k >> 1) & 3)
     __device__ static int swz(int k) { return TN >= 64 ? (k & 7) : ((k >> 1) & 3); }
 };
 
+// A warp job = (range of consecutive tasks, 64-column tile). The tasks' k-step records are
+// consecutive, so the warp streams the range's k-steps through one ring: copies run SPM_STAGES
+// k-steps ahead across task boundaries, and at a task's last k-step its sums are stored (and
+// the next task starts from zero), instead of every task paying the ring's fill latency.
 template <bool BF16, typename IT, int TN>
 __global__ void __launch_bounds__(SPM_WARPS * 32, SpmGeom<TN>::MINB)
-sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
-              const SpKStep* __restrict__ ks, const __half* __restrict__ B, float* __restrict__ C,
-              double* __restrict__ ws, const IT* __restrict__ row_map, int64_t M, int64_t K,
-              int64_t N, unsigned* __restrict__ err) {
+sp_mma_kernel(const SpMmaTask* __restrict__ tasks, const int32_t* __restrict__ ranges,
+              int64_t nranges, int ntn, const SpKStep* __restrict__ ks,
+              const __half* __restrict__ B, float* __restrict__ C, double* __restrict__ ws,
+              const IT* __restrict__ row_map, int64_t M, int64_t K, int64_t N,
+              unsigned* __restrict__ err) {
     using namespace warpmma;
     using G = SpmGeom<TN>;
     extern __shared__ __align__(128) uint8_t spm_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t t = (int64_t)(blockIdx.x / ntn) * SPM_WARPS + warp;
-    if (t >= ntasks) return;  // warp-uniform; the warps of a CTA never wait on one another
-    const int64_t n0 = (int64_t)(blockIdx.x % ntn) * TN;
+    const int64_t job = (int64_t)blockIdx.x * SPM_WARPS + warp;
+    if (job >= nranges * ntn) return;  // warp-uniform; the warps of a CTA never wait on one another
+    const int64_t rg = job / ntn;
+    const int64_t n0 = (int64_t)(job % ntn) * TN;
+    const int t0 = ranges[rg], t1 = ranges[rg + 1];
     const uint32_t slab0 = smem_u32(spm_smem + warp * G::WSMEM);
     const uint32_t ring0 = slab0 + SPM_STAGES * G::SLAB;  // SPM_MRING k-step records
-    const SpMmaTask tk = tasks[t];
-    const int nks = tk.nks;
-    const uint64_t rec = reinterpret_cast<uint64_t>(ks + tk.ks0);
+    // the range's k-steps: [q0, q0 + nq)
+    const SpMmaTask tfirst = tasks[t0];
+    const SpMmaTask tlast = tasks[t1 - 1];
+    const int64_t q0 = tfirst.ks0;
+    const int nq = (int)(tlast.ks0 + tlast.nks - q0);
+    const uint64_t rec = reinterpret_cast<uint64_t>(ks + q0);
     // copies: lane l takes the 16-byte chunk l % CH (8 columns) of slab rows kr .. kr + RPL - 1
     const int ch = lane % G::CH, kr = (lane / G::CH) * G::RPL;
     const uint32_t klim = (n0 + ch * 8 < N) ? (uint32_t)K : 0u;  // column c copied iff c < klim
@@ -621,7 +632,7 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
     const uint64_t rec_l = rec + lane * 16;
     const uint32_t ring_l = ring0 + lane * 16;
     auto meta_copy = [&](int q) {
-        if (lane < 8 && q < nks)
+        if (lane < 8 && q < nq)
             cp_async16_sa(ring_l + (uint32_t)(q & (SPM_MRING - 1)) * 128u, rec_l + (uint64_t)q * 128u,
                           16);
     };
@@ -629,7 +640,7 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
     // [0, klim) copies nothing and zero-fills (the source given is B's first row, a valid address)
     const uint32_t ring_c = ring0 + kr * 4;
     auto issue = [&](int q) {
-        if (q < nks) {
+        if (q < nq) {
             const uint32_t st = slab0 + (uint32_t)(q & (SPM_STAGES - 1)) * G::SLAB;
             uint32_t c[G::RPL];
             const uint32_t ca = ring_c + (uint32_t)(q & (SPM_MRING - 1)) * 128u;
@@ -654,6 +665,63 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
             }
         }
     };
+    // Each group of SPM_GROUP k-steps of a task accumulates in the tensor core from zero (acc);
+    // the group sums are added to sum with round-to-nearest fp32 adds.
+    float acc[G::NT][4], sum[G::NT][4];
+#pragma unroll
+    for (int j = 0; j < G::NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sum[j][q] = 0.0f;
+    // the task being summed: its descriptor, its k-steps [cst, cend) in range positions
+    int cur = t0;
+    SpMmaTask tk = tfirst;
+    int cst = (int)(tk.ks0 - q0), cend = cst + tk.nks;
+    // stores task tk's sums (zeros if it has no k-step) and clears them
+    auto finish = [&]() {
+        if (tk.out >= 0) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int i = g + 8 * h;
+                if (!((tk.mask >> i) & 1u)) continue;
+                const int64_t r = (int64_t)tk.out * 16 + i;
+                if (r >= M) continue;
+                const int64_t o = row_map ? (int64_t)row_map[r] : r;
+                if (o < 0 || o >= M) {
+                    flag_error(err, DERR_PERM_OUT_OF_RANGE);
+                    continue;
+                }
+                float* dst = C + o * N + n0;
+#pragma unroll
+                for (int j = 0; j < G::NT; ++j) {
+                    const int n = j * 8 + 2 * tq;
+                    if (n0 + n < N)
+                        *reinterpret_cast<float2*>(dst + n) =
+                            make_float2(sum[j][2 * h], sum[j][2 * h + 1]);
+                }
+            }
+        } else if (g == 0) {  // a chunk: row 0 holds its partial
+            double* dst = ws + (int64_t)(-(tk.out + 1)) * N + n0;
+#pragma unroll
+            for (int j = 0; j < G::NT; ++j) {
+                const int n = j * 8 + 2 * tq;
+                if (n0 + n < N) {
+                    dst[n] = (double)sum[j][0];
+                    dst[n + 1] = (double)sum[j][1];
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < G::NT; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) sum[j][q] = 0.0f;
+    };
+    // moves on to the next task of the range (cur + 1 < t1)
+    auto next_task = [&]() {
+        ++cur;
+        tk = tasks[cur];
+        cst = (int)(tk.ks0 - q0);
+        cend = cst + tk.nks;
+    };
     // Group order: the records of k-steps 0 .. SPM_STAGES-1 first (waited for), then group g
     // holds k-step g's B rows and k-step (g + SPM_STAGES)'s record, so a record has landed one
     // iteration before the copies that read its columns are issued.
@@ -668,14 +736,12 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
         meta_copy(q + SPM_STAGES);
         cp_async_commit();
     }
-    // Each group of SPM_GROUP k-steps accumulates in the tensor core from zero (acc); the group
-    // sums are added to sum with round-to-nearest fp32 adds.
-    float acc[G::NT][4], sum[G::NT][4];
-#pragma unroll
-    for (int j = 0; j < G::NT; ++j)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) sum[j][q] = 0.0f;
-    for (int s = 0; s < nks; ++s) {
+    for (int s = 0; s < nq; ++s) {
+        // tasks that ended before k-step s are stored now (their stores overlap this step's wait)
+        while (cend <= s && cur + 1 < t1) {
+            finish();
+            next_task();
+        }
         issue(s + SPM_STAGES - 1);
         meta_copy(s + 2 * SPM_STAGES - 1);
         cp_async_commit();
@@ -689,7 +755,8 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
         a[2] = spm_afrag(w1, g);
         a[3] = spm_afrag(w1, g + 8);
         const uint32_t st = slab0 + (uint32_t)(s & (SPM_STAGES - 1)) * G::SLAB;
-        if ((s & (SPM_GROUP - 1)) == 0) {
+        const int ts = s - cst;  // k-step within the task
+        if ((ts & (SPM_GROUP - 1)) == 0) {
 #pragma unroll
             for (int jp = 0; jp < G::NT / 2; ++jp) {
                 uint32_t b[4];
@@ -706,7 +773,7 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
                 mma_16816<BF16>(acc[2 * jp + 1], a, b[2], b[3]);
             }
         }
-        if ((s & (SPM_GROUP - 1)) == SPM_GROUP - 1 || s == nks - 1) {
+        if ((ts & (SPM_GROUP - 1)) == SPM_GROUP - 1 || s == cend - 1) {
 #pragma unroll
             for (int j = 0; j < G::NT; ++j)
 #pragma unroll
@@ -715,36 +782,11 @@ sp_mma_kernel(const SpMmaTask* __restrict__ tasks, int64_t ntasks, int ntn,
         __syncwarp();  // every lane is done with this slot before it is refilled
     }
     cp_async_wait<0>();
-    if (tk.out >= 0) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int i = g + 8 * h;
-            if (!((tk.mask >> i) & 1u)) continue;
-            const int64_t r = (int64_t)tk.out * 16 + i;
-            if (r >= M) continue;
-            const int64_t o = row_map ? (int64_t)row_map[r] : r;
-            if (o < 0 || o >= M) {
-                flag_error(err, DERR_PERM_OUT_OF_RANGE);
-                continue;
-            }
-            float* dst = C + o * N + n0;
-#pragma unroll
-            for (int j = 0; j < G::NT; ++j) {
-                const int n = j * 8 + 2 * tq;
-                if (n0 + n < N)
-                    *reinterpret_cast<float2*>(dst + n) = make_float2(sum[j][2 * h], sum[j][2 * h + 1]);
-            }
-        }
-    } else if (g == 0) {  // a chunk: row 0 holds its partial
-        double* dst = ws + (int64_t)(-(tk.out + 1)) * N + n0;
-#pragma unroll
-        for (int j = 0; j < G::NT; ++j) {
-            const int n = j * 8 + 2 * tq;
-            if (n0 + n < N) {
-                dst[n] = (double)sum[j][0];
-                dst[n + 1] = (double)sum[j][1];
-            }
-        }
+    // the range's last task, and any after it without k-steps
+    finish();
+    while (cur + 1 < t1) {
+        next_task();
+        finish();
     }
 }
 
@@ -940,6 +982,25 @@ void sparse_rows_build(Handle& h, int64_t nbr, int64_t M, const IT* rp, const IT
                                           cudaMemcpyHostToDevice, s));
             XS_CHECK_CUDA(cudaMemcpyAsync(out.mlong_first.get(), mfirst.data(),
                                           mfirst.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+            // Warp ranges: consecutive tasks of about equal work (k-steps, plus two for a task's
+            // start and store), SPM_RANGES_PER_SM per SM; a warp streams its range's k-steps
+            // through one ring, so a task's first loads overlap the previous task's last steps.
+            const int64_t nr = std::max<int64_t>(
+                1, std::min<int64_t>((int64_t)mt.size(), (int64_t)sm_count(h.device) * SPM_RANGES_PER_SM));
+            int64_t total = 0;
+            for (const SpMmaTask& t : mt) total += t.nks + 2;
+            std::vector<int32_t> rb(1, 0);
+            int64_t acc = 0;
+            for (size_t i = 0; i < mt.size(); ++i) {
+                acc += mt[i].nks + 2;
+                if ((int64_t)rb.size() < nr && acc * nr >= total * (int64_t)rb.size())
+                    rb.push_back((int32_t)(i + 1));
+            }
+            if (rb.back() != (int32_t)mt.size()) rb.push_back((int32_t)mt.size());
+            out.nmranges = (int64_t)rb.size() - 1;
+            out.mranges = DevBuf<int32_t>(rb.size(), s);
+            XS_CHECK_CUDA(cudaMemcpyAsync(out.mranges.get(), rb.data(), rb.size() * sizeof(int32_t),
+                                          cudaMemcpyHostToDevice, s));
             sp_kstep_fill_kernel<VT><<<sp_grid(h, out.nmtasks), 256, 0, s>>>(
                 out.mtasks.get(), out.nmtasks, out.rptr.get(), out.col.get(),
                 reinterpret_cast<const VT*>(out.val.get()), out.ksteps.get());
@@ -968,7 +1029,7 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C,
             auto launch = [&](auto tn_const) {
                 constexpr int TN = decltype(tn_const)::value;
                 const int ntn = (int)ceil_div(N, TN);
-                const int64_t blocks = ceil_div(sp.nmtasks, SPM_WARPS) * ntn;
+                const int64_t blocks = ceil_div(sp.nmranges * ntn, SPM_WARPS);
                 XS_REQUIRE(blocks < (int64_t(1) << 31), XSPMM_STATUS_UNSUPPORTED,
                            "too many tasks for the tensor-core gather");
                 const int smem = SPM_WARPS * SpmGeom<TN>::WSMEM;
@@ -983,7 +1044,7 @@ void sparse_rows_execute(Handle& h, const SparseRows& sp, const VT* B, float* C,
                     attr_set.fetch_or(bit, std::memory_order_relaxed);
                 }
                 kern<<<(unsigned)blocks, SPM_WARPS * 32, smem, h.stream>>>(
-                    sp.mtasks.get(), sp.nmtasks, ntn, sp.ksteps.get(),
+                    sp.mtasks.get(), sp.mranges.get(), sp.nmranges, ntn, sp.ksteps.get(),
                     reinterpret_cast<const __half*>(B), C, ws.get(), map, M, K, N, h.d_err);
             };
             launch(std::integral_constant<int, SPM_TN>());
