@@ -46,7 +46,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) of one Tier-1 product, summed over its launches, from a one-pass ncu
 # capture of this bench at full size on one B200 (profiles/tier1_gather_cfg5.md, which gives the
 # command); keyed by (workload, N, ranks). Other workloads report null.
-TRAFFIC = {("cfg5_gnn_rmat_2^20", 128, 1): 1129831424}
+TRAFFIC = {("cfg5_gnn_rmat_2^20", 128, 1): 1175840384}
 
 
 def peaks():
